@@ -1,0 +1,546 @@
+"""Benchmark of the continuous-batching decode cache step.
+
+Workload (per GPU; sequences shard across ranks with no collective, so the
+per-GPU work is fixed as N grows -- weak scaling):
+  48 layers, 3 GDN : 1 full attention (36 + 12), GDN 16 key / 32 value heads
+  128 x 128 fp32 state, attention 16 q / 2 kv heads, D = 256, page 16;
+  256 ragged sequences, context lengths U[512, 16k]. Each step every
+  sequence finishes with probability 0.02 (pages and state slot released)
+  and a new sequence with a U[256, 2k] prompt is admitted in its place; the
+  prompt's KV pages are written (prefill, timed separately) and it decodes in
+  the same step.
+A step = one decode token for every active sequence through all 48 layers'
+cache work: GDN state update, paged KV append, split-K paged attention.
+Inputs are seeded synthetic tensors with the config's distributions; the
+per-step working set (~90 GB) exceeds L2, so no flush is needed.
+
+Arms:
+  default           the CUDA path (libshellcache.so through its C ABI)
+  --impl reference  the reference's CPU math for the path (float64 NumPy
+                    oracles restated in oracle/) on the host cores, on a
+                    bounded sample of sequences per step
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode cache-step tokens/sec at batch 256 ragged; achieved HBM GB/s vs B200 peak"
+UNIT = "tokens/s"
+SEED = 3  # configs 1-4 use seeds 1-4
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--min-len", type=int, default=512)
+    ap.add_argument("--max-len", type=int, default=16_384)
+    ap.add_argument("--churn", type=float, default=0.02)
+    ap.add_argument("--num-pages", type=int, default=150_000)
+    ap.add_argument("--pages-per-split", type=int, default=64)
+    ap.add_argument("--cpu-sample", type=int, default=0,
+                    help="sequences in the CPU baseline sample (0 = auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+        self.index = visible[index].strip() if index < len(visible) and visible[index].strip() \
+            else str(index)
+        self.rows = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.rows.append([x.strip() for x in out.stdout.strip().split(",")])
+            except Exception:  # noqa: BLE001 -- clocks are advisory
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ workload
+class Workload:
+    """Engine, caches, per-layer inputs and the churn process of one rank."""
+
+    def __init__(self, args, rank: int, device):
+        import torch
+
+        from shellsmith_b200.engine import HybridCacheEngine, HybridConfig
+        from shellsmith_b200.workloads import gdn_token_inputs_device
+
+        self.args = args
+        self.device = device
+        self.cfg = HybridConfig(max_seqs=args.batch, num_pages=args.num_pages,
+                                max_context=args.max_len + 2048 + args.steps + args.warmup + 64,
+                                pages_per_split=args.pages_per_split)
+        cfg = self.cfg
+        self.engine = HybridCacheEngine(cfg, device, seed=SEED + 1000 * rank)
+        self.rng = np.random.default_rng(SEED + 1000 * rank)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(SEED + 1000 * rank)
+        # Pool and state contents: tile one random block over the buffers
+        # (the values never steer control flow; tiling keeps setup short).
+        block = torch.randn(1 << 27, generator=gen, device=device)
+        kv_flat = self.engine.kv.view(-1)
+        tile = block.to(torch.bfloat16)
+        for start in range(0, kv_flat.numel(), tile.numel()):
+            part = kv_flat[start:start + tile.numel()]
+            part.copy_(tile[:part.numel()])
+        st_flat = self.engine.state.view(-1)
+        tile = block.mul(0.05).to(self.engine.state.dtype)
+        for start in range(0, st_flat.numel(), tile.numel()):
+            part = st_flat[start:start + tile.numel()]
+            part.copy_(tile[:part.numel()])
+        del block, tile
+        # Running sequences: admitted with their current context (already
+        # prefilled); each decode step appends one token.
+        lengths = self.rng.integers(args.min_len, args.max_len + 1, size=args.batch)
+        self.next_id = 0
+        for length in lengths:
+            self.engine.blocks.admit(self._new_id(), int(length) - 1)
+        # Per-layer inputs and outputs (device-resident, reused every step).
+        self.inputs, self.outputs = {}, {}
+        B = cfg.max_seqs
+        for layer in range(cfg.layers):
+            if cfg.is_attention(layer):
+                q = torch.randn((B, cfg.q_heads, cfg.head_dim), generator=gen,
+                                device=device).to(torch.bfloat16)
+                k = torch.randn((B, cfg.kv_heads, cfg.head_dim), generator=gen,
+                                device=device).to(torch.bfloat16)
+                v = torch.randn((B, cfg.kv_heads, cfg.head_dim), generator=gen,
+                                device=device).to(torch.bfloat16)
+                self.inputs[layer] = (q, k, v)
+                self.outputs[layer] = torch.empty((B, cfg.q_heads, cfg.head_dim),
+                                                  dtype=torch.bfloat16, device=device)
+            else:
+                self.inputs[layer] = gdn_token_inputs_device(
+                    gen, B, cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.key_dim, cfg.value_dim,
+                    device=device)
+                self.outputs[layer] = torch.empty((B, cfg.gdn_value_heads, cfg.value_dim),
+                                                  dtype=torch.bfloat16, device=device)
+        # Prompt K/V source for prefills of admitted sequences.
+        self.prompt_k = torch.randn((2048, cfg.kv_heads, cfg.head_dim), generator=gen,
+                                    device=device).to(torch.bfloat16)
+        self.prompt_v = torch.randn_like(self.prompt_k)
+        self.finished = 0
+        self.admitted = 0
+        self.prefill_tokens = 0
+
+    def _new_id(self):
+        self.next_id += 1
+        return self.next_id
+
+    def churn(self) -> list:
+        """Retire Bernoulli(p) finishers and admit replacements; returns new slots."""
+        blocks = self.engine.blocks
+        active = np.flatnonzero(blocks.active)
+        done = active[self.rng.random(len(active)) < self.args.churn]
+        for slot in done.tolist():
+            self.engine.release(slot)
+        self.finished += len(done)
+        new = []
+        for _ in range(len(done)):
+            prompt = int(self.rng.integers(256, 2048 + 1))
+            if not blocks.can_admit(prompt + 1):
+                break
+            new.append((self.engine.admit(self._new_id(), prompt), prompt))
+        self.admitted += len(new)
+        return new
+
+    def prefill(self, new: list) -> None:
+        """Write the admitted prompts' K/V into every attention layer's pages."""
+        for slot, prompt in new:
+            for layer in self.cfg.attention_layers:
+                self.engine.write_prompt_kv(slot, layer, self.prompt_k[:prompt],
+                                            self.prompt_v[:prompt])
+            self.prefill_tokens += prompt
+
+
+def run_ours(args, world, rank, local):
+    import torch
+
+    from shellsmith_b200 import _build, _capi
+
+    _build.build()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = Workload(args, rank, device)
+    eng = wl.engine
+    cfg = wl.cfg
+    stream = torch.cuda.current_stream(device)
+
+    # Launch counter: kernels this build launches per decode step.
+    def launches_per_step():
+        return len(cfg.gdn_layers) + len(cfg.attention_layers) * 3  # append, split, combine
+
+    def step(timed_events=None, layer_events=None):
+        new = wl.churn()
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        wl.prefill(new)
+        p1.record(stream)
+        n = eng.begin_step()
+        lengths = eng.blocks.lengths[eng.blocks.active].copy()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        if layer_events is None:
+            eng.decode_step(wl.inputs, wl.outputs)
+        else:
+            for layer in range(cfg.layers):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                if cfg.is_attention(layer):
+                    eng.attention_layer(layer, *wl.inputs[layer], wl.outputs[layer])
+                else:
+                    eng.gdn_layer(layer, *wl.inputs[layer], wl.outputs[layer])
+                e1.record(stream)
+                layer_events.append((cfg.is_attention(layer), e0, e1, lengths))
+        s1.record(stream)
+        if timed_events is not None:
+            timed_events.append((s0, s1, p0, p1, n, lengths, len(new)))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _capi.check_device()
+
+    barrier(world)
+    torch.cuda.synchronize()
+    events, layer_events = [], []
+    with ClockSampler(local) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step(events, layer_events)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    barrier(world)
+    _capi.check_device()
+
+    decode_ms = [s0.elapsed_time(s1) for s0, s1, *_ in events]
+    prefill_ms = [p0.elapsed_time(p1) for _, _, p0, p1, *_ in events]
+    tokens = sum(e[4] for e in events)
+    decode_s = sum(decode_ms) / 1e3
+    bytes_total = sum(eng.step_bytes(e[5])["total"] for e in events)
+    gdn_bytes = sum(eng.step_bytes(e[5])["gdn"] for e in events)
+    attn_ms = sum(a.elapsed_time(b) for is_attn, a, b, _ in layer_events if is_attn)
+    gdn_ms = sum(a.elapsed_time(b) for is_attn, a, b, _ in layer_events if not is_attn)
+    attn_bytes = sum(eng.step_bytes(le[3])["attention_per_layer"]
+                     for le in layer_events if le[0])
+    n_attn_launch = sum(1 for le in layer_events if le[0])
+    n_gdn_launch = sum(1 for le in layer_events if not le[0])
+
+    decode_s_max = max_over_ranks(decode_s, world)
+    tokens_all = sum_over_ranks(tokens, world)
+    wall_max = max_over_ranks(wall, world)
+    peaks = measured_peaks()
+    hbm = peaks["hbm_gbs"]
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, wl, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, wl)
+
+    if rank != 0:
+        return None
+    step_gbs = bytes_total / decode_s / 1e9
+    attn_gbs = attn_bytes / (attn_ms / 1e3) / 1e9
+    gdn_gbs = gdn_bytes / (gdn_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(tokens_all / decode_s_max, 1),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(decode_s_max * 1e3 / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 kv / fp32 gdn state",
+        "data": "synthetic (seeded; config 3 shapes and distributions)",
+        "config": {
+            "workload": "config3 hybrid decode cache step: 48 layers (36 GDN + 12 attention), "
+                        "256 ragged sequences per GPU, ctx U[512,16k], churn 0.02/step",
+            "global_batch": args.batch * world, "seq_len": f"U[{args.min_len},{args.max_len}]",
+            "parallelism": f"sequence-sharded x{world}, no collective",
+            "gdn": "Hk16/Hv32 dk=dv=128 fp32 state", "attention": "Hq16/Hkv2 D256 page16",
+            "pages_per_split": args.pages_per_split,
+            "l2": "working set ~90 GB/step > L2 (no flush needed)",
+        },
+        "hbm": {"step_gbs": round(step_gbs, 1), "peak_gbs": hbm,
+                "frac": round(step_gbs / hbm, 4), "peak_source": peaks["source"],
+                "bytes_per_step": round(bytes_total / max(1, len(events))),
+                "gdn_gbs": round(gdn_gbs, 1), "attention_gbs": round(attn_gbs, 1)},
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_attention (append+split+combine)",
+                     "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(attn_gbs / hbm, 4), "traffic": None,
+                     "peak_source": peaks["source"]},
+        "prefill": {"ms_per_step": round(statistics.mean(prefill_ms), 3),
+                    "tokens": wl.prefill_tokens, "admitted": wl.admitted,
+                    "finished": wl.finished,
+                    "note": "prompt K/V written to every attention layer; GDN prompt state "
+                            "starts at zero (chunked prefill kernel not in this step)"},
+        "wall_ms_per_step": round(wall_max * 1e3 / args.steps, 3),
+        "gpu_launches": launches_per_step() * args.steps + wl.admitted * len(
+            cfg.attention_layers),
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def run_e2e(args, wl, world):
+    """Same step through the public API with host buffers: pinned H2D inputs and
+    D2H outputs every step, copies overlapped with compute on side streams."""
+    import torch
+
+    eng, cfg = wl.engine, wl.cfg
+    comp = torch.cuda.current_stream(wl.device)
+    h2d = torch.cuda.Stream(wl.device)
+    d2h = torch.cuda.Stream(wl.device)
+    host_in = {l: tuple(t.cpu().pin_memory() for t in wl.inputs[l]) for l in range(cfg.layers)}
+    host_out = {l: torch.empty(wl.outputs[l].shape, dtype=wl.outputs[l].dtype).pin_memory()
+                for l in range(cfg.layers)}
+    bytes_in = sum(t.numel() * t.element_size() for ts in host_in.values() for t in ts)
+    bytes_out = sum(t.numel() * t.element_size() for t in host_out.values())
+
+    def step():
+        new = wl.churn()
+        wl.prefill(new)
+        n = eng.begin_step()
+        ready = []
+        with torch.cuda.stream(h2d):
+            h2d.wait_stream(comp)
+            for l in range(cfg.layers):
+                for dst, src in zip(wl.inputs[l], host_in[l]):
+                    dst.copy_(src, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                ready.append(ev)
+        for l in range(cfg.layers):
+            comp.wait_event(ready[l])
+            if cfg.is_attention(l):
+                eng.attention_layer(l, *wl.inputs[l], wl.outputs[l])
+            else:
+                eng.gdn_layer(l, *wl.inputs[l], wl.outputs[l])
+            done = torch.cuda.Event()
+            done.record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done)
+                host_out[l].copy_(wl.outputs[l], non_blocking=True)
+        comp.wait_stream(d2h)
+        return n
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    tokens = 0
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tokens += step()
+    torch.cuda.synchronize()
+    elapsed = max_over_ranks(time.perf_counter() - t0, world)
+    tokens = sum_over_ranks(tokens, world)
+    return {"value": round(tokens / elapsed, 1), "unit": UNIT,
+            "h2d_bytes_per_step": int(bytes_in), "d2h_bytes_per_step": int(bytes_out),
+            "ms_per_step": round(elapsed * 1e3 / args.steps, 3)}
+
+
+def cpu_baseline(args, wl):
+    """The oracle step on the host cores for a bounded sample of the same sequences."""
+    from oracle import cpu_step
+
+    cfg = wl.cfg
+    threads = cpu_step.host_threads()
+    active = np.flatnonzero(wl.engine.blocks.active)
+    sample = args.cpu_sample or min(len(active), 32, max(4, threads))
+    lengths = wl.engine.blocks.lengths[active[:sample]]
+    rng = np.random.default_rng(SEED)
+    seqs = [cpu_step.SampledSequence(rng, int(L), len(cfg.gdn_layers), len(cfg.attention_layers),
+                                     cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.key_dim,
+                                     cfg.value_dim, cfg.q_heads, cfg.kv_heads, cfg.head_dim, 8)
+            for L in lengths]
+    layers = [cfg.is_attention(l) for l in range(cfg.layers)]
+    elapsed = cpu_step.run_sample(seqs, layers, 1.0 / math.sqrt(cfg.head_dim), threads, SEED)
+    return {"value": round(len(seqs) / elapsed, 2), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"{len(seqs)} of the step's sequences (mean ctx "
+                      f"{int(np.mean(lengths))}) x 48 layers, one decode token each, "
+                      f"float64/fp32 NumPy oracle, {threads} threads"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU math (oracle port) on the host cores."""
+    if rank != 0:
+        return None
+    from oracle import cpu_step
+
+    rng = np.random.default_rng(SEED)
+    threads = cpu_step.host_threads()
+    sample = args.cpu_sample or min(32, max(4, threads))
+    lengths = rng.integers(args.min_len, args.max_len + 1, size=sample)
+    layers = [l % 4 == 3 for l in range(48)]
+    seqs = [cpu_step.SampledSequence(rng, int(L), 36, 12, 16, 32, 128, 128, 16, 2, 256,
+                                     args.steps + args.warmup + 1) for L in lengths]
+    for i in range(args.warmup):
+        cpu_step.run_sample(seqs, layers, 1.0 / 16.0, threads, SEED + i)
+    elapsed = 0.0
+    for i in range(args.steps):
+        elapsed += cpu_step.run_sample(seqs, layers, 1.0 / 16.0, threads, SEED + 100 + i)
+    value = len(seqs) * args.steps / elapsed
+    desc = (f"{len(seqs)} sequences (ctx U[{args.min_len},{args.max_len}]) x 48 layers per step, "
+            f"float64/fp32 NumPy oracle port, {threads} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(elapsed * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64/f32", "data": "synthetic",
+        "config": {"workload": "config3 hybrid decode cache step (CPU oracle sample)",
+                   "global_batch": len(seqs), "seq_len": f"U[{args.min_len},{args.max_len}]",
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads,
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args) if args.impl == "ours" else (
+        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if args.impl == "ours" and world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * shellcache: C ABI of the B200 (sm_100a) rollout-cache path.
+ *
+ * The path is the decode-time cache work of a hybrid gated-delta-net (GDN) /
+ * full-attention decoder, as served by shellsmith's studio_compute sampler:
+ *   - the GDN recurrent-state update for one token (and for chunked prefill),
+ *   - the append of new keys/values into a paged KV pool,
+ *   - split-K decode attention over ragged pages, and its (out, lse) combine.
+ *
+ * Conventions (every entry point):
+ *   - Returns 0 on success, or a positive SC_ERR_* code. No C++ exception
+ *     crosses this boundary. sc_last_error() gives the text of the most recent
+ *     nonzero status on the calling host thread.
+ *   - Every tensor pointer is a device pointer. The caller owns every buffer.
+ *     Tensors are dense and row-major in the shape written beside them.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Work is only
+ *     enqueued; nothing synchronises unless the comment says so.
+ *   - sc_bf16 is the raw 16-bit pattern of a bfloat16 value.
+ *
+ * Paged KV pool layout (defined by this library; the reference has no paging):
+ *   kv_pool[num_pages][Hkv][2][P][D] bf16, index 0 = keys, 1 = values,
+ *   P = page size in tokens. Inside one (page, kv head, K|V) block the row of
+ *   token t stores its 16-byte chunk c at chunk position c ^ (t & 7), so one
+ *   bulk copy of the block lands in shared memory already bank-swizzled for
+ *   ldmatrix. Use sc_kv_gather() to read logical keys/values back.
+ *   A slot is page * P + offset; a negative slot means "skip this token".
+ */
+#ifndef SHELLCACHE_H
+#define SHELLCACHE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t sc_bf16;
+
+enum {
+  SC_OK = 0,
+  SC_ERR_INVALID = 1,      /* bad shape, pointer or argument          */
+  SC_ERR_UNSUPPORTED = 2,  /* shape outside the compiled kernel set    */
+  SC_ERR_CUDA = 3,         /* a CUDA runtime call or launch failed     */
+  SC_ERR_DEVICE = 4        /* a kernel reported a device-side fault    */
+};
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int sc_version(void);
+
+/* Copies the text of the last nonzero status on this host thread into buf
+ * (NUL-terminated, at most n bytes). Returns the last status code. */
+int sc_last_error(char* buf, int n);
+
+/* Reads the device-side status word that kernels set when a bounded wait
+ * gives up or an index is out of range (0 = clean), then clears it.
+ * Synchronises `stream`. Returns SC_OK or SC_ERR_CUDA. */
+int sc_device_status(unsigned int* status, void* stream);
+
+/* --------------------------------------------------------------------------
+ * (a) GDN single-token recurrent update, state updated IN PLACE.
+ *
+ * Replaces studio_compute/numerics/gdn_token.py:18-42 `gated_delta_token`
+ * (kernel shellsmith_bf16_gdn_token_v1, gdn_token.py:45-79). For each row b,
+ * value head h (key head h / (Hv / Hk)) and value row i:
+ *   decayed  = g[b,h] * S[i,:]
+ *   delta    = beta[b,h] * (v[b,h,i] - decayed . k)
+ *   S[i,:]   = decayed + delta * k          (stored back into `state`)
+ *   out[b,h,i] = S[i,:] . q
+ *
+ * q, k   [B, Hk, dk] bf16       (already L2-normalised, as the reference's
+ *                                 _normalize_qk leaves them)
+ * v      [B, Hv, dv] bf16
+ * g      [B, Hv] fp32           multiplicative decay a_t = exp(g_t)
+ * beta   [B, Hv] fp32
+ * state  [slots, Hv, dv, dk]    fp32 (sc_gdn_decode) or bf16 (_bf16 variant)
+ * state_slot [B] int32          state row of batch row b; NULL = identity;
+ *                                 a negative entry skips the row
+ * out    [B, Hv, dv] bf16
+ * Supported: dk in {32, 64, 128, 256}, Hv % Hk == 0, dv >= 1.
+ * The bf16 variant reproduces the reference rounding points: the decayed
+ * state is fp32, the updated state is rounded to bf16 and the output is
+ * taken from the rounded state (gdn_token.py:60-77).
+ * ------------------------------------------------------------------------ */
+int sc_gdn_decode(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
+                  const float* g, const float* beta, float* state,
+                  const int32_t* state_slot, sc_bf16* out, int B, int Hk, int Hv,
+                  int dk, int dv, void* stream);
+
+int sc_gdn_decode_bf16(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
+                       const float* g, const float* beta, sc_bf16* state,
+                       const int32_t* state_slot, sc_bf16* out, int B, int Hk,
+                       int Hv, int dk, int dv, void* stream);
+
+/* --------------------------------------------------------------------------
+ * (b) KV append: scatter new keys/values into the paged pool.
+ *
+ * Replaces the KV write of mlx-vlm KVCache.update_and_fetch and
+ * studio_compute/mlx_request_cache.py:59-63 `OwnedKV.update_and_fetch`
+ * (concatenate along L), called from mlx_decode.py:94-100 through
+ * _prepare_projected_qkv.
+ *
+ * k, v          [ntok, Hkv, D] bf16
+ * slot_mapping  [ntok] int64, slot = page * P + offset, < 0 = skip
+ * kv_pool       [num_pages, Hkv, 2, P, D] bf16 (layout above)
+ * Supported: D in {64, 128, 256}, P in {8, 16, 32}.
+ * ------------------------------------------------------------------------ */
+int sc_kv_append(const sc_bf16* k, const sc_bf16* v, sc_bf16* kv_pool,
+                 const int64_t* slot_mapping, int ntok, int Hkv, int D, int P,
+                 int64_t num_pages, void* stream);
+
+/* Reads logical keys/values back out of the pool: for each token i,
+ * k_out[i] / v_out[i] ([Hkv, D]) = the entries at slot_mapping[i]
+ * (zeros where the slot is negative). The inverse of sc_kv_append. */
+int sc_kv_gather(const sc_bf16* kv_pool, const int64_t* slot_mapping,
+                 sc_bf16* k_out, sc_bf16* v_out, int ntok, int Hkv, int D, int P,
+                 int64_t num_pages, void* stream);
+
+/* Copies whole pages inside a pool: page dst[i] <- page src[i], all heads.
+ * The copy-on-write step of a forked prefix (replaces the private copies of
+ * studio_compute/mlx_request_cache.py:15-39 `fork_cache`). */
+int sc_kv_copy_pages(sc_bf16* kv_pool, const int32_t* src, const int32_t* dst,
+                     int npages, int Hkv, int D, int P, int64_t num_pages,
+                     void* stream);
+
+/* --------------------------------------------------------------------------
+ * (c) Split-K paged decode attention (one query token per sequence).
+ *
+ * Replaces the per-request decode SDPA of studio_compute/mlx_decode.py:80-106
+ * `_attention_rows` (mlx-vlm scaled_dot_product_attention over the cache).
+ * The math is scripts/mlx_attention_qualify.py:234-275 `numpy_attention`
+ * with one query at offset ctx_len - 1 (attends to every cached token):
+ *   out[b,h] = softmax(scale * q[b,h] . K_b[j]^T) V_b[j],  j < ctx_len[b],
+ *   kv head of h = h / (Hq / Hkv).
+ *
+ * q            [B, Hq, D] bf16
+ * kv_pool      [num_pages, Hkv, 2, P, D] bf16
+ * block_table  [B, max_pages] int32 (row stride max_pages); an entry outside
+ *              [0, num_pages) sets the device status word (DEV_BAD_INDEX)
+ * ctx_len      [B] int32, tokens to attend (includes the appended token)
+ * pages_per_split  pages one CTA reduces; the sequence is cut into
+ *                  ceil(ceil(ctx_len / P) / pages_per_split) splits
+ * num_splits   grid bound: >= the largest split count in the batch
+ * part_out     [B, Hq, num_splits, D] fp32 scratch (normalised partials)
+ * part_lse     [B, Hq, num_splits] fp32 scratch (natural-log partial lse)
+ * out          [B, Hq, D] bf16
+ * lse_out      [B, Hq] fp32 or NULL: natural-log logsumexp of the scaled
+ *              scores (what a cross-device combine needs)
+ * When num_splits == 1 the scratch may be NULL and no combine launches.
+ * A sequence with ctx_len == 0 gets a zero output and lse = -inf.
+ * Supported: D in {64, 128, 256}, P == 16, Hq % Hkv == 0.
+ * ------------------------------------------------------------------------ */
+int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
+                              int64_t num_pages, const int32_t* block_table,
+                              const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
+                              int P, int max_pages, int pages_per_split,
+                              int num_splits, float scale,
+                              float* part_out, float* part_lse, sc_bf16* out,
+                              float* lse_out, void* stream);
+
+/* Merges per-part normalised outputs with their lse:
+ *   out[r] = sum_s exp(lse[r,s] - M) o[r,s] / sum_s exp(lse[r,s] - M)
+ * over s < nparts (rows r = 0..rows-1, parts with lse = -inf ignored).
+ * part_out [rows, nparts, D] fp32, part_lse [rows, nparts] fp32,
+ * out [rows, D] bf16, lse_out [rows] fp32 or NULL.
+ * This is the cross-GPU combine of a KV-sharded long sequence. */
+int sc_attention_combine(const float* part_out, const float* part_lse,
+                         int rows, int nparts, int D, sc_bf16* out,
+                         float* lse_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHELLCACHE_H */

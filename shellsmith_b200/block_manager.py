@@ -1,0 +1,140 @@
+"""Host page allocator, block tables and GDN state slots for the paged cache.
+
+The reference has no paging: each request owns a concatenating KV buffer
+(studio_compute/mlx_request_cache.py:48-100) and a recurrent-cache copy, and
+admission is a byte reservation (inference.py:21-56, model.py:271-288). This
+block manager is the paged counterpart. Its logical effects follow the
+reference -- a request is admitted or deferred, advanced one token per
+decode step, and released with all of its resources -- while the physical
+placement (which page, which slot) is this build's own, deterministic:
+
+  * pages come from a LIFO free list seeded with a permutation of the pool
+    (seeded RNG), and a release pushes the pages back in reverse order;
+  * state slots come from a LIFO list of [0, max_seqs); a sequence's slot is
+    also its batch row, its block-table row and its GDN state row;
+  * a sequence of n tokens holds ceil(n / P) pages; the token at position t
+    lives at slot page[t // P] * P + t % P.
+
+Everything here is host NumPy; the device copies of the block table, the
+context lengths and the slot mapping are refreshed by the engine.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+class OutOfPages(MemoryError):
+    """The pool cannot hold the requested tokens."""
+
+
+class BlockManager:
+    def __init__(self, num_pages: int, page_size: int, max_seqs: int, max_pages_per_seq: int,
+                 seed: int | None = 0):
+        if num_pages < 1 or page_size < 1 or max_seqs < 1 or max_pages_per_seq < 1:
+            raise ValueError("BlockManager sizes must be positive")
+        self.num_pages = num_pages
+        self.page_size = page_size
+        self.max_seqs = max_seqs
+        self.max_pages_per_seq = max_pages_per_seq
+        order = (np.random.default_rng(seed).permutation(num_pages) if seed is not None
+                 else np.arange(num_pages))
+        # pop() takes from the end: reverse so the first page handed out is order[0].
+        self._free_pages = [int(p) for p in order[::-1]]
+        self._free_slots = list(range(max_seqs - 1, -1, -1))
+        self.table = np.zeros((max_seqs, max_pages_per_seq), np.int32)
+        self.lengths = np.zeros(max_seqs, np.int64)
+        self.active = np.zeros(max_seqs, bool)
+        self.pages: dict[int, list] = {}
+        self.owner: dict[int, object] = {}
+        self.dirty_rows: set = set()
+
+    # ------------------------------------------------------------ queries
+    @property
+    def free_pages(self) -> int:
+        return len(self._free_pages)
+
+    @property
+    def free_slots(self) -> int:
+        return len(self._free_slots)
+
+    def pages_for(self, tokens: int) -> int:
+        return -(-int(tokens) // self.page_size)
+
+    def can_admit(self, tokens: int) -> bool:
+        need = self.pages_for(tokens)
+        return (bool(self._free_slots) and need <= len(self._free_pages)
+                and need <= self.max_pages_per_seq)
+
+    def slot_of_position(self, slot: int, position: int) -> int:
+        page = self.pages[slot][position // self.page_size]
+        return page * self.page_size + position % self.page_size
+
+    # ------------------------------------------------------------ lifecycle
+    def admit(self, owner, tokens: int) -> int:
+        """Reserve a state slot and pages for `tokens` cached tokens; returns the slot."""
+        if not self._free_slots:
+            raise OutOfPages("no free sequence slot")
+        need = self.pages_for(tokens)
+        if need > self.max_pages_per_seq:
+            raise OutOfPages(f"{tokens} tokens exceed {self.max_pages_per_seq} pages per sequence")
+        if need > len(self._free_pages):
+            raise OutOfPages(f"{need} pages needed, {len(self._free_pages)} free")
+        slot = self._free_slots.pop()
+        pages = [self._free_pages.pop() for _ in range(need)]
+        self.pages[slot] = pages
+        self.owner[slot] = owner
+        self.table[slot, :need] = pages
+        self.table[slot, need:] = 0
+        self.lengths[slot] = tokens
+        self.active[slot] = True
+        self.dirty_rows.add(slot)
+        return slot
+
+    def prompt_slots(self, slot: int, start: int, stop: int) -> np.ndarray:
+        """Slot mapping (int64) of positions [start, stop) of a sequence."""
+        pages = np.asarray(self.pages[slot], np.int64)
+        pos = np.arange(start, stop, dtype=np.int64)
+        return pages[pos // self.page_size] * self.page_size + pos % self.page_size
+
+    def append_token(self, slots: np.ndarray) -> np.ndarray:
+        """Grow each listed sequence by one token; returns the new tokens' KV slots.
+
+        A sequence whose length is a multiple of P takes one new page (LIFO).
+        Raises OutOfPages before changing anything if the pool cannot cover
+        every sequence that needs a page.
+        """
+        slots = np.asarray(slots, np.int64)
+        lengths = self.lengths[slots]
+        needs_page = lengths % self.page_size == 0
+        if int(needs_page.sum()) > len(self._free_pages):
+            raise OutOfPages("pool exhausted while appending decode tokens")
+        if np.any(lengths // self.page_size + needs_page > self.max_pages_per_seq):
+            raise OutOfPages("a sequence outgrew max_pages_per_seq")
+        out = np.empty(len(slots), np.int64)
+        for i, (slot, length, new_page) in enumerate(zip(slots.tolist(), lengths.tolist(),
+                                                         needs_page.tolist())):
+            if new_page:
+                page = self._free_pages.pop()
+                self.pages[slot].append(page)
+                self.table[slot, length // self.page_size] = page
+                self.dirty_rows.add(slot)
+            out[i] = self.pages[slot][length // self.page_size] * self.page_size + (
+                length % self.page_size)
+        self.lengths[slots] = lengths + 1
+        return out
+
+    def release(self, slot: int) -> None:
+        """Return a sequence's pages (reverse order) and its slot to the free lists."""
+        pages = self.pages.pop(slot)
+        self._free_pages.extend(reversed(pages))
+        self.owner.pop(slot, None)
+        self.lengths[slot] = 0
+        self.active[slot] = False
+        self._free_slots.append(slot)
+        self.dirty_rows.add(slot)
+
+    def take_dirty_rows(self) -> list:
+        rows = sorted(self.dirty_rows)
+        self.dirty_rows.clear()
+        return rows

@@ -1,0 +1,149 @@
+// Shared helpers of the shellcache kernels: status reporting, bf16 packing,
+// bounded mbarrier waits and the bulk-copy (TMA engine) primitives.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/shellcache.h"
+
+namespace sc {
+
+// ---------------------------------------------------------------- host status
+// The text of the last nonzero status on this host thread.
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+#define SC_REQUIRE(cond, code, ...)                         \
+  do {                                                      \
+    if (!(cond)) return ::sc::set_error((code), __VA_ARGS__); \
+  } while (0)
+
+// ---------------------------------------------------------------- device status
+// Bits of the device status word (sc_device_status reads and clears it).
+enum : unsigned int {
+  DEV_WAIT_TIMEOUT = 1u,    // a bounded mbarrier wait gave up
+  DEV_BAD_INDEX = 2u,       // a page / slot index fell outside the pool
+};
+// Device address of the status word on the current device (host function;
+// kernels receive it as an argument, so no relocatable device code is needed).
+unsigned int* device_status_word();
+
+__device__ __forceinline__ void flag_device(unsigned int* status, unsigned int bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------- bf16 helpers
+__device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
+__device__ __forceinline__ float bf16_to_f(uint16_t x) { return __uint_as_float(uint32_t(x) << 16); }
+
+__device__ __forceinline__ uint16_t f_to_bf16(float x) {
+  __nv_bfloat16 h = __float2bfloat16_rn(x);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Packs (lo, hi) into one bf16x2 register, round-to-nearest-even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------- mbarrier + bulk copy
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+// One try_wait on the given phase parity; true once that phase completed.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: gives up after `limit` polls (each try_wait already blocks
+// for a hardware-defined slice), flags DEV_WAIT_TIMEOUT and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  unsigned int* status,
+                                                  uint32_t limit = (1u << 20)) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  flag_device(status, DEV_WAIT_TIMEOUT);
+  return false;
+}
+
+// Untiled bulk copy global -> shared (TMA engine), completion counted in bytes
+// on `bar`. Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------- warp MMA helpers
+// ldmatrix x4 (optionally transposed) from a shared address.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                          uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D(16x8 f32) += A(16x16 bf16, row) * B(16x8 bf16, col).
+__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transposes one 8x8 b16 matrix held in the ldmatrix fragment layout.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+}  // namespace sc

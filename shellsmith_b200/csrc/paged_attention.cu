@@ -1,0 +1,384 @@
+// K7 split-K paged decode attention and the (out, lse) combine.
+//
+// Reference math: scripts/mlx_attention_qualify.py:234-275 `numpy_attention`
+// for one query at the last position (query_offset = keys - 1), GQA head
+// j = h // group. Runtime call site: studio_compute/mlx_decode.py:80-106
+// `_attention_rows`, which runs mlx-vlm SDPA one request at a time.
+//
+// B200 mapping.
+//   Grid (split, kv head x head group, sequence). A CTA reduces pages
+//   [split * pages_per_split, ...) of one sequence for up to 8 query heads
+//   that share one kv head, so each K/V byte is read from HBM once per group.
+//   Each warp owns NSTAGE shared-memory stages and streams its pages through
+//   them with one untiled bulk copy (TMA engine) per page: K and V of one
+//   (page, kv head) are one contiguous 2*P*D*2-byte block, pre-swizzled in HBM
+//   so ldmatrix reads it without bank conflicts.
+//   Scores are computed transposed, S^T[token, head] = K Q^T, with
+//   mma.m16n8k16 (M = 16 tokens = one page, N = 8 heads, K = D): no padding
+//   rows. The probabilities are transposed in registers with movmatrix into
+//   the B operand of O^T[dim, head] += V^T P^T.
+//   Online softmax runs in the log2 domain; warps merge in shared memory and
+//   the CTA writes a normalised partial and its lse (or the final bf16 output
+//   when the sequence needs one split).
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace sc {
+namespace {
+
+constexpr int kPage = 16;
+constexpr int kHeadsPerTile = 8;
+
+template <int D>
+struct AttnShape {
+  static constexpr int ROW_BYTES = D * 2;
+  static constexpr int KV_BYTES = kPage * ROW_BYTES;  // K or V block of one page, one head
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES;
+  static constexpr int KSTEPS = D / 16;
+};
+
+template <int D, int NW, int NSTAGE>
+__global__ void __launch_bounds__(NW * 32)
+    paged_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kv_pool,
+                        const int32_t* __restrict__ block_table,
+                        const int32_t* __restrict__ ctx_len, int Hq, int Hkv, int G, int HG,
+                        int max_pages, int pages_per_split, int num_splits, float scale_log2,
+                        float* __restrict__ part_out, float* __restrict__ part_lse,
+                        uint16_t* __restrict__ out, float* __restrict__ lse_out,
+                        long long num_pages, unsigned int* status) {
+  using S = AttnShape<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NW * NSTAGE * S::STAGE_BYTES);
+
+  // After any bounded wait has given up on this device, later CTAs stop at
+  // once instead of each waiting out its own limit.
+  if (status != nullptr && (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT))
+    return;
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / HG;
+  const int hg = blockIdx.y - kvh * HG;
+  const int b = blockIdx.z;
+  const int L = ctx_len[b];
+  const int npages = (L + kPage - 1) / kPage;
+  const int p_begin = split * pages_per_split;
+  if (npages == 0 && split == 0) {  // nothing to attend: zero output, lse = -inf
+    for (int idx = threadIdx.x; idx < min(kHeadsPerTile, G - hg * kHeadsPerTile) * D;
+         idx += blockDim.x) {
+      const size_t row = (size_t)b * Hq + kvh * G + hg * kHeadsPerTile + idx / D;
+      if (num_splits == 1) {
+        out[row * D + idx % D] = 0;
+        if (idx % D == 0 && lse_out != nullptr) lse_out[row] = -CUDART_INF_F;
+      }
+    }
+    return;
+  }
+  if (p_begin >= npages) return;  // uniform over the CTA
+  const int n_here = min(npages, p_begin + pages_per_split) - p_begin;
+  const int heads_here = min(kHeadsPerTile, G - hg * kHeadsPerTile);
+  const int head0 = kvh * G + hg * kHeadsPerTile;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NW * NSTAGE; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // Q^T as the B operand: b0 = q[n][16kk + 2c .. +1], b1 = q[n][16kk + 8 + 2c .. +1].
+  uint32_t qf[S::KSTEPS][2];
+  {
+    const int n = lane >> 2, c = lane & 3;
+    const bool valid = n < heads_here;
+    const uint16_t* qp = q + ((size_t)b * Hq + head0 + (valid ? n : 0)) * D;
+#pragma unroll
+    for (int kk = 0; kk < S::KSTEPS; ++kk) {
+      qf[kk][0] = valid ? *reinterpret_cast<const uint32_t*>(qp + 16 * kk + 2 * c) : 0u;
+      qf[kk][1] = valid ? *reinterpret_cast<const uint32_t*>(qp + 16 * kk + 8 + 2 * c) : 0u;
+    }
+  }
+
+  // Pages of this warp: p_begin + warp + j * NW, j < nj.
+  const int nj = n_here > warp ? (n_here - warp + NW - 1) / NW : 0;
+  uint8_t* stage = smem + warp * NSTAGE * S::STAGE_BYTES;
+  uint64_t* bar = bars + warp * NSTAGE;
+  const int32_t* bt_row = block_table + (size_t)b * max_pages;
+
+  auto issue = [&](int j) {
+    int page = bt_row[p_begin + warp + j * NW];
+    if (page < 0 || page >= num_pages) {
+      flag_device(status, DEV_BAD_INDEX);
+      page = 0;  // keep the copy in bounds; the status word reports the fault
+    }
+    const uint8_t* src =
+        reinterpret_cast<const uint8_t*>(kv_pool) + ((size_t)page * Hkv + kvh) * S::STAGE_BYTES;
+    const int s = j % NSTAGE;
+    mbar_arrive_expect_tx(&bar[s], S::STAGE_BYTES);
+    bulk_g2s(stage + s * S::STAGE_BYTES, src, S::STAGE_BYTES, &bar[s]);
+  };
+
+  int issued = 0;
+  if (lane == 0)
+    for (; issued < NSTAGE && issued < nj; ++issued) issue(issued);
+  issued = __shfl_sync(0xffffffffu, issued, 0);
+
+  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F;  // running max of heads 2c, 2c+1 (log2 units)
+  float l0 = 0.f, l1 = 0.f;                      // this lane's partial sums
+  float o[S::KSTEPS][4];
+#pragma unroll
+  for (int mt = 0; mt < S::KSTEPS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  const int tk = r8 + 8 * (mi & 1);   // token row this lane addresses for K
+  const int tv = r8 + 8 * (mi >> 1);  // token row this lane addresses for V^T
+  int consumed = 0;
+  for (int j = 0; j < nj; ++j) {
+    const int s = j % NSTAGE;
+    if (!mbar_wait_bounded(&bar[s], (j / NSTAGE) & 1, status)) break;
+    const uint32_t kbase = smem_addr(stage + s * S::STAGE_BYTES);
+    const uint32_t vbase = kbase + S::KV_BYTES;
+
+    float sc4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < S::KSTEPS; ++kk) {
+      const int chunk = 2 * kk + (mi >> 1);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kbase + tk * S::ROW_BYTES + ((chunk ^ (tk & 7)) << 4), a0, a1, a2, a3);
+      mma_bf16_16816(sc4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+    }
+
+    const int tok0 = (p_begin + warp + j * NW) * kPage + (lane >> 2);
+    const bool lo_ok = tok0 < L, hi_ok = tok0 + 8 < L;
+    const float x0 = lo_ok ? sc4[0] * scale_log2 : -CUDART_INF_F;
+    const float x1 = lo_ok ? sc4[1] * scale_log2 : -CUDART_INF_F;
+    const float x2 = hi_ok ? sc4[2] * scale_log2 : -CUDART_INF_F;
+    const float x3 = hi_ok ? sc4[3] * scale_log2 : -CUDART_INF_F;
+    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    // The first token of every page is < L, so mx0 / mx1 are finite.
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+    const float p0 = exp2f(x0 - mn0), p1 = exp2f(x1 - mn1);
+    const float p2 = exp2f(x2 - mn0), p3 = exp2f(x3 - mn1);
+    l0 = fmaf(l0, c0, p0 + p2);
+    l1 = fmaf(l1, c1, p1 + p3);
+    m0 = mn0;
+    m1 = mn1;
+    const uint32_t pb0 = movmatrix_t(pack_bf16x2(p0, p1));
+    const uint32_t pb1 = movmatrix_t(pack_bf16x2(p2, p3));
+#pragma unroll
+    for (int mt = 0; mt < S::KSTEPS; ++mt) {
+      o[mt][0] *= c0;
+      o[mt][1] *= c1;
+      o[mt][2] *= c0;
+      o[mt][3] *= c1;
+      const int chunk = 2 * mt + (mi & 1);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vbase + tv * S::ROW_BYTES + ((chunk ^ (tv & 7)) << 4), a0, a1, a2, a3);
+      mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+    consumed = j + 1;
+    __syncwarp();
+    if (lane == 0 && issued < nj) {
+      fence_proxy_async_smem();
+      issue(issued);
+    }
+    if (issued < nj) ++issued;
+  }
+  if (consumed < nj) {
+    // A wait gave up (already flagged): drain this warp's copies in flight so
+    // the CTA never exits with a bulk copy still writing its shared memory.
+    for (int j = consumed; j < issued; ++j)
+      if (!mbar_wait_bounded(&bar[j % NSTAGE], (j / NSTAGE) & 1, status)) break;
+  }
+
+#pragma unroll
+  for (int off = 4; off <= 16; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  __syncthreads();  // every stage is drained; reuse the stage memory
+
+  float* red_o = reinterpret_cast<float*>(smem);                 // [NW][8][D]
+  float* red_m = red_o + NW * kHeadsPerTile * D;                 // [NW][8]
+  float* red_l = red_m + NW * kHeadsPerTile;                     // [NW][8]
+  {
+    const int d0 = lane >> 2, h0 = 2 * (lane & 3);
+    float* w0 = red_o + (warp * kHeadsPerTile + h0) * D;
+    float* w1 = w0 + D;
+#pragma unroll
+    for (int mt = 0; mt < S::KSTEPS; ++mt) {
+      w0[16 * mt + d0] = o[mt][0];
+      w1[16 * mt + d0] = o[mt][1];
+      w0[16 * mt + d0 + 8] = o[mt][2];
+      w1[16 * mt + d0 + 8] = o[mt][3];
+    }
+    if (lane < 4) {
+      red_m[warp * kHeadsPerTile + h0] = m0;
+      red_m[warp * kHeadsPerTile + h0 + 1] = m1;
+      red_l[warp * kHeadsPerTile + h0] = l0;
+      red_l[warp * kHeadsPerTile + h0 + 1] = l1;
+    }
+  }
+  __syncthreads();
+
+  constexpr float kLn2 = 0.6931471805599453f;
+  for (int idx = threadIdx.x; idx < heads_here * D; idx += NW * 32) {
+    const int n = idx / D, d = idx - (idx / D) * D;
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w * kHeadsPerTile + n]);
+    float lsum = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = red_m[w * kHeadsPerTile + n];
+      const float f = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
+      lsum = fmaf(red_l[w * kHeadsPerTile + n], f, lsum);
+      acc = fmaf(red_o[(w * kHeadsPerTile + n) * D + d], f, acc);
+    }
+    const float val = acc / lsum;
+    const float lse = (M + log2f(lsum)) * kLn2;
+    const size_t row = (size_t)b * Hq + head0 + n;
+    if (num_splits == 1) {
+      out[row * D + d] = f_to_bf16(val);
+      if (d == 0 && lse_out != nullptr) lse_out[row] = lse;
+    } else {
+      part_out[(row * num_splits + split) * D + d] = val;
+      if (d == 0) part_lse[row * num_splits + split] = lse;
+    }
+  }
+}
+
+// One CTA per output row: merges the split partials of that row.
+// With ctx_len != NULL only the splits the decode kernel wrote are read.
+__global__ void combine_kernel(const float* __restrict__ part_out,
+                               const float* __restrict__ part_lse,
+                               const int32_t* __restrict__ ctx_len, int Hq, int nparts,
+                               int pages_per_split, int D, uint16_t* __restrict__ out,
+                               float* __restrict__ lse_out) {
+  const int row = blockIdx.x;
+  int ns = nparts;
+  if (ctx_len != nullptr) {
+    const int npages = (ctx_len[row / Hq] + kPage - 1) / kPage;
+    ns = min(nparts, (npages + pages_per_split - 1) / pages_per_split);
+  }
+  const float* lse = part_lse + (size_t)row * nparts;
+  float M = -CUDART_INF_F;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, lse[s]);
+  float wsum = 0.f;
+  if (M != -CUDART_INF_F)
+    for (int s = 0; s < ns; ++s) wsum += lse[s] == -CUDART_INF_F ? 0.f : __expf(lse[s] - M);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    if (M != -CUDART_INF_F)
+      for (int s = 0; s < ns; ++s)
+        if (lse[s] != -CUDART_INF_F)
+          acc = fmaf(__expf(lse[s] - M), part_out[((size_t)row * nparts + s) * D + d], acc);
+    out[(size_t)row * D + d] = f_to_bf16(M == -CUDART_INF_F ? 0.f : acc / wsum);
+  }
+  if (threadIdx.x == 0 && lse_out != nullptr)
+    lse_out[row] = M == -CUDART_INF_F ? -CUDART_INF_F : M + logf(wsum);
+}
+
+constexpr int kWarpsPerCta = 4;
+constexpr int kStages = 2;
+
+template <int D>
+int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* block_table,
+                  const int32_t* ctx_len, int B, int Hq, int Hkv, int max_pages,
+                  int pages_per_split, int num_splits, float scale, float* part_out,
+                  float* part_lse, uint16_t* out, float* lse_out, long long num_pages,
+                  cudaStream_t s) {
+  using S = AttnShape<D>;
+  constexpr int NW = kWarpsPerCta, NST = kStages;
+  const size_t smem = (size_t)NW * NST * S::STAGE_BYTES + NW * NST * sizeof(uint64_t);
+  auto kernel = paged_decode_kernel<D, NW, NST>;
+  static int configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t err =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess)
+      return set_error(SC_ERR_CUDA, "sc_paged_decode_attention: smem attribute: %s",
+                       cudaGetErrorString(err));
+    configured[dev] = 1;
+  }
+  const int G = Hq / Hkv;
+  const int HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid(num_splits, Hkv * HG, B);
+  kernel<<<grid, NW * 32, smem, s>>>(q, kv_pool, block_table, ctx_len, Hq, Hkv, G, HG, max_pages,
+                                     pages_per_split, num_splits, scale_log2, part_out, part_lse,
+                                     out, lse_out, num_pages, device_status_word());
+  if (int rc = check_launch("sc_paged_decode_attention")) return rc;
+  if (num_splits > 1) {
+    combine_kernel<<<B * Hq, 128, 0, s>>>(part_out, part_lse, ctx_len, Hq, num_splits,
+                                         pages_per_split, D, out, lse_out);
+    return check_launch("sc_paged_decode_attention(combine)");
+  }
+  return SC_OK;
+}
+
+}  // namespace
+}  // namespace sc
+
+extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
+                                         int64_t num_pages, const int32_t* block_table,
+                                         const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
+                                         int P, int max_pages, int pages_per_split,
+                                         int num_splits, float scale,
+                                         float* part_out, float* part_lse, sc_bf16* out,
+                                         float* lse_out, void* stream) {
+  const char* name = "sc_paged_decode_attention";
+  SC_REQUIRE(q && kv_pool && block_table && ctx_len && out, SC_ERR_INVALID, "%s: null pointer",
+             name);
+  SC_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, SC_ERR_INVALID,
+             "%s: bad heads Hq=%d Hkv=%d", name, Hq, Hkv);
+  SC_REQUIRE(P == sc::kPage, SC_ERR_UNSUPPORTED, "%s: page size %d != 16", name, P);
+  SC_REQUIRE(max_pages > 0 && pages_per_split > 0 && num_splits > 0, SC_ERR_INVALID,
+             "%s: bad split plan max_pages=%d pages_per_split=%d num_splits=%d", name, max_pages,
+             pages_per_split, num_splits);
+  SC_REQUIRE(num_splits == 1 || (part_out && part_lse), SC_ERR_INVALID,
+             "%s: num_splits > 1 needs part_out and part_lse", name);
+  SC_REQUIRE(num_splits <= 65535 && B <= 65535 && Hkv * ((Hq / Hkv + 7) / 8) <= 65535,
+             SC_ERR_INVALID, "%s: grid too large", name);
+  SC_REQUIRE(num_pages > 0, SC_ERR_INVALID, "%s: num_pages=%lld", name, (long long)num_pages);
+  if (B == 0) return SC_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (D) {
+    case 64:
+      return sc::launch_decode<64>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+                                   pages_per_split, num_splits, scale, part_out, part_lse, out,
+                                   lse_out, num_pages, s);
+    case 128:
+      return sc::launch_decode<128>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+                                    pages_per_split, num_splits, scale, part_out, part_lse, out,
+                                    lse_out, num_pages, s);
+    case 256:
+      return sc::launch_decode<256>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+                                    pages_per_split, num_splits, scale, part_out, part_lse, out,
+                                    lse_out, num_pages, s);
+    default:
+      return sc::set_error(SC_ERR_UNSUPPORTED, "%s: D=%d not in {64,128,256}", name, D);
+  }
+}
+
+extern "C" int sc_attention_combine(const float* part_out, const float* part_lse, int rows,
+                                    int nparts, int D, sc_bf16* out, float* lse_out,
+                                    void* stream) {
+  const char* name = "sc_attention_combine";
+  SC_REQUIRE(part_out && part_lse && out, SC_ERR_INVALID, "%s: null pointer", name);
+  SC_REQUIRE(rows >= 0 && nparts > 0 && D > 0, SC_ERR_INVALID, "%s: rows=%d nparts=%d D=%d", name,
+             rows, nparts, D);
+  if (rows == 0) return SC_OK;
+  sc::combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      part_out, part_lse, nullptr, 1, nparts, 1, D, out, lse_out);
+  return sc::check_launch(name);
+}

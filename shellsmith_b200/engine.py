@@ -1,0 +1,189 @@
+"""Hybrid GDN / full-attention cache engine: the decode cache step on one GPU.
+
+The reference's decode step (studio_compute/mlx_decode.py:18-77
+`decode_rows`) walks the layers; GDN layers concatenate every request's
+recurrent cache, run the token kernel and split the caches back (42-60), and
+attention layers run one request at a time (`_attention_rows`, 80-106). Here
+the caches are persistent device pools and one launch covers every row:
+
+  GDN layer        sc_gdn_decode over all rows, state rows = sequence slots
+  attention layer  sc_kv_append of the new token, then
+                   sc_paged_decode_attention over each row's pages
+
+A sequence's slot is its batch row, its block-table row and its GDN state row,
+so no gather/scatter of caches happens per step; inactive rows are skipped by
+the kernels (state slot -1, slot mapping -1, context length 0).
+Projections, norms and the MLP are outside the cache path and are not run.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import numerics, paged
+from .block_manager import BlockManager
+
+
+@dataclass
+class HybridConfig:
+    layers: int = 48
+    attention_every: int = 4          # layer l is full attention when l % 4 == 3 (3:1)
+    gdn_key_heads: int = 16
+    gdn_value_heads: int = 32
+    key_dim: int = 128
+    value_dim: int = 128
+    q_heads: int = 16
+    kv_heads: int = 2
+    head_dim: int = 256
+    page_size: int = paged.PAGE_SIZE
+    max_seqs: int = 256
+    num_pages: int = 150_000
+    max_context: int = 16_384 + 2_048 + 1_024
+    state_dtype: torch.dtype = torch.float32
+    pages_per_split: int = 64
+
+    def is_attention(self, layer: int) -> bool:
+        return layer % self.attention_every == self.attention_every - 1
+
+    @property
+    def gdn_layers(self) -> list:
+        return [l for l in range(self.layers) if not self.is_attention(l)]
+
+    @property
+    def attention_layers(self) -> list:
+        return [l for l in range(self.layers) if self.is_attention(l)]
+
+    @property
+    def max_pages_per_seq(self) -> int:
+        return math.ceil(self.max_context / self.page_size)
+
+    def state_bytes(self) -> int:
+        elem = torch.finfo(self.state_dtype).bits // 8
+        return (len(self.gdn_layers) * self.max_seqs * self.gdn_value_heads * self.value_dim
+                * self.key_dim * elem)
+
+    def kv_bytes(self) -> int:
+        return (len(self.attention_layers) * self.num_pages * self.kv_heads * 2 * self.page_size
+                * self.head_dim * 2)
+
+
+class HybridCacheEngine:
+    """Device pools + block manager for one GPU's share of sequences."""
+
+    def __init__(self, cfg: HybridConfig, device: torch.device | str = "cuda", seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        dev = self.device
+        n_gdn, n_attn = len(cfg.gdn_layers), len(cfg.attention_layers)
+        self.gdn_index = {l: i for i, l in enumerate(cfg.gdn_layers)}
+        self.attn_index = {l: i for i, l in enumerate(cfg.attention_layers)}
+        self.state = torch.zeros((n_gdn, cfg.max_seqs, cfg.gdn_value_heads, cfg.value_dim,
+                                  cfg.key_dim), dtype=cfg.state_dtype, device=dev)
+        self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads, 2, cfg.page_size,
+                               cfg.head_dim), dtype=torch.bfloat16, device=dev)
+        self.blocks = BlockManager(cfg.num_pages, cfg.page_size, cfg.max_seqs,
+                                   cfg.max_pages_per_seq, seed=seed)
+        # Pinned host mirrors, copied to the device once per step.
+        self._h_table = torch.zeros((cfg.max_seqs, cfg.max_pages_per_seq), dtype=torch.int32,
+                                    pin_memory=True)
+        self.blocks.table = self._h_table.numpy()
+        self._h_ctx = torch.zeros(cfg.max_seqs, dtype=torch.int32, pin_memory=True)
+        self._h_slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, pin_memory=True)
+        self._h_state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, pin_memory=True)
+        self.table = torch.zeros_like(self._h_table, device=dev)
+        self.ctx_len = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
+        self.slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, device=dev)
+        self.state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, device=dev)
+        self._staged = torch.cuda.Event()
+        self._staged.record()
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        pps, nsplit = paged.split_plan(cfg.max_pages_per_seq, cfg.pages_per_split)
+        self.workspace = paged.AttentionWorkspace(cfg.max_seqs, cfg.q_heads, cfg.head_dim, nsplit,
+                                                  device=dev)
+        self.max_pages_in_batch = 1
+
+    # ------------------------------------------------------------ lifecycle
+    def admit(self, owner, prompt_len: int) -> int:
+        """Reserve a slot and pages for a prompt; its GDN state starts at zero."""
+        slot = self.blocks.admit(owner, prompt_len)
+        self.state[:, slot].zero_()
+        return slot
+
+    def release(self, slot: int) -> None:
+        self.blocks.release(slot)
+
+    def write_prompt_kv(self, slot: int, layer: int, k: torch.Tensor, v: torch.Tensor,
+                        start: int = 0) -> None:
+        """Scatter prompt K/V [n, Hkv, D] of one attention layer at positions start.. ."""
+        slots = self.blocks.prompt_slots(slot, start, start + k.shape[0])
+        paged.kv_append(k, v, self.kv[self.attn_index[layer]],
+                        torch.from_numpy(slots).to(self.device, non_blocking=True))
+
+    def begin_step(self) -> int:
+        """Append one token to every active sequence and stage the step's tables.
+
+        Returns the number of active rows (tokens this step decodes).
+        """
+        self._staged.synchronize()  # the previous step's copies have read the staging
+        blocks = self.blocks
+        active = np.flatnonzero(blocks.active)
+        slot_map = np.full(self.cfg.max_seqs, -1, np.int64)
+        slot_map[active] = blocks.append_token(active)
+        self._h_slot_map.numpy()[:] = slot_map
+        self._h_ctx.numpy()[:] = blocks.lengths.astype(np.int32)
+        state_slot = np.full(self.cfg.max_seqs, -1, np.int32)
+        state_slot[active] = active
+        self._h_state_slot.numpy()[:] = state_slot
+        self.max_pages_in_batch = max(1, int(blocks.pages_for(blocks.lengths.max())))
+        self.table.copy_(self._h_table, non_blocking=True)
+        self.ctx_len.copy_(self._h_ctx, non_blocking=True)
+        self.slot_map.copy_(self._h_slot_map, non_blocking=True)
+        self.state_slot.copy_(self._h_state_slot, non_blocking=True)
+        self._staged.record()
+        return len(active)
+
+    # ------------------------------------------------------------ decode
+    def gdn_layer(self, layer: int, q, k, v, decay, beta, out) -> None:
+        numerics.gdn_decode(q, k, v, decay, beta, self.state[self.gdn_index[layer]],
+                            self.state_slot, out=out)
+
+    def attention_layer(self, layer: int, q, k_new, v_new, out) -> None:
+        pool = self.kv[self.attn_index[layer]]
+        paged.kv_append(k_new, v_new, pool, self.slot_map)
+        paged.paged_decode_attention(q, pool, self.table, self.ctx_len, self.scale,
+                                     max_pages_in_batch=self.max_pages_in_batch,
+                                     pages_per_split=self.cfg.pages_per_split,
+                                     workspace=self.workspace, out=out)
+
+    def decode_step(self, inputs: dict, outputs: dict) -> None:
+        """Run every layer's cache work for the staged token of each active row.
+
+        inputs[l] = (q, k, v, decay, beta) for GDN layers, (q, k, v) for
+        attention layers; outputs[l] receives that layer's mixer output.
+        """
+        for layer in range(self.cfg.layers):
+            if self.cfg.is_attention(layer):
+                self.attention_layer(layer, *inputs[layer], outputs[layer])
+            else:
+                self.gdn_layer(layer, *inputs[layer], outputs[layer])
+
+    # ------------------------------------------------------------ accounting
+    def step_bytes(self, lengths: np.ndarray) -> dict:
+        """Algorithmic HBM bytes of one decode step for active context lengths."""
+        c = self.cfg
+        n = len(lengths)
+        gdn = len(c.gdn_layers) * n * (
+            2 * c.gdn_value_heads * c.value_dim * c.key_dim * (torch.finfo(c.state_dtype).bits // 8)
+            + (2 * c.gdn_key_heads * c.key_dim + 2 * c.gdn_value_heads * c.value_dim) * 2
+            + 2 * c.gdn_value_heads * 4)
+        row = c.kv_heads * c.head_dim * 2 * 2          # K + V bytes of one token
+        pages = np.ceil(lengths / c.page_size)
+        attn_layer = (float(lengths.sum()) * row + n * row + n * c.q_heads * c.head_dim * 2 * 2
+                      + float(pages.sum()) * 4)
+        return {"gdn": float(gdn), "attention_per_layer": attn_layer,
+                "attention": attn_layer * len(c.attention_layers),
+                "total": float(gdn) + attn_layer * len(c.attention_layers)}

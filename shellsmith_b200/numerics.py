@@ -1,0 +1,95 @@
+"""GDN recurrent-state kernels behind the reference's call-site names.
+
+Mirrors studio_compute/numerics (reference paths relative to the shellsmith
+project root):
+  gated_delta_token    numerics/gdn_token.py:18-42 -- same argument names,
+                       layouts and assertion behaviour; the state may be
+                       bf16 (reference rounding) or fp32 (this build's
+                       default), and it is updated IN PLACE (the returned
+                       next state is the same tensor). The reference returns
+                       a new array and its caller drops the old one
+                       (mlx_decode.py:53,59-60), so the two are observably
+                       equivalent at that call site.
+  gdn_decode           the batched engine form: [B, H, d] rows, per-row state
+                       slots into a persistent [slots, Hv, dv, dk] pool.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _capi
+from ._torch import ptr, require_cuda, stream_of
+
+
+def gdn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+               beta: torch.Tensor, state: torch.Tensor, state_slot: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """One-token GDN update of rows b (state row state_slot[b]), in place.
+
+    q, k [B, Hk, dk] bf16; v [B, Hv, dv] bf16; g (decay), beta [B, Hv] fp32;
+    state [slots, Hv, dv, dk] fp32 or bf16; state_slot [B] int32 or None
+    (identity). Returns out [B, Hv, dv] bf16.
+    """
+    B, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        require_cuda(name, t, torch.bfloat16, 3, align=8)
+    for name, t in (("g", g), ("beta", beta)):
+        require_cuda(name, t, torch.float32, 2, align=4)
+    if k.shape != q.shape or v.shape[0] != B or g.shape != (B, Hv) or beta.shape != (B, Hv):
+        raise ValueError("gdn_decode: inconsistent shapes")
+    if state.dim() != 4 or tuple(state.shape[1:]) != (Hv, dv, dk):
+        raise ValueError(f"gdn_decode: state must be [slots, {Hv}, {dv}, {dk}]")
+    if state_slot is None and state.shape[0] < B:
+        raise ValueError("gdn_decode: state has fewer slots than rows")
+    if state_slot is not None:
+        require_cuda("state_slot", state_slot, torch.int32, 1, align=4)
+        if state_slot.shape[0] != B:
+            raise ValueError("gdn_decode: state_slot must have one entry per row")
+    if out is None:
+        out = torch.empty((B, Hv, dv), dtype=torch.bfloat16, device=q.device)
+    require_cuda("out", out, torch.bfloat16, 3, align=2)
+    if state.dtype == torch.float32:
+        require_cuda("state", state, torch.float32, 4)
+        name = "sc_gdn_decode"
+    elif state.dtype == torch.bfloat16:
+        require_cuda("state", state, torch.bfloat16, 4, align=8)
+        name = "sc_gdn_decode_bf16"
+    else:
+        raise TypeError("gdn_decode: state must be float32 or bfloat16")
+    _capi.call(name, ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(state), ptr(state_slot),
+               ptr(out), B, Hk, Hv, dk, dv, stream_of(q))
+    return out
+
+
+def gated_delta_token(q_BLJK: torch.Tensor, k_BLJK: torch.Tensor, v_BLHV: torch.Tensor,
+                      g_BLH: torch.Tensor, beta_BLH: torch.Tensor,
+                      state_BHVK: torch.Tensor) -> tuple:
+    """Apply the sequential recurrence for one autoregressive token.
+
+    Same contract as the reference (gdn_token.py:18-42): exactly one row,
+    keys % 32 == 0, heads % key_heads == 0, bf16 q/k/v. g and beta may be
+    bf16 (reference) or fp32; the state may be bf16 (reference rounding) or
+    fp32. Returns (output [B,1,Hv,dv] bf16, state) with the state advanced in
+    place.
+    """
+    batch, length, key_heads, keys = q_BLJK.shape
+    heads, values = v_BLHV.shape[-2:]
+    assert length == 1 and keys % 32 == 0 and heads % key_heads == 0
+    assert k_BLJK.shape == q_BLJK.shape and v_BLHV.shape[:2] == (batch, 1)
+    assert g_BLH.shape == beta_BLH.shape == (batch, 1, heads)
+    assert state_BHVK.shape == (batch, heads, values, keys)
+    assert all(x.dtype == torch.bfloat16 for x in (q_BLJK, k_BLJK, v_BLHV))
+    assert g_BLH.dtype in (torch.bfloat16, torch.float32)
+    assert beta_BLH.dtype in (torch.bfloat16, torch.float32)
+    assert state_BHVK.dtype in (torch.bfloat16, torch.float32)
+    out = gdn_decode(
+        q_BLJK.reshape(batch, key_heads, keys).contiguous(),
+        k_BLJK.reshape(batch, key_heads, keys).contiguous(),
+        v_BLHV.reshape(batch, heads, values).contiguous(),
+        g_BLH.reshape(batch, heads).float().contiguous(),
+        beta_BLH.reshape(batch, heads).float().contiguous(),
+        state_BHVK,
+    )
+    return out.reshape(batch, 1, heads, values), state_BHVK

@@ -1,0 +1,161 @@
+"""Paged KV pool and split-K decode attention (device side).
+
+The reference keeps one concatenating KV buffer per request
+(studio_compute/mlx_request_cache.py:48-100 `OwnedKV`) and runs one SDPA per
+request (mlx_decode.py:80-106). Here every attention layer owns one page pool
+kv_pool[num_pages, Hkv, 2, P, D] (bf16) shared by all sequences; the host
+block manager hands out pages, and these functions move and read them:
+
+  kv_append               scatter new tokens' K/V through a slot mapping
+  kv_gather               read logical K/V back (inverse of kv_append)
+  kv_copy_pages           page-level copy-on-write of forked prefixes
+  paged_decode_attention  split-K attention of one query per sequence over
+                          its ragged pages, then the (out, lse) combine
+  attention_combine       merge per-part (out, lse), e.g. across GPUs
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _capi
+from ._torch import ptr, require_cuda, stream_of
+
+PAGE_SIZE = 16
+
+
+def new_pool(num_pages: int, kv_heads: int, head_dim: int, page_size: int = PAGE_SIZE,
+             device: str | torch.device = "cuda") -> torch.Tensor:
+    """Allocate one layer's pool [num_pages, Hkv, 2, P, D] bf16 (uninitialised)."""
+    return torch.empty((num_pages, kv_heads, 2, page_size, head_dim), dtype=torch.bfloat16,
+                       device=device)
+
+
+def _pool_dims(kv_pool: torch.Tensor):
+    require_cuda("kv_pool", kv_pool, torch.bfloat16, 5)
+    num_pages, hkv, two, page, dim = kv_pool.shape
+    if two != 2:
+        raise ValueError("kv_pool must be [num_pages, Hkv, 2, P, D]")
+    return num_pages, hkv, page, dim
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, kv_pool: torch.Tensor,
+              slot_mapping: torch.Tensor) -> None:
+    """Write k/v [ntok, Hkv, D] into the pool at slot_mapping [ntok] (int64, <0 skips)."""
+    num_pages, hkv, page, dim = _pool_dims(kv_pool)
+    require_cuda("k", k, torch.bfloat16, 3)
+    require_cuda("v", v, torch.bfloat16, 3)
+    require_cuda("slot_mapping", slot_mapping, torch.int64, 1, align=8)
+    ntok = k.shape[0]
+    if k.shape != (ntok, hkv, dim) or v.shape != k.shape or slot_mapping.shape[0] != ntok:
+        raise ValueError("kv_append: k/v must be [ntok, Hkv, D] with one slot per token")
+    _capi.call("sc_kv_append", ptr(k), ptr(v), ptr(kv_pool), ptr(slot_mapping), ntok, hkv, dim,
+               page, num_pages, stream_of(kv_pool))
+
+
+def kv_gather(kv_pool: torch.Tensor, slot_mapping: torch.Tensor) -> tuple:
+    """Logical k, v [ntok, Hkv, D] stored at slot_mapping (zeros for negative slots)."""
+    num_pages, hkv, page, dim = _pool_dims(kv_pool)
+    require_cuda("slot_mapping", slot_mapping, torch.int64, 1, align=8)
+    ntok = slot_mapping.shape[0]
+    k = torch.empty((ntok, hkv, dim), dtype=torch.bfloat16, device=kv_pool.device)
+    v = torch.empty_like(k)
+    _capi.call("sc_kv_gather", ptr(kv_pool), ptr(slot_mapping), ptr(k), ptr(v), ntok, hkv, dim,
+               page, num_pages, stream_of(kv_pool))
+    return k, v
+
+
+def kv_copy_pages(kv_pool: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
+    """Copy pages src[i] -> dst[i] (int32), every head, K and V."""
+    num_pages, hkv, page, dim = _pool_dims(kv_pool)
+    require_cuda("src", src, torch.int32, 1, align=4)
+    require_cuda("dst", dst, torch.int32, 1, align=4)
+    if src.shape != dst.shape:
+        raise ValueError("kv_copy_pages: src and dst must match")
+    _capi.call("sc_kv_copy_pages", ptr(kv_pool), ptr(src), ptr(dst), src.shape[0], hkv, dim,
+               page, num_pages, stream_of(kv_pool))
+
+
+def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None) -> tuple:
+    """(pages_per_split, num_splits) for a batch whose longest sequence has that many pages.
+
+    A split of 64 pages streams 1 MiB of K/V per kv head (D = 256): small
+    enough that a ragged batch has no long tail on 148 SMs, large enough that
+    the partials (8 heads x D fp32) stay under 1% of the K/V bytes.
+    """
+    pps = pages_per_split or 64
+    return pps, max(1, math.ceil(max(1, max_pages_in_batch) / pps))
+
+
+class AttentionWorkspace:
+    """Reusable split-K scratch (partials and their lse) for one layer shape."""
+
+    def __init__(self, batch: int, q_heads: int, head_dim: int, num_splits: int,
+                 device: str | torch.device = "cuda"):
+        self.num_splits = num_splits
+        self.part_out = torch.empty((batch, q_heads, num_splits, head_dim), dtype=torch.float32,
+                                    device=device)
+        self.part_lse = torch.empty((batch, q_heads, num_splits), dtype=torch.float32,
+                                    device=device)
+
+    def fits(self, batch: int, q_heads: int, head_dim: int, num_splits: int) -> bool:
+        b, h, s, d = self.part_out.shape
+        return b >= batch and h == q_heads and d == head_dim and s == num_splits
+
+
+def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: torch.Tensor,
+                           ctx_len: torch.Tensor, scale: float, *,
+                           max_pages_in_batch: int | None = None,
+                           pages_per_split: int | None = None,
+                           workspace: AttentionWorkspace | None = None,
+                           out: torch.Tensor | None = None,
+                           lse_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention of q [B, Hq, D] over each sequence's ctx_len[b] cached tokens.
+
+    block_table [B, max_pages] int32 lists each sequence's pages in token
+    order. max_pages_in_batch (host-known) sizes the grid; when omitted the
+    block-table width is used, which never syncs the device.
+    """
+    num_pages, hkv, page, dim = _pool_dims(kv_pool)
+    require_cuda("q", q, torch.bfloat16, 3)
+    require_cuda("block_table", block_table, torch.int32, 2, align=4)
+    require_cuda("ctx_len", ctx_len, torch.int32, 1, align=4)
+    B, hq, d = q.shape
+    if d != dim or hq % hkv or block_table.shape[0] != B or ctx_len.shape[0] != B:
+        raise ValueError("paged_decode_attention: inconsistent shapes")
+    max_pages = block_table.shape[1]
+    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split)
+    if out is None:
+        out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)
+    require_cuda("out", out, torch.bfloat16, 3)
+    if lse_out is not None:
+        require_cuda("lse_out", lse_out, torch.float32, 1, align=4)
+    part_out = part_lse = None
+    if nsplit > 1:
+        if workspace is None or not workspace.fits(B, hq, dim, nsplit):
+            workspace = AttentionWorkspace(B, hq, dim, nsplit, device=q.device)
+        part_out, part_lse = workspace.part_out, workspace.part_lse
+    _capi.call("sc_paged_decode_attention", ptr(q), ptr(kv_pool), num_pages, ptr(block_table),
+               ptr(ctx_len), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
+               ptr(part_out), ptr(part_lse), ptr(out), ptr(lse_out), stream_of(q))
+    return out
+
+
+def attention_combine(part_out: torch.Tensor, part_lse: torch.Tensor,
+                      out: torch.Tensor | None = None,
+                      lse_out: torch.Tensor | None = None) -> tuple:
+    """Merge part_out [rows, S, D] fp32 with part_lse [rows, S] -> (out bf16, lse fp32)."""
+    require_cuda("part_out", part_out, torch.float32, 3)
+    require_cuda("part_lse", part_lse, torch.float32, 2, align=4)
+    rows, nparts, dim = part_out.shape
+    if part_lse.shape != (rows, nparts):
+        raise ValueError("attention_combine: part_lse must be [rows, S]")
+    if out is None:
+        out = torch.empty((rows, dim), dtype=torch.bfloat16, device=part_out.device)
+    if lse_out is None:
+        lse_out = torch.empty((rows,), dtype=torch.float32, device=part_out.device)
+    _capi.call("sc_attention_combine", ptr(part_out), ptr(part_lse), rows, nparts, dim, ptr(out),
+               ptr(lse_out), stream_of(part_out))
+    return out, lse_out

@@ -1,0 +1,171 @@
+"""K4 paged KV append and K7 split-K decode attention on the GPU vs the CPU oracle.
+
+Bars: the pool layout and append/gather round trip are bit-exact; attention
+outputs are within rtol 2e-2 / atol 2e-3 of float64 `numpy_attention` math
+(restated in oracle.attention), lse within 1e-3.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from shellsmith_b200 import paged
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 2e-2, 2e-3
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def test_append_layout_bit_exact_and_gather_roundtrip(cuda):
+    rng = np.random.default_rng(3)
+    num_pages, hkv, P, D = 11, 2, 16, 256
+    pool = torch.zeros((num_pages, hkv, 2, P, D), dtype=torch.bfloat16, device=cuda)
+    ntok = 40
+    slots = rng.permutation(num_pages * P)[:ntok].astype(np.int64)
+    slots[5] = -1
+    k = torch.randn((ntok, hkv, D), device=cuda).to(torch.bfloat16)
+    v = torch.randn((ntok, hkv, D), device=cuda).to(torch.bfloat16)
+    slot_t = torch.from_numpy(slots).to(cuda)
+    paged.kv_append(k, v, pool, slot_t)
+    # Layout: the oracle's scatter of the same bits must produce the same pool.
+    want = np.zeros(pool.numel(), np.uint16)
+    oatt.pool_write(want, slots, _bits(k), _bits(v), hkv, P, D)
+    assert np.array_equal(_bits(pool).reshape(-1), want)
+    kg, vg = paged.kv_gather(pool, slot_t)
+    keep = slots >= 0
+    assert torch.equal(kg[keep], k[keep]) and torch.equal(vg[keep], v[keep])
+    assert torch.count_nonzero(kg[~keep]) == 0
+    # Copy-on-write pages.
+    src = torch.tensor([1, 4], dtype=torch.int32, device=cuda)
+    dst = torch.tensor([9, 0], dtype=torch.int32, device=cuda)
+    before = pool.clone()
+    paged.kv_copy_pages(pool, src, dst)
+    assert torch.equal(pool[9], before[1]) and torch.equal(pool[0], before[4])
+    assert torch.equal(pool[2:9], before[2:9])
+
+
+def _build_case(rng, lengths, hq, hkv, D, num_pages, cuda, pages_per_seq=None):
+    """Random pool contents and block tables for the given context lengths."""
+    P = paged.PAGE_SIZE
+    need = [math.ceil(L / P) for L in lengths]
+    width = pages_per_seq or max(1, max(need))
+    perm = rng.permutation(num_pages)
+    assert sum(need) <= num_pages
+    table = np.zeros((len(lengths), width), np.int32)
+    cursor = 0
+    for b, n in enumerate(need):
+        table[b, :n] = perm[cursor:cursor + n]
+        cursor += n
+    pool = torch.randn((num_pages, hkv, 2, P, D), device=cuda).to(torch.bfloat16)
+    q = torch.randn((len(lengths), hq, D), device=cuda).to(torch.bfloat16)
+    return pool, q, table
+
+
+def _oracle(pool_np, q_np, table, lengths, hkv, D, scale):
+    outs, lses = [], []
+    for b, L in enumerate(lengths):
+        k, v = oatt.pool_read_pages(pool_np, table[b], L, hkv, paged.PAGE_SIZE, D)
+        o, l = oatt.decode_attention(q_np[b], k, v, scale)
+        outs.append(o)
+        lses.append(l)
+    return np.stack(outs), np.stack(lses)
+
+
+@pytest.mark.parametrize("hq,hkv,D", [(16, 2, 256), (24, 4, 256), (24, 2, 256), (8, 8, 128),
+                                      (4, 1, 64)])
+@pytest.mark.parametrize("pages_per_split", [1, 3, 64])
+def test_decode_attention_matches_oracle(cuda, hq, hkv, D, pages_per_split):
+    rng = np.random.default_rng(hq * 100 + hkv * 10 + D + pages_per_split)
+    lengths = [1, 15, 16, 17, 33, 200, 517, 64]
+    pool, q, table = _build_case(rng, lengths, hq, hkv, D, 160, cuda, pages_per_seq=40)
+    scale = 1.0 / math.sqrt(D)
+    ctx = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    lse = torch.empty(len(lengths) * hq, dtype=torch.float32, device=cuda)
+    out = paged.paged_decode_attention(q, pool, torch.from_numpy(table).to(cuda), ctx, scale,
+                                       pages_per_split=pages_per_split, lse_out=lse)
+    want, want_lse = _oracle(pool.float().cpu().numpy(), q.float().cpu().numpy(), table, lengths,
+                             hkv, D, scale)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(lse.cpu().numpy().reshape(want_lse.shape), want_lse, atol=1e-3)
+
+
+def test_known_answer_uniform_scores(cuda):
+    """q = 0 makes every score equal: the output is the mean of the values.
+    (The reference oracle's known answer: v = [1, 3, 8] seen by the last query -> 4.)"""
+    P, D = paged.PAGE_SIZE, 64
+    pool = torch.zeros((4, 1, 2, P, D), dtype=torch.bfloat16, device=cuda)
+    k = torch.zeros((3, 1, D), dtype=torch.bfloat16, device=cuda)
+    v = torch.zeros((3, 1, D), dtype=torch.bfloat16, device=cuda)
+    v[:, 0, :] = torch.tensor([1.0, 3.0, 8.0], device=cuda)[:, None]
+    paged.kv_append(k, v, pool, torch.tensor([32, 33, 34], dtype=torch.int64, device=cuda))
+    q = torch.zeros((1, 2, D), dtype=torch.bfloat16, device=cuda)
+    out = paged.paged_decode_attention(q, pool, torch.tensor([[2]], dtype=torch.int32,
+                                                             device=cuda),
+                                       torch.tensor([3], dtype=torch.int32, device=cuda), 1.0)
+    assert torch.all(out.float() == 4.0)
+    # The first two keys alone (the reference's first query row) average to 2.
+    out = paged.paged_decode_attention(q, pool, torch.tensor([[2]], dtype=torch.int32,
+                                                             device=cuda),
+                                       torch.tensor([2], dtype=torch.int32, device=cuda), 1.0)
+    assert torch.all(out.float() == 2.0)
+
+
+def test_empty_sequence_gives_zero(cuda):
+    pool = torch.randn((4, 2, 2, 16, 128), device=cuda).to(torch.bfloat16)
+    q = torch.randn((2, 4, 128), device=cuda).to(torch.bfloat16)
+    table = torch.tensor([[0, 1], [2, 3]], dtype=torch.int32, device=cuda)
+    ctx = torch.tensor([0, 20], dtype=torch.int32, device=cuda)
+    for pps in (1, 8):
+        out = paged.paged_decode_attention(q, pool, table, ctx, 0.1, pages_per_split=pps)
+        assert torch.count_nonzero(out[0]) == 0 and torch.isfinite(out[1].float()).all()
+
+
+def test_combine_matches_oracle(cuda):
+    rng = np.random.default_rng(11)
+    rows, parts, D = 7, 5, 256
+    po = rng.standard_normal((rows, parts, D)).astype(np.float32)
+    pl = (rng.standard_normal((rows, parts)) * 3).astype(np.float32)
+    pl[2, 1] = -np.inf
+    pl[4, :] = -np.inf
+    out, lse = paged.attention_combine(torch.from_numpy(po).to(cuda),
+                                       torch.from_numpy(pl).to(cuda))
+    want, want_lse = oatt.combine(po, pl)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    got_lse = lse.cpu().numpy()
+    assert np.isneginf(got_lse[4]) and np.isneginf(want_lse[4])
+    fin = np.isfinite(want_lse)
+    np.testing.assert_allclose(got_lse[fin], want_lse[fin], rtol=1e-5, atol=1e-5)
+
+
+def test_split_combine_algebra_matches_single_pass(cuda):
+    """Splitting a long sequence into parts and combining equals one pass."""
+    rng = np.random.default_rng(12)
+    pool, q, table = _build_case(rng, [3000], 16, 2, 256, 200, cuda)
+    ctx = torch.tensor([3000], dtype=torch.int32, device=cuda)
+    bt = torch.from_numpy(table).to(cuda)
+    one = paged.paged_decode_attention(q, pool, bt, ctx, 0.0625, pages_per_split=4096)
+    many = paged.paged_decode_attention(q, pool, bt, ctx, 0.0625, pages_per_split=5)
+    np.testing.assert_allclose(one.float().cpu().numpy(), many.float().cpu().numpy(),
+                               rtol=RTOL, atol=ATOL)
+
+
+def test_bad_page_index_sets_device_status(cuda):
+    """An out-of-range page in a block table is reported, not dereferenced."""
+    from shellsmith_b200 import _capi
+
+    _capi.device_status()
+    pool = torch.randn((4, 1, 2, 16, 64), device=cuda).to(torch.bfloat16)
+    q = torch.randn((1, 2, 64), device=cuda).to(torch.bfloat16)
+    table = torch.tensor([[0, 99]], dtype=torch.int32, device=cuda)
+    paged.paged_decode_attention(q, pool, table, torch.tensor([20], dtype=torch.int32,
+                                                              device=cuda), 0.1)
+    with pytest.raises(_capi.DeviceFault):
+        _capi.check_device()
+    assert _capi.device_status() == 0
