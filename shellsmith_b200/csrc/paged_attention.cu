@@ -139,6 +139,16 @@ __global__ void __launch_bounds__(NW * 32)
     if (!mbar_wait_bounded(&bar[s], (j / NSTAGE) & 1, status)) break;
     const uint32_t kbase = smem_addr(stage + s * S::STAGE_BYTES);
     const uint32_t vbase = kbase + S::KV_BYTES;
+    const int page_tok = (p_begin + warp + j * NW) * kPage;
+    if (page_tok + kPage > L) {
+      // Rows past the context hold whatever the pool held (possibly Inf/NaN
+      // bits); their probability is 0, but 0 * Inf would poison the sum.
+      uint4* vrows = reinterpret_cast<uint4*>(stage + s * S::STAGE_BYTES + S::KV_BYTES);
+      for (int c = (L - page_tok) * (S::ROW_BYTES / 16) + lane; c < kPage * (S::ROW_BYTES / 16);
+           c += 32)
+        vrows[c] = make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+    }
 
     float sc4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -149,7 +159,7 @@ __global__ void __launch_bounds__(NW * 32)
       mma_bf16_16816(sc4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
     }
 
-    const int tok0 = (p_begin + warp + j * NW) * kPage + (lane >> 2);
+    const int tok0 = page_tok + (lane >> 2);
     const bool lo_ok = tok0 < L, hi_ok = tok0 + 8 < L;
     const float x0 = lo_ok ? sc4[0] * scale_log2 : -CUDART_INF_F;
     const float x1 = lo_ok ? sc4[1] * scale_log2 : -CUDART_INF_F;
