@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=48,
+                    help="decoder layers (3 GDN : 1 attention); fewer only for profiling")
     ap.add_argument("--min-len", type=int, default=512)
     ap.add_argument("--max-len", type=int, default=16_384)
     ap.add_argument("--churn", type=float, default=0.02)
@@ -178,7 +180,7 @@ class Workload:
 
         self.args = args
         self.device = device
-        self.cfg = HybridConfig(max_seqs=args.batch, num_pages=args.num_pages,
+        self.cfg = HybridConfig(layers=args.layers, max_seqs=args.batch, num_pages=args.num_pages,
                                 max_context=args.max_len + 2048 + args.steps + args.warmup + 64,
                                 pages_per_split=args.pages_per_split)
         cfg = self.cfg
@@ -373,8 +375,10 @@ def run_ours(args, world, rank, local):
         "dtype": "bf16 kv / fp32 gdn state",
         "data": "synthetic (seeded; config 3 shapes and distributions)",
         "config": {
-            "workload": "config3 hybrid decode cache step: 48 layers (36 GDN + 12 attention), "
-                        "256 ragged sequences per GPU, ctx U[512,16k], churn 0.02/step",
+            "workload": f"config3 hybrid decode cache step: {cfg.layers} layers "
+                        f"({len(cfg.gdn_layers)} GDN + {len(cfg.attention_layers)} attention), "
+                        f"{args.batch} ragged sequences per GPU, ctx U[{args.min_len},"
+                        f"{args.max_len}], churn {args.churn}/step",
             "global_batch": args.batch * world, "seq_len": f"U[{args.min_len},{args.max_len}]",
             "parallelism": f"sequence-sharded x{world}, no collective",
             "gdn": "Hk16/Hv32 dk=dv=128 fp32 state", "attention": "Hq16/Hkv2 D256 page16",
@@ -473,7 +477,8 @@ def cpu_baseline(args, wl):
     threads = cpu_step.host_threads()
     active = np.flatnonzero(wl.engine.blocks.active)
     sample = args.cpu_sample or min(len(active), 32, max(4, threads))
-    lengths = wl.engine.blocks.lengths[active[:sample]]
+    picked = np.random.default_rng(SEED).choice(active, size=sample, replace=False)
+    lengths = wl.engine.blocks.lengths[picked]
     rng = np.random.default_rng(SEED)
     seqs = [cpu_step.SampledSequence(rng, int(L), len(cfg.gdn_layers), len(cfg.attention_layers),
                                      cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.key_dim,
@@ -483,8 +488,8 @@ def cpu_baseline(args, wl):
     elapsed = cpu_step.run_sample(seqs, layers, 1.0 / math.sqrt(cfg.head_dim), threads, SEED)
     return {"value": round(len(seqs) / elapsed, 2), "unit": UNIT, "cores": threads,
             "kind": "port",
-            "sample": f"{len(seqs)} of the step's sequences (mean ctx "
-                      f"{int(np.mean(lengths))}) x 48 layers, one decode token each, "
+            "sample": f"{len(seqs)} of the step's sequences, drawn at random (mean ctx "
+                      f"{int(np.mean(lengths))}) x {cfg.layers} layers, one decode token each, "
                       f"float64/fp32 NumPy oracle, {threads} threads"}
 
 
