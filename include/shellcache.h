@@ -157,6 +157,38 @@ int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
                               float* part_out, float* part_lse, sc_bf16* out,
                               float* lse_out, void* stream);
 
+/* Split-K decode attention that allocates nothing and takes no scratch.
+ *
+ * No counterpart in the reference: it exists for callers of this library
+ * that cannot allocate device memory at call time -- a plain C / FFI host
+ * that embeds the library without a device allocator of its own, a process
+ * whose device memory belongs to another framework's caching allocator (a
+ * raw cudaMalloc beside it escapes that pool's accounting), or a decode loop
+ * that must neither synchronise the device (cudaFree does) nor risk running
+ * out of memory in the middle of a step.
+ *
+ * Same arguments and results as sc_paged_decode_attention without
+ * part_out / part_lse: the split partials go to a fixed array inside the
+ * library of SC_NOALLOC_SCRATCH_FLOATS floats (32 MiB), which every GPU that
+ * loads the library holds until the process exits. A call needs
+ * B * Hq * num_splits * (D + 1) floats when num_splits > 1 and returns
+ * SC_ERR_INVALID (nothing launched) when that exceeds the array.
+ * The first call on a device looks up the array's device address (a one-time
+ * set-up per device); make that first call before any stream capture.
+ * All calls share the one array and it keeps the last call's contents;
+ * nothing in it needs to start at zero, because every partial a call reads
+ * is written earlier in the same call. Calls that overlap on the GPU (other
+ * streams, other host threads) race on the array: serialise them.
+ * It calls no cudaMalloc, cudaFree or other allocating routine. */
+#define SC_NOALLOC_SCRATCH_FLOATS 8388608
+int sc_paged_decode_attention_noalloc(const sc_bf16* q, const sc_bf16* kv_pool,
+                                      int64_t num_pages, const int32_t* block_table,
+                                      const int32_t* ctx_len, int B, int Hq, int Hkv,
+                                      int D, int P, int max_pages,
+                                      int pages_per_split, int num_splits,
+                                      float scale, sc_bf16* out, float* lse_out,
+                                      void* stream);
+
 /* Merges per-part normalised outputs with their lse:
  *   out[r] = sum_s exp(lse[r,s] - M) o[r,s] / sum_s exp(lse[r,s] - M)
  * over s < nparts (rows r = 0..rows-1, parts with lse = -inf ignored).

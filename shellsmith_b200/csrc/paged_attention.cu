@@ -22,6 +22,8 @@
 //   when the sequence needs one split).
 #include <math_constants.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace sc {
@@ -391,4 +393,72 @@ extern "C" int sc_attention_combine(const float* part_out, const float* part_lse
   sc::combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       part_out, part_lse, nullptr, 1, nparts, 1, D, out, lse_out);
   return sc::check_launch(name);
+}
+
+// ---------------------------------------------------------------------------
+// Split-K decode attention for callers that cannot allocate device memory.
+//
+// The split partials live in one file-scope device array instead of caller
+// scratch. Every GPU that loads this library holds the array (32 MiB) until
+// the process exits. Host code must not pass the array's name to a kernel:
+// on the host that name is only a stand-in symbol, so the device address is
+// looked up once per device with cudaGetSymbolAddress and cached.
+namespace sc {
+namespace {
+
+__device__ __align__(256) float g_noalloc_partials[SC_NOALLOC_SCRATCH_FLOATS];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_partials on the current device (set-up on the
+// first call per device), or nullptr with the error recorded.
+float* noalloc_scratch(const char* name) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error(SC_ERR_CUDA, "%s: no current device (%s)", name, cudaGetErrorString(err));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (err != cudaSuccess || p == nullptr) {
+      set_error(SC_ERR_CUDA, "%s: cudaGetSymbolAddress failed: %s", name,
+                cudaGetErrorString(err));
+      return nullptr;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  return g_noalloc_addr[dev];
+}
+
+}  // namespace
+}  // namespace sc
+
+extern "C" int sc_paged_decode_attention_noalloc(const sc_bf16* q, const sc_bf16* kv_pool,
+                                                 int64_t num_pages, const int32_t* block_table,
+                                                 const int32_t* ctx_len, int B, int Hq, int Hkv,
+                                                 int D, int P, int max_pages, int pages_per_split,
+                                                 int num_splits, float scale, sc_bf16* out,
+                                                 float* lse_out, void* stream) {
+  const char* name = "sc_paged_decode_attention_noalloc";
+  SC_REQUIRE(B >= 0 && Hq > 0 && num_splits > 0 && D > 0, SC_ERR_INVALID,
+             "%s: bad sizes B=%d Hq=%d num_splits=%d D=%d", name, B, Hq, num_splits, D);
+  // Partials [B, Hq, num_splits, D] followed by their lse [B, Hq, num_splits].
+  const long long rows = (long long)B * Hq * num_splits;
+  const long long need = rows * (D + 1LL);
+  SC_REQUIRE(num_splits == 1 || need <= SC_NOALLOC_SCRATCH_FLOATS, SC_ERR_INVALID,
+             "%s: B*Hq*num_splits*(D+1) = %lld floats exceeds the built-in scratch of %d floats "
+             "(32 MiB); use fewer splits (larger pages_per_split) or sc_paged_decode_attention "
+             "with caller scratch",
+             name, need, SC_NOALLOC_SCRATCH_FLOATS);
+  float* scratch = sc::noalloc_scratch(name);
+  if (scratch == nullptr) return SC_ERR_CUDA;
+  float* part_out = num_splits > 1 ? scratch : nullptr;
+  float* part_lse = num_splits > 1 ? scratch + rows * D : nullptr;
+  return sc_paged_decode_attention(q, kv_pool, num_pages, block_table, ctx_len, B, Hq, Hkv, D, P,
+                                   max_pages, pages_per_split, num_splits, scale, part_out,
+                                   part_lse, out, lse_out, stream);
 }
