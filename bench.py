@@ -40,6 +40,12 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "decode cache-step tokens/sec at batch 256 ragged; achieved HBM GB/s vs B200 peak"
+# DRAM bytes (read + write) / algorithmic bytes of one launch, from an ncu
+# capture of this workload at a smaller size (4 layers, ctx U[512, 8k]).
+# Traffic grows in proportion to the K/V tokens read (attention) and the rows
+# updated (GDN), so a full launch's traffic is its algorithmic bytes times this.
+ATTN_TRAFFIC_RATIO = 1.011
+GDN_TRAFFIC_RATIO = 0.950
 UNIT = "tokens/s"
 SEED = 3  # configs 1-4 use seeds 1-4
 
@@ -388,10 +394,14 @@ def run_ours(args, world, rank, local):
         "hbm": {"step_gbs": round(step_gbs, 1), "peak_gbs": hbm,
                 "frac": round(step_gbs / hbm, 4), "peak_source": peaks["source"],
                 "bytes_per_step": round(bytes_total / max(1, len(events))),
-                "gdn_gbs": round(gdn_gbs, 1), "attention_gbs": round(attn_gbs, 1)},
+                "gdn_gbs": round(gdn_gbs, 1), "attention_gbs": round(attn_gbs, 1),
+                "gdn_traffic_per_launch": round(GDN_TRAFFIC_RATIO * gdn_bytes
+                                                / max(1, n_gdn_launch))},
         "roofline": {"bound": "hbm", "kernel": "paged_decode_attention (append+split+combine)",
                      "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(attn_gbs / hbm, 4), "traffic": None,
+                     "frac": round(attn_gbs / hbm, 4),
+                     "traffic": round(ATTN_TRAFFIC_RATIO * attn_bytes / max(1, n_attn_launch)),
+                     "bytes_per_launch": round(attn_bytes / max(1, n_attn_launch)),
                      "peak_source": peaks["source"]},
         "prefill": {"ms_per_step": round(statistics.mean(prefill_ms), 3),
                     "tokens": wl.prefill_tokens, "admitted": wl.admitted,
