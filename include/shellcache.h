@@ -74,7 +74,9 @@ int sc_device_status(unsigned int* status, void* stream);
  * beta   [B, Hv] fp32
  * state  [slots, Hv, dv, dk]    fp32 (sc_gdn_decode) or bf16 (_bf16 variant)
  * state_slot [B] int32          state row of batch row b; NULL = identity;
- *                                 a negative entry skips the row
+ *                                 a negative entry skips the row; an entry
+ *                                 >= num_slots (rows in `state`) is flagged
+ *                                 (DEV_BAD_INDEX) and skipped
  * out    [B, Hv, dv] bf16
  * Supported: dk in {32, 64, 128, 256}, Hv % Hk == 0, dv >= 1.
  * The bf16 variant reproduces the reference rounding points: the decayed
@@ -84,12 +86,37 @@ int sc_device_status(unsigned int* status, void* stream);
 int sc_gdn_decode(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
                   const float* g, const float* beta, float* state,
                   const int32_t* state_slot, sc_bf16* out, int B, int Hk, int Hv,
-                  int dk, int dv, void* stream);
+                  int dk, int dv, int num_slots, void* stream);
 
 int sc_gdn_decode_bf16(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
                        const float* g, const float* beta, sc_bf16* state,
                        const int32_t* state_slot, sc_bf16* out, int B, int Hk,
-                       int Hv, int dk, int dv, void* stream);
+                       int Hv, int dk, int dv, int num_slots, void* stream);
+
+/* GDN chunked prefill (chunk 64) on tcgen05 tensor cores, state IN PLACE.
+ *
+ * Replaces studio_compute/numerics/ops.py:151-215 `gated_delta_chunked`
+ * (and the fused numerics/gdn_fused.py:86-122 `gated_delta_chunks` once its
+ * gates are made): runs every token of each sequence through the recurrence
+ * above, starting from its state row and leaving the final state there.
+ *
+ * Packed token-major layout: token n of sequence b is row
+ * cu_seqlens[b] + n (or b * T + n when cu_seqlens is NULL).
+ * q, k   [tokens, Hk, 128] bf16 (L2-normalised), 16-byte aligned
+ * v      [tokens, Hv, 128] bf16
+ * g      [tokens, Hv] fp32 multiplicative decay (clamped to [1e-6, 1] before
+ *        its log, as the reference's fp32 chunk path does); beta [tokens, Hv]
+ * state  [num_slots, Hv, 128, 128] fp32; state_slot [B] int32 or NULL
+ *        (identity); a slot >= num_slots is flagged and its sequence skipped
+ * cu_seqlens [B + 1] int32 or NULL (then every sequence has T tokens)
+ * out    [tokens, Hv, 128] bf16
+ * total_tokens  number of packed tokens when cu_seqlens is given
+ * Supported: dk = dv = 128, Hv % Hk == 0. */
+int sc_gdn_chunk_prefill(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
+                         const float* g, const float* beta, float* state,
+                         const int32_t* state_slot, const int32_t* cu_seqlens,
+                         sc_bf16* out, int B, int T, int total_tokens, int Hk, int Hv,
+                         int dk, int dv, int num_slots, void* stream);
 
 /* --------------------------------------------------------------------------
  * (b) KV append: scatter new keys/values into the paged pool.

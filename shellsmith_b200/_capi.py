@@ -22,8 +22,10 @@ SIGNATURES = {
     "sc_version": [],
     "sc_last_error": [ctypes.c_char_p, _I],
     "sc_device_status": [ctypes.POINTER(ctypes.c_uint), _P],
-    "sc_gdn_decode": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
-    "sc_gdn_decode_bf16": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
+    "sc_gdn_decode": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "sc_gdn_decode_bf16": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "sc_gdn_chunk_prefill": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                             _I, _P],
     "sc_kv_append": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_gather": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_copy_pages": [_P, _P, _P, _I, _I, _I, _I, _I64, _P],

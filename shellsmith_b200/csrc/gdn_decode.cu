@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kWarps * 32)
                       const uint16_t* __restrict__ v, const float* __restrict__ g,
                       const float* __restrict__ beta, ST* __restrict__ state,
                       const int32_t* __restrict__ state_slot, uint16_t* __restrict__ out,
-                      int Hk, int Hv, int dv) {
+                      int Hk, int Hv, int dv, int num_slots, unsigned int* status) {
   using Shape = RowShape<DK>;
   constexpr int LPR = Shape::LPR, VPL = Shape::VPL, RPP = Shape::RPP, U = Shape::U;
 
@@ -80,6 +80,10 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int h = bh - b * Hv;
   const int slot = state_slot != nullptr ? state_slot[b] : b;
   if (slot < 0) return;
+  if (slot >= num_slots) {
+    if (threadIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
+    return;
+  }
   const int kh = h / (Hv / Hk);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -156,11 +160,14 @@ __global__ void __launch_bounds__(kWarps * 32)
 template <typename ST>
 int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       const float* g, const float* beta, ST* state, const int32_t* slot,
-                      uint16_t* out, int B, int Hk, int Hv, int dk, int dv, void* stream) {
+                      uint16_t* out, int B, int Hk, int Hv, int dk, int dv, int num_slots,
+                      void* stream) {
   SC_REQUIRE(q && k && v && g && beta && state && out, SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE(B >= 0 && Hk > 0 && Hv > 0 && dv > 0, SC_ERR_INVALID,
              "%s: bad sizes B=%d Hk=%d Hv=%d dv=%d", name, B, Hk, Hv, dv);
   SC_REQUIRE(Hv % Hk == 0, SC_ERR_INVALID, "%s: Hv=%d not a multiple of Hk=%d", name, Hv, Hk);
+  SC_REQUIRE(num_slots > 0 && (slot != nullptr || num_slots >= B), SC_ERR_INVALID,
+             "%s: num_slots=%d for B=%d", name, num_slots, B);
   SC_REQUIRE((long long)B * Hv < (1LL << 31), SC_ERR_INVALID, "%s: B*Hv too large", name);
   if (B == 0) return SC_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -169,7 +176,8 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
   case DK_: {                                                                                \
     dim3 grid(B * Hv, (dv + RowShape<DK_>::ROWS_PER_CTA - 1) / RowShape<DK_>::ROWS_PER_CTA); \
     gdn_decode_kernel<DK_, ST><<<grid, block, 0, s>>>(q, k, v, g, beta, state, slot, out, Hk, \
-                                                      Hv, dv);                               \
+                                                      Hv, dv, num_slots,                     \
+                                                      device_status_word());                 \
     break;                                                                                   \
   }
   switch (dk) {
@@ -189,15 +197,16 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
 
 extern "C" int sc_gdn_decode(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v, const float* g,
                              const float* beta, float* state, const int32_t* state_slot,
-                             sc_bf16* out, int B, int Hk, int Hv, int dk, int dv, void* stream) {
+                             sc_bf16* out, int B, int Hk, int Hv, int dk, int dv, int num_slots,
+                             void* stream) {
   return sc::launch_gdn_decode<float>("sc_gdn_decode", q, k, v, g, beta, state, state_slot, out, B,
-                                      Hk, Hv, dk, dv, stream);
+                                      Hk, Hv, dk, dv, num_slots, stream);
 }
 
 extern "C" int sc_gdn_decode_bf16(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
                                   const float* g, const float* beta, sc_bf16* state,
                                   const int32_t* state_slot, sc_bf16* out, int B, int Hk, int Hv,
-                                  int dk, int dv, void* stream) {
+                                  int dk, int dv, int num_slots, void* stream) {
   return sc::launch_gdn_decode<uint16_t>("sc_gdn_decode_bf16", q, k, v, g, beta, state, state_slot,
-                                         out, B, Hk, Hv, dk, dv, stream);
+                                         out, B, Hk, Hv, dk, dv, num_slots, stream);
 }

@@ -59,7 +59,7 @@ def gdn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tenso
     else:
         raise TypeError("gdn_decode: state must be float32 or bfloat16")
     _capi.call(name, ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(state), ptr(state_slot),
-               ptr(out), B, Hk, Hv, dk, dv, stream_of(q))
+               ptr(out), B, Hk, Hv, dk, dv, state.shape[0], stream_of(q))
     return out
 
 
@@ -93,3 +93,78 @@ def gated_delta_token(q_BLJK: torch.Tensor, k_BLJK: torch.Tensor, v_BLHV: torch.
         state_BHVK,
     )
     return out.reshape(batch, 1, heads, values), state_BHVK
+
+
+def gdn_chunk_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                      beta: torch.Tensor, state: torch.Tensor,
+                      state_slot: torch.Tensor | None = None,
+                      cu_seqlens: torch.Tensor | None = None, *, T: int | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked (64) GDN prefill of packed sequences on the tensor cores, state in place.
+
+    q, k [tokens, Hk, 128] bf16; v [tokens, Hv, 128] bf16; g (decay), beta
+    [tokens, Hv] fp32; state [slots, Hv, 128, 128] fp32. Sequence b is rows
+    cu_seqlens[b]:cu_seqlens[b+1] (int32 [B+1]), or b*T:(b+1)*T when
+    cu_seqlens is None. Returns out [tokens, Hv, 128] bf16.
+    """
+    tokens, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        require_cuda(name, t, torch.bfloat16, 3)
+    for name, t in (("g", g), ("beta", beta)):
+        require_cuda(name, t, torch.float32, 2, align=4)
+    require_cuda("state", state, torch.float32, 4)
+    if k.shape != q.shape or v.shape[0] != tokens or g.shape != (tokens, Hv) \
+            or beta.shape != (tokens, Hv):
+        raise ValueError("gdn_chunk_prefill: inconsistent shapes")
+    if tuple(state.shape[1:]) != (Hv, dv, dk):
+        raise ValueError(f"gdn_chunk_prefill: state must be [slots, {Hv}, {dv}, {dk}]")
+    if cu_seqlens is None:
+        if T is None or T <= 0 or tokens % T:
+            raise ValueError("gdn_chunk_prefill: give cu_seqlens or a T dividing the tokens")
+        B = tokens // T
+    else:
+        require_cuda("cu_seqlens", cu_seqlens, torch.int32, 1, align=4)
+        B = cu_seqlens.shape[0] - 1
+        T = 0
+    if state_slot is not None:
+        require_cuda("state_slot", state_slot, torch.int32, 1, align=4)
+        if state_slot.shape[0] != B:
+            raise ValueError("gdn_chunk_prefill: one state slot per sequence")
+    elif state.shape[0] < B:
+        raise ValueError("gdn_chunk_prefill: state has fewer slots than sequences")
+    if out is None:
+        out = torch.empty((tokens, Hv, dv), dtype=torch.bfloat16, device=q.device)
+    require_cuda("out", out, torch.bfloat16, 3, align=2)
+    _capi.call("sc_gdn_chunk_prefill", ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(state),
+               ptr(state_slot), ptr(cu_seqlens), ptr(out), B, T, tokens, Hk, Hv, dk, dv,
+               state.shape[0], stream_of(q))
+    return out
+
+
+def gated_delta_chunked(q, k, v, g, beta, state, chunk=64, *, compute_dtype=None,
+                        backend=None) -> tuple:
+    """Chunked gated delta rule with the reference's signature (ops.py:151).
+
+    q, k [B, T, Hk, 128], v [B, T, Hv, 128] bf16; g (decay), beta [B, T, Hv];
+    state [B, Hv, 128, 128]. Returns (y [B, T, Hv, 128] in v's dtype, final
+    fp32 state). The chunk is 64 and the arithmetic is fixed (fp32
+    accumulation, split-bf16 operands); `compute_dtype` and `backend` are
+    accepted for call-site compatibility. An fp32 contiguous state is
+    advanced in place and returned; any other state is copied first.
+    """
+    if chunk != 64:
+        raise ValueError("gated_delta_chunked: the tensor-core kernel uses chunk = 64")
+    B, T, Hk, dk = q.shape
+    Hv, dv = v.shape[-2:]
+    assert k.shape == q.shape and v.shape[:2] == (B, T) and Hv % Hk == 0
+    assert g.shape == beta.shape == (B, T, Hv) and state.shape == (B, Hv, dv, dk)
+    s = state if (state.dtype == torch.float32 and state.is_contiguous()) else \
+        state.float().contiguous()
+    y = gdn_chunk_prefill(
+        q.to(torch.bfloat16).reshape(B * T, Hk, dk).contiguous(),
+        k.to(torch.bfloat16).reshape(B * T, Hk, dk).contiguous(),
+        v.to(torch.bfloat16).reshape(B * T, Hv, dv).contiguous(),
+        g.float().reshape(B * T, Hv).contiguous(), beta.float().reshape(B * T, Hv).contiguous(),
+        s, T=T)
+    return y.reshape(B, T, Hv, dv).to(v.dtype), s

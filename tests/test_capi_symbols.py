@@ -41,7 +41,7 @@ def test_version_and_error_text_without_gpu(library):
     assert library.sc_version() >= 100
     # Argument validation runs on the host before any CUDA call.
     code = library.sc_gdn_decode(None, None, None, None, None, None, None, None, 1, 1, 1, 128,
-                                 128, None)
+                                 128, 1, None)
     assert code == 1
     assert "null pointer" in _capi.last_error()
     code = library.sc_paged_decode_attention(1, 1, 10, 1, 1, 1, 16, 2, 256, 8, 4, 64, 1, 0.1,

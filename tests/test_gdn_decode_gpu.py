@@ -121,3 +121,17 @@ def test_bad_shapes_raise(cuda):
     state = torch.zeros((1, 6, 16, 48), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(AssertionError):  # keys % 32 != 0, as the reference asserts
         numerics.gated_delta_token(q, q, v, g, g, state)
+
+
+def test_out_of_range_state_slot_is_flagged_not_read(cuda):
+    from shellsmith_b200 import _capi
+
+    _capi.device_status()
+    rng = np.random.default_rng(8)
+    q, k, v, g, beta = gdn_token_inputs(rng, 2, 2, 4, 128, 128)
+    state = torch.zeros((2, 4, 128, 128), dtype=torch.float32, device=cuda)
+    slot = torch.tensor([0, 5], dtype=torch.int32, device=cuda)
+    numerics.gdn_decode(*_dev(q, k, v, g, beta), state, slot)
+    with pytest.raises(_capi.DeviceFault):
+        _capi.check_device()
+    assert torch.count_nonzero(state[1]) == 0
