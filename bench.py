@@ -68,6 +68,8 @@ def parse():
                     help="sequences in the CPU baseline sample (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-config1", action="store_true",
+                    help="skip the config-1 chunked-prefill measurement")
     return ap.parse_args()
 
 
@@ -234,13 +236,24 @@ class Workload:
                     device=device)
                 self.outputs[layer] = torch.empty((B, cfg.gdn_value_heads, cfg.value_dim),
                                                   dtype=torch.bfloat16, device=device)
-        # Prompt K/V source for prefills of admitted sequences.
-        self.prompt_k = torch.randn((2048, cfg.kv_heads, cfg.head_dim), generator=gen,
+        # Prompt inputs for the prefill of admitted sequences: one packed
+        # buffer of PROMPT_CAP tokens, shared by every layer (values are
+        # synthetic; their distributions match the decode inputs).
+        cap = self.PROMPT_CAP
+        self.prompt_k = torch.randn((cap, cfg.kv_heads, cfg.head_dim), generator=gen,
                                     device=device).to(torch.bfloat16)
         self.prompt_v = torch.randn_like(self.prompt_k)
+        self.prompt_gdn = gdn_token_inputs_device(gen, cap, cfg.gdn_key_heads,
+                                                  cfg.gdn_value_heads, cfg.key_dim,
+                                                  cfg.value_dim, device=device)
+        self.prompt_out = torch.empty((cap, cfg.gdn_value_heads, cfg.value_dim),
+                                      dtype=torch.bfloat16, device=device)
         self.finished = 0
         self.admitted = 0
         self.prefill_tokens = 0
+        self.prefill_launches = 0
+
+    PROMPT_CAP = 16384
 
     def _new_id(self):
         self.next_id += 1
@@ -264,12 +277,19 @@ class Workload:
         return new
 
     def prefill(self, new: list) -> None:
-        """Write the admitted prompts' K/V into every attention layer's pages."""
-        for slot, prompt in new:
-            for layer in self.cfg.attention_layers:
-                self.engine.write_prompt_kv(slot, layer, self.prompt_k[:prompt],
-                                            self.prompt_v[:prompt])
-            self.prefill_tokens += prompt
+        """Prefill the admitted prompts: chunked GDN prefill into their state
+        rows (all GDN layers) and their K/V into every attention layer's pages."""
+        gdn = lambda layer, n: tuple(t[:n] for t in self.prompt_gdn)  # noqa: E731
+        kv = lambda layer, n: (self.prompt_k[:n], self.prompt_v[:n])  # noqa: E731
+        group, total = [], 0
+        for slot, prompt in new + [(None, None)]:
+            if slot is None or total + prompt > self.PROMPT_CAP:
+                self.prefill_launches += self.engine.prefill(group, gdn, kv, self.prompt_out)
+                group, total = [], 0
+            if slot is not None:
+                group.append((slot, prompt))
+                total += prompt
+                self.prefill_tokens += prompt
 
 
 def run_ours(args, world, rank, local):
@@ -326,6 +346,7 @@ def run_ours(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     events, layer_events = [], []
+    launches_before = wl.prefill_launches
     with ClockSampler(local) as clocks:
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -334,6 +355,7 @@ def run_ours(args, world, rank, local):
         wall = time.perf_counter() - t0
     barrier(world)
     _capi.check_device()
+    timed_launches = launches_per_step() * args.steps + wl.prefill_launches - launches_before
 
     decode_ms = [s0.elapsed_time(s1) for s0, s1, *_ in events]
     prefill_ms = [p0.elapsed_time(p1) for _, _, p0, p1, *_ in events]
@@ -357,6 +379,9 @@ def run_ours(args, world, rank, local):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, wl, world)
+    prefill_c1 = None
+    if not args.no_config1 and rank == 0:
+        prefill_c1 = config1_prefill(device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -406,24 +431,74 @@ def run_ours(args, world, rank, local):
         "prefill": {"ms_per_step": round(statistics.mean(prefill_ms), 3),
                     "tokens": wl.prefill_tokens, "admitted": wl.admitted,
                     "finished": wl.finished,
-                    "note": "prompt K/V written to every attention layer; GDN prompt state "
-                            "starts at zero (chunked prefill kernel not in this step)"},
+                    "note": "admitted prompts: chunked GDN prefill (tcgen05) into their state "
+                            "rows for every GDN layer + K/V written to every attention layer; "
+                            "timed separately, excluded from decode bytes"},
         "wall_ms_per_step": round(wall_max * 1e3 / args.steps, 3),
-        "gpu_launches": launches_per_step() * args.steps + wl.admitted * len(
-            cfg.attention_layers),
+        "gpu_launches": timed_launches,
         "clocks": clocks.summary(),
     }
     if e2e is not None:
         line["e2e"] = e2e
+    if prefill_c1 is not None:
+        line["config1_prefill"] = prefill_c1
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
     return line
 
 
+def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:
+    """Config 1: chunked GDN prefill, B=8, T=4096, 16 key / 32 value heads, 128 x 128,
+    fp32 state, on the tensor cores. Algorithmic FLOPs and bytes of the reference
+    chunk algorithm (per (sequence, value head, chunk): QK^T/KK^T, two solves, two
+    m-products, three state products, the inverse)."""
+    import torch
+
+    from shellsmith_b200 import numerics
+    from shellsmith_b200.workloads import gdn_token_inputs_device
+
+    B, T, Hk, Hv, d, C = 8, 4096, 16, 32, 128, 64
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    q, k, v, decay, beta = gdn_token_inputs_device(gen, B * T, Hk, Hv, d, d, device=device)
+    state = torch.zeros((B, Hv, d, d), dtype=torch.float32, device=device)
+    out = torch.empty((B * T, Hv, d), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        numerics.gdn_chunk_prefill(q, k, v, decay, beta, state, T=T, out=out)
+    times = []
+    for _ in range(steps):
+        state.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        numerics.gdn_chunk_prefill(q, k, v, decay, beta, state, T=T, out=out)
+        e1.record(stream)
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = statistics.median(a.elapsed_time(b) for a, b in times)
+    per_chunk = 3 * (2 * 2 * C * C * d) + 3 * 2 * C * d * d + 2 * C ** 3 / 3
+    flops = per_chunk * B * Hv * (T // C)
+    nbytes = (2 * B * T * Hk * d * 2 + 2 * B * T * Hv * d * 2 + 2 * B * T * Hv * 4
+              + 2 * B * Hv * d * d * 4)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
+        ROOT / "MEASURED_PEAKS.json").exists() else {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+    tflops = flops / (ms / 1e3) / 1e12
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"workload": "config1 chunked GDN prefill B=8 T=4096 Hk16/Hv32 128x128 fp32 state",
+            "ms": round(ms, 3), "tokens_per_s": round(B * T / (ms / 1e3), 1),
+            "algorithmic_gflop": round(flops / 1e9, 1), "tflops": round(tflops, 1),
+            "tensor_peak_tflops": peaks["bf16_tflops"],
+            "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
+            "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4),
+            "launches": steps}
+
+
 def run_e2e(args, wl, world):
-    """Same step through the public API with host buffers: pinned H2D inputs and
-    D2H outputs every step, copies overlapped with compute on side streams."""
+    """Same step through the public API with host buffers: every step stages its
+    tables (host bookkeeping), copies every layer's inputs host->device from
+    pinned memory and every output back, copies overlapped with compute on side
+    streams; wall clock per step, summed over the steps."""
     import torch
 
     eng, cfg = wl.engine, wl.cfg
@@ -437,8 +512,6 @@ def run_e2e(args, wl, world):
     bytes_out = sum(t.numel() * t.element_size() for t in host_out.values())
 
     def step():
-        new = wl.churn()
-        wl.prefill(new)
         n = eng.begin_step()
         ready = []
         with torch.cuda.stream(h2d):
@@ -463,16 +536,25 @@ def run_e2e(args, wl, world):
         comp.wait_stream(d2h)
         return n
 
+    def admit():
+        # Churn and prefill of admitted prompts are reported separately; they
+        # run before the timed part of each step.
+        wl.prefill(wl.churn())
+        torch.cuda.synchronize()
+
     for _ in range(2):
+        admit()
         step()
     torch.cuda.synchronize()
     barrier(world)
-    tokens = 0
-    t0 = time.perf_counter()
+    tokens, elapsed = 0, 0.0
     for _ in range(args.steps):
+        admit()
+        t0 = time.perf_counter()
         tokens += step()
-    torch.cuda.synchronize()
-    elapsed = max_over_ranks(time.perf_counter() - t0, world)
+        torch.cuda.synchronize()
+        elapsed += time.perf_counter() - t0
+    elapsed = max_over_ranks(elapsed, world)
     tokens = sum_over_ranks(tokens, world)
     return {"value": round(tokens / elapsed, 1), "unit": UNIT,
             "h2d_bytes_per_step": int(bytes_in), "d2h_bytes_per_step": int(bytes_out),

@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kC = 64;    // chunk length
 constexpr int kD = 128;   // key and value width
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // 8 warps: two per TMEM lane quarter
 
 // Shared memory plan (byte offsets from a 1024-aligned base).
 constexpr uint32_t OFF_KQ = 0;          // [2 dk halves][K rows 0-63 | Q rows 64-127][128 B]
@@ -51,7 +51,8 @@ constexpr uint32_t OFF_SMALL = 180224;  // lg, beta, decay, r [64] floats; barri
 // Aliases used while a chunk is prepared (regions free at that time):
 constexpr uint32_t OFF_MH = OFF_SH;            // m hi [128 rows (0-63 used)][128 B]
 constexpr uint32_t OFF_ML = OFF_SH + 16384;    // m lo
-constexpr uint32_t OFF_AMAT = OFF_SH + 32768;  // A (strict lower) fp32 [64][68]
+constexpr uint32_t OFF_AMAT = OFF_SH + 32768;  // A (strict lower) fp32 [64][68], then X
+constexpr uint32_t OFF_TBUF = OFF_SH + 50176;  // inverse scratch fp32 [32][32]
 constexpr uint32_t OFF_XTH = OFF_WH;           // X^T rows hi [64 rows][128 B]
 constexpr uint32_t OFF_XTL = OFF_WL;           // lo
 constexpr int kAStride = 68;                   // fp32 row stride of A (conflict-free float4 rows)
@@ -77,6 +78,22 @@ __device__ __forceinline__ void store_chunks_hilo(uint8_t* hi, uint8_t* lo, int 
   }
 }
 
+// Stores 8 consecutive values as one 16-byte chunk (chunk index c of a row) of
+// a hi tile and a lo tile.
+__device__ __forceinline__ void store_chunk8_hilo(uint8_t* hi, uint8_t* lo, int row, int c,
+                                                  const float* x) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float a = x[2 * e], b = x[2 * e + 1];
+    h[e] = pack_bf16x2(a, b);
+    l[e] = pack_bf16x2(a - bf16_lo(h[e]), b - bf16_hi(h[e]));
+  }
+  const uint32_t off = (uint32_t)row * 128u + (uint32_t)(((c ^ (row & 7)) << 4));
+  *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_chunk_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -88,13 +105,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  float* s_lg = reinterpret_cast<float*>(sm + OFF_SMALL);
+  float* s_lg = reinterpret_cast<float*>(sm + OFF_SMALL);  // log2 prefix sums of the gates
   float* s_beta = s_lg + 64;
   float* s_decay = s_beta + 64;
   float* s_r = s_decay + 64;
   uint64_t* bar_tma = reinterpret_cast<uint64_t*>(s_r + 64);
   uint64_t* bar_mma = bar_tma + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  float* Xf = reinterpret_cast<float*>(sm + OFF_AMAT);  // A, inverted in place into X
+  float* Tbuf = reinterpret_cast<float*>(sm + OFF_TBUF);
 
   const int bh = blockIdx.x;
   const int b = bh / Hv;
@@ -114,7 +133,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int i = tid;  // value row = TMEM lane
+  const int lane_id = tid & 31;
+  // Two warps serve each TMEM lane quarter; `hf` picks the half of the columns.
+  const int quarter = warp & 3;
+  const int hf = warp >> 2;
+  const int row = quarter * 32 + lane_id;  // TMEM lane: value row i (or token row t)
+  const uint32_t lane = (uint32_t)(quarter * 32) << 16;
 
   if (tid == 0) {
     mbar_init(bar_tma, 1);
@@ -126,12 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *s_tmem;
-  const uint32_t lane = (uint32_t)(warp * 32) << 16;
 
-  // Initial state row i -> TMEM.
-  float* srow = state + ((size_t)slot * Hv + h) * kD * kD + (size_t)i * kD;
+  // Initial state: row i, columns [64 hf, 64 hf + 64) -> TMEM.
+  float* srow = state + ((size_t)slot * Hv + h) * kD * kD + (size_t)row * kD + 64 * hf;
 #pragma unroll 1
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < 2; ++q) {
     float v[32];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -141,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       v[4 * e + 2] = x.z;
       v[4 * e + 3] = x.w;
     }
-    tc::tmem_st32(tmem + lane + T_S + 32 * q, v);
+    tc::tmem_st32(tmem + lane + T_S + 64 * hf + 32 * q, v);
   }
   tc::tmem_wait_st();
 
@@ -150,10 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int pending_tma = 0, pending_mma = 0;
   const int nchunks = (len + kC - 1) / kC;
   auto wait_mma = [&]() {
-    int done = mbar_wait_bounded(bar_mma, mma_phase, status) ? 1 : 0;
-    if (done) {
-      mma_phase ^= 1;
-    }
+    const int done = mbar_wait_bounded(bar_mma, mma_phase, status) ? 1 : 0;
+    if (done) mma_phase ^= 1;
     ok = __syncthreads_and(done && ok);
     if (ok) pending_mma = 0;
     tc::fence_after();
@@ -165,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tok0 = start + c * kC;
     const int valid = min(kC, len - c * kC);
 
-    // ---- (1) chunk tiles by TMA; gates on the CUDA cores meanwhile.
+    // ---- (1) chunk tiles by TMA; gates (log2 domain) on the CUDA cores meanwhile.
     if (tid == 0) {
       mbar_arrive_expect_tx(bar_tma, 6 * 8192);
 #pragma unroll
@@ -180,11 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool on = tid < valid;
       const float gv = on ? g[(size_t)(tok0 + tid) * Hv + h] : 1.f;
       s_beta[tid] = on ? beta[(size_t)(tok0 + tid) * Hv + h] : 0.f;
-      float lg = logf(fminf(fmaxf(gv, 1e-6f), 1.f));
+      float lg = log2f(fminf(fmaxf(gv, 1e-6f), 1.f));
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const float y = __shfl_up_sync(0xffffffffu, lg, off);
-        if ((tid & 31) >= off) lg += y;
+        if (lane_id >= off) lg += y;
       }
       s_lg[tid] = lg;
     }
@@ -192,8 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid >= 32 && tid < 64) s_lg[tid] += s_lg[31];
     __syncthreads();
     if (tid < 64) {
-      s_decay[tid] = expf(s_lg[tid]);
-      s_r[tid] = expf(s_lg[63] - s_lg[tid]);
+      s_decay[tid] = exp2f(s_lg[tid]);
+      s_r[tid] = exp2f(s_lg[63] - s_lg[tid]);
     }
     {
       const int done = mbar_wait_bounded(bar_tma, tma_phase, status) ? 1 : 0;
@@ -219,59 +240,142 @@ __global__ void __launch_bounds__(kThreads, 1)
     pending_mma = 1;
     if (!wait_mma()) break;
 
-    // ---- (3) rows t of A (warps 0-1) and of m (warps 2-3).
+    // ---- (3) A rows (lanes 0-63) in fp32 smem and m rows (lanes 64-127) as
+    //          bf16 hi/lo; this warp owns columns [32 hf, 32 hf + 32).
     {
-      float row[64];
-      tc::tmem_ld32(tmem + lane + T_KK, row);
-      tc::tmem_ld32(tmem + lane + T_KK + 32, row + 32);
-      const int t = tid & 63;
+      float v[32];
+      tc::tmem_ld32(tmem + lane + T_KK + 32 * hf, v);
+      const int t = row & 63;
       const float lgt = s_lg[t];
-      if (warp < 2) {
+      if (quarter < 2) {
         const float bt = s_beta[t];
-        float4* arow = reinterpret_cast<float4*>(sm + OFF_AMAT) + t * (kAStride / 4);
+        float4* arow = reinterpret_cast<float4*>(Xf + t * kAStride + 32 * hf);
 #pragma unroll
-        for (int j4 = 0; j4 < 16; ++j4) {
-          float4 a;
-          const int j = 4 * j4;
-          a.x = j + 0 < t ? bt * expf(lgt - s_lg[j + 0]) * row[j + 0] : 0.f;
-          a.y = j + 1 < t ? bt * expf(lgt - s_lg[j + 1]) * row[j + 1] : 0.f;
-          a.z = j + 2 < t ? bt * expf(lgt - s_lg[j + 2]) * row[j + 2] : 0.f;
-          a.w = j + 3 < t ? bt * expf(lgt - s_lg[j + 3]) * row[j + 3] : 0.f;
-          arow[j4] = a;
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float a[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = 32 * hf + 4 * j4 + e;
+            a[e] = j < t ? bt * exp2f(lgt - s_lg[j]) * v[4 * j4 + e] : 0.f;
+          }
+          arow[j4] = make_float4(a[0], a[1], a[2], a[3]);
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 64; ++j) row[j] = j <= t ? expf(lgt - s_lg[j]) * row[j] : 0.f;
-        tc::store_row_hilo(sm + OFF_MH, sm + OFF_ML, t, row);
+        for (int e = 0; e < 32; ++e) {
+          const int j = 32 * hf + e;
+          v[e] = j <= t ? exp2f(lgt - s_lg[j]) * v[e] : 0.f;
+        }
+        store_chunks_hilo(sm + OFF_MH, sm + OFF_ML, t, 4 * hf, v);
       }
     }
     __syncthreads();
 
-    // ---- (4) X = (I + A)^-1, column j per thread (warps 0-1).
-    if (warp < 2) {
-      const int j = tid;
-      const float* A = reinterpret_cast<const float*>(sm + OFF_AMAT);
-      float x[64];
+    // ---- (4) X = (I + A)^-1 in place, by 16 x 16 blocks.
+    // L0: warp w < 4 inverts diagonal block w; lane c < 16 owns column c.
+    if (warp < 4) {
+      const int c16 = lane_id & 15;
+      const float* Ab = Xf + (16 * warp) * kAStride + 16 * warp;
+      float x[16];
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {
-        float acc = (t == j) ? 1.f : 0.f;
+      for (int r = 0; r < 16; ++r) {
+        float acc = (r == c16) ? 1.f : 0.f;
 #pragma unroll
-        for (int k = 0; k < t; ++k) acc = fmaf(-A[t * kAStride + k], x[k], acc);
-        x[t] = acc;
+        for (int k = 0; k < r; ++k) acc = fmaf(-Ab[r * kAStride + k], x[k], acc);
+        x[r] = acc;
       }
-      tc::store_row_hilo(sm + OFF_XTH, sm + OFF_XTL, j, x);  // X^T row j
+      __syncwarp();
+      if (lane_id < 16) {
+        float* Xb = Xf + (16 * warp) * kAStride + 16 * warp + c16;
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {                           // X rows, column j
-        const uint16_t hi = f_to_bf16(x[t]);
-        const uint16_t lo = f_to_bf16(x[t] - bf16_to_f(hi));
-        *reinterpret_cast<uint16_t*>(sm + OFF_XYH + tc::swz(t, j)) = hi;
-        *reinterpret_cast<uint16_t*>(sm + OFF_XYL + tc::swz(t, j)) = lo;
+        for (int r = 0; r < 16; ++r) Xb[r * kAStride] = x[r];
       }
+    }
+    __syncthreads();
+    // L1: X[2p+1][2p] = -D_{2p+1}^-1 (A[2p+1][2p] D_{2p}^-1), p = 0, 1.
+    {
+      const int p = tid >> 7, r = (tid >> 3) & 15, c0 = (tid & 7) * 2;
+      const float* Arow = Xf + (16 * (2 * p + 1) + r) * kAStride + 16 * (2 * p);
+      const float* Xd = Xf + (16 * (2 * p)) * kAStride + 16 * (2 * p) + c0;
+      float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float a = Arow[k];
+        t0 = fmaf(a, Xd[k * kAStride], t0);
+        t1 = fmaf(a, Xd[k * kAStride + 1], t1);
+      }
+      Tbuf[p * 256 + r * 16 + c0] = t0;
+      Tbuf[p * 256 + r * 16 + c0 + 1] = t1;
+      __syncthreads();
+      const float* Drow = Xf + (16 * (2 * p + 1) + r) * kAStride + 16 * (2 * p + 1);
+      float x0 = 0.f, x1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float d = Drow[k];
+        x0 = fmaf(d, Tbuf[p * 256 + k * 16 + c0], x0);
+        x1 = fmaf(d, Tbuf[p * 256 + k * 16 + c0 + 1], x1);
+      }
+      float* Xo = Xf + (16 * (2 * p + 1) + r) * kAStride + 16 * (2 * p) + c0;
+      Xo[0] = -x0;
+      Xo[1] = -x1;
+    }
+    __syncthreads();
+    // L2: X[32:64][0:32] = -X[32:64][32:64] (A[32:64][0:32] X[0:32][0:32]).
+    {
+      const int r = tid >> 3, c0 = (tid & 7) * 4;
+      const float* Arow = Xf + (32 + r) * kAStride;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int k = 0; k < 32; ++k) {
+        const float a = Arow[k];
+        const float4 xk = *reinterpret_cast<const float4*>(Xf + k * kAStride + c0);
+        acc.x = fmaf(a, xk.x, acc.x);
+        acc.y = fmaf(a, xk.y, acc.y);
+        acc.z = fmaf(a, xk.z, acc.z);
+        acc.w = fmaf(a, xk.w, acc.w);
+      }
+      *reinterpret_cast<float4*>(Tbuf + r * 32 + c0) = acc;
+      __syncthreads();
+      const float* Drow = Xf + (32 + r) * kAStride + 32;
+      float4 xo = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int k = 0; k < 32; ++k) {
+        const float d = Drow[k];
+        const float4 tk = *reinterpret_cast<const float4*>(Tbuf + k * 32 + c0);
+        xo.x = fmaf(d, tk.x, xo.x);
+        xo.y = fmaf(d, tk.y, xo.y);
+        xo.z = fmaf(d, tk.z, xo.z);
+        xo.w = fmaf(d, tk.w, xo.w);
+      }
+      __syncthreads();  // every thread has read A[32:64][0:32] and X before it is overwritten
+      *reinterpret_cast<float4*>(Xf + (32 + r) * kAStride + c0) =
+          make_float4(-xo.x, -xo.y, -xo.z, -xo.w);
+    }
+    __syncthreads();
+    // X -> bf16 hi/lo: X^T rows (B of the Y GEMM) and X rows (rows 0-63 of [X;Y]).
+    {
+      const int j = tid & 63, part = tid >> 6;
+      float xc[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) xc[e] = Xf[(16 * part + e) * kAStride + j];
+      store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, j, 2 * part, xc);
+      store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, j, 2 * part + 1, xc + 8);
+      const float4* xr = reinterpret_cast<const float4*>(Xf + j * kAStride + 16 * part);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float4 x4 = xr[e];
+        xc[4 * e] = x4.x;
+        xc[4 * e + 1] = x4.y;
+        xc[4 * e + 2] = x4.z;
+        xc[4 * e + 3] = x4.w;
+      }
+      store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part, xc);
+      store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part + 1, xc + 8);
     }
     fence_proxy_async_smem();
     __syncthreads();
 
-    // ---- (5) Y = m X -> TMEM cols T_Y (lanes 0-63).
+    // ---- (5) Y = m X -> TMEM cols T_Y (lanes 0-63); rows -> [X;Y] rows 64-127.
     if (tid == 0) {
       tc::fence_after();
       constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
@@ -289,25 +393,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     pending_mma = 1;
     if (!wait_mma()) break;
-    if (warp < 2) {
-      float y[64];
-      tc::tmem_ld32(tmem + lane + T_Y, y);
-      tc::tmem_ld32(tmem + lane + T_Y + 32, y + 32);
-      tc::store_row_hilo(sm + OFF_XYH, sm + OFF_XYL, 64 + tid, y);
+    if (quarter < 2) {
+      float y[32];
+      tc::tmem_ld32(tmem + lane + T_Y + 32 * hf, y);
+      store_chunks_hilo(sm + OFF_XYH, sm + OFF_XYL, 64 + row, 4 * hf, y);
     }
 
-    // ---- (6) S hi/lo -> smem (A of G12); decay_63 * S -> TMEM.
+    // ---- (6) S hi/lo -> smem (A of G12); decay_63 * S -> TMEM. Columns [64 hf, +64).
     {
       const float dl = s_decay[63];
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         float v[32];
-        tc::tmem_ld32(tmem + lane + T_S + 32 * q, v);
-        const uint32_t kb = (uint32_t)(q >> 1) * 16384u;
-        store_chunks_hilo(sm + OFF_SH + kb, sm + OFF_SL + kb, i, 4 * (q & 1), v);
+        const uint32_t col = T_S + 64 * hf + 32 * q;
+        tc::tmem_ld32(tmem + lane + col, v);
+        store_chunks_hilo(sm + OFF_SH + hf * 16384, sm + OFF_SL + hf * 16384, row, 4 * q, v);
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] *= dl;
-        tc::tmem_st32(tmem + lane + T_S + 32 * q, v);
+        tc::tmem_st32(tmem + lane + col, v);
       }
       tc::tmem_wait_st();
     }
@@ -335,30 +438,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     pending_mma = 1;
     if (!wait_mma()) break;
 
-    // ---- (8) W^T row i; zero U^T columns; decay * P2^T in the O^T columns.
+    // ---- (8) W^T row i for tokens [32 hf, +32); zero those U^T columns;
+    //          decay * P2^T in the matching O^T columns.
     {
-      float p[64];
-      tc::tmem_ld32(tmem + lane + T_P, p);
-      tc::tmem_ld32(tmem + lane + T_P + 32, p + 32);
-      const uint8_t* vt = sm + OFF_V + (i >> 6) * 8192;
-      const int iv = i & 63;
+      float p[32];
+      tc::tmem_ld32(tmem + lane + T_P + 32 * hf, p);
+      const uint8_t* vt = sm + OFF_V + (row >> 6) * 8192;
+      const int iv = row & 63;
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {
+      for (int e = 0; e < 32; ++e) {
+        const int t = 32 * hf + e;
         const float vti = bf16_to_f(*reinterpret_cast<const uint16_t*>(vt + tc::swz(t, iv)));
-        p[t] = s_beta[t] * (vti - s_decay[t] * p[t]);
+        p[e] = s_beta[t] * (vti - s_decay[t] * p[e]);
       }
-      tc::store_row_hilo(sm + OFF_WH, sm + OFF_WL, i, p);
+      store_chunks_hilo(sm + OFF_WH, sm + OFF_WL, row, 4 * hf, p);
       float z[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) z[e] = 0.f;
-      tc::tmem_st32(tmem + lane + T_P, z);
-      tc::tmem_st32(tmem + lane + T_P + 32, z);
-      tc::tmem_ld32(tmem + lane + T_P + 64, p);
-      tc::tmem_ld32(tmem + lane + T_P + 96, p + 32);
+      tc::tmem_st32(tmem + lane + T_P + 32 * hf, z);
+      tc::tmem_ld32(tmem + lane + T_P + 64 + 32 * hf, p);
 #pragma unroll
-      for (int t = 0; t < 64; ++t) p[t] *= s_decay[t];
-      tc::tmem_st32(tmem + lane + T_P + 64, p);
-      tc::tmem_st32(tmem + lane + T_P + 96, p + 32);
+      for (int e = 0; e < 32; ++e) p[e] *= s_decay[32 * hf + e];
+      tc::tmem_st32(tmem + lane + T_P + 64 + 32 * hf, p);
       tc::tmem_wait_st();
     }
     fence_proxy_async_smem();
@@ -384,20 +485,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     pending_mma = 1;
     if (!wait_mma()) break;
 
-    // ---- (10) O^T -> out (bf16); (U^T r) hi/lo -> smem (A of GS).
+    // ---- (10) O^T -> out (bf16) for tokens [32 hf, +32); (U^T r) hi/lo -> smem.
     {
-      float u[64];
-      tc::tmem_ld32(tmem + lane + T_P + 64, u);
-      tc::tmem_ld32(tmem + lane + T_P + 96, u + 32);
-      uint16_t* orow = out + ((size_t)tok0 * Hv + h) * kD + i;
+      float u[32];
+      tc::tmem_ld32(tmem + lane + T_P + 64 + 32 * hf, u);
+      uint16_t* orow = out + ((size_t)(tok0 + 32 * hf) * Hv + h) * kD + row;
 #pragma unroll
-      for (int t = 0; t < 64; ++t)
-        if (t < valid) orow[(size_t)t * Hv * kD] = f_to_bf16(u[t]);
-      tc::tmem_ld32(tmem + lane + T_P, u);
-      tc::tmem_ld32(tmem + lane + T_P + 32, u + 32);
+      for (int e = 0; e < 32; ++e)
+        if (32 * hf + e < valid) orow[(size_t)e * Hv * kD] = f_to_bf16(u[e]);
+      tc::tmem_ld32(tmem + lane + T_P + 32 * hf, u);
 #pragma unroll
-      for (int t = 0; t < 64; ++t) u[t] *= s_r[t];
-      tc::store_row_hilo(sm + OFF_WH, sm + OFF_WL, i, u);
+      for (int e = 0; e < 32; ++e) u[e] *= s_r[32 * hf + e];
+      store_chunks_hilo(sm + OFF_WH, sm + OFF_WL, row, 4 * hf, u);
     }
     fence_proxy_async_smem();
     tc::fence_before();
@@ -426,9 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (pending_mma) mbar_wait_bounded(bar_mma, mma_phase, status);
   } else {
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 2; ++q) {
       float v[32];
-      tc::tmem_ld32(tmem + lane + T_S + 32 * q, v);
+      tc::tmem_ld32(tmem + lane + T_S + 64 * hf + 32 * q, v);
 #pragma unroll
       for (int e = 0; e < 8; ++e)
         reinterpret_cast<float4*>(srow + 32 * q)[e] =

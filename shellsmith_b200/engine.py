@@ -116,6 +116,38 @@ class HybridCacheEngine:
     def release(self, slot: int) -> None:
         self.blocks.release(slot)
 
+    def prefill(self, new: list, gdn_inputs, kv_inputs, out=None) -> int:
+        """Run admitted prompts through every layer's cache work.
+
+        new: [(slot, prompt_len)] of sequences admitted this step (their GDN
+        state rows start at zero). gdn_inputs(layer, ntok) -> (q, k, v, decay,
+        beta) packed [ntok, ...] in `new` order; kv_inputs(layer, ntok) -> (k, v)
+        [ntok, Hkv, D]. GDN layers run the chunked prefill kernel over all
+        prompts at once (one launch per layer, varlen); attention layers write
+        the prompts' K/V into their pages. Returns the kernels launched.
+        """
+        if not new:
+            return 0
+        lengths = [n for _, n in new]
+        total = int(sum(lengths))
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32),
+                          device=self.device)
+        slots = torch.tensor([s for s, _ in new], dtype=torch.int32, device=self.device)
+        kv_slots = torch.from_numpy(np.concatenate(
+            [self.blocks.prompt_slots(s, 0, n) for s, n in new])).to(self.device)
+        launched = 0
+        for layer in range(self.cfg.layers):
+            if self.cfg.is_attention(layer):
+                k, v = kv_inputs(layer, total)
+                paged.kv_append(k, v, self.kv[self.attn_index[layer]], kv_slots)
+            else:
+                q, k, v, decay, beta = gdn_inputs(layer, total)
+                numerics.gdn_chunk_prefill(q, k, v, decay, beta,
+                                           self.state[self.gdn_index[layer]], slots, cu,
+                                           out=None if out is None else out[:total])
+            launched += 1
+        return launched
+
     def write_prompt_kv(self, slot: int, layer: int, k: torch.Tensor, v: torch.Tensor,
                         start: int = 0) -> None:
         """Scatter prompt K/V [n, Hkv, D] of one attention layer at positions start.. ."""
