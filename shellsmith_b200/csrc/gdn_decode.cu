@@ -13,12 +13,21 @@
 // U rows of loads before it computes, giving 16*U*VPL bytes in flight per
 // lane. Loads and stores use the streaming (evict-first) cache hint: the
 // state of one layer is far larger than L2 and is not reused in the step.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace sc {
 namespace {
 
-constexpr int kWarps = 4;
+// Launch shape: warps per CTA and state rows each lane keeps in flight.
+#ifndef SC_GDN_WARPS
+#define SC_GDN_WARPS 4
+#endif
+#ifndef SC_GDN_ROWS_IN_FLIGHT
+#define SC_GDN_ROWS_IN_FLIGHT 8
+#endif
+constexpr int kWarps = SC_GDN_WARPS;
 
 template <typename ST>
 struct StateIO;
@@ -60,7 +69,7 @@ struct RowShape {
   static constexpr int LPR = (DK / 4 >= 32) ? 32 : DK / 4;  // lanes per state row
   static constexpr int VPL = DK / (4 * LPR);                 // float4 per lane per row
   static constexpr int RPP = 32 / LPR;                       // rows per warp pass
-  static constexpr int U = (VPL >= 2) ? 4 : 8;               // passes in flight
+  static constexpr int U = (VPL >= 2) ? SC_GDN_ROWS_IN_FLIGHT / 2 : SC_GDN_ROWS_IN_FLIGHT;
   static constexpr int ROWS_PER_WARP = RPP * U;
   static constexpr int ROWS_PER_CTA = kWarps * ROWS_PER_WARP;
 };
@@ -157,6 +166,104 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// Fast path for an fp32 state with dk = 128: one CTA per (row b, value head h)
+// streams the dv x 128 state through shared memory in 32-row chunks of 16 KiB,
+// each one bulk copy (TMA engine) in and one bulk copy out, so an SM keeps
+// ~3 x 64 KiB of state loads in flight without spending registers on them.
+// Warp w updates rows 8w..8w+7 of each chunk in place in shared memory.
+constexpr int kBulkRows = 32;
+constexpr int kBulkChunkBytes = kBulkRows * 128 * 4;
+#ifndef SC_GDN_BULK_CHUNKS
+#define SC_GDN_BULK_CHUNKS 2  // 16 KiB chunks per CTA (32 KiB: ~7 CTAs per SM)
+#endif
+constexpr int kBulkChunksPerCta = SC_GDN_BULK_CHUNKS;
+
+__global__ void __launch_bounds__(128)
+    gdn_decode_bulk_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                           const uint16_t* __restrict__ v, const float* __restrict__ g,
+                           const float* __restrict__ beta, float* __restrict__ state,
+                           const int32_t* __restrict__ state_slot, uint16_t* __restrict__ out,
+                           int Hk, int Hv, int dv, int num_slots, unsigned int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int nchunks = kBulkChunksPerCta;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nchunks * kBulkChunkBytes);
+  const int chunk0 = blockIdx.y * nchunks;  // first 32-row chunk of this CTA
+  const int bh = blockIdx.x;
+  const int b = bh / Hv;
+  const int h = bh - b * Hv;
+  const int slot = state_slot != nullptr ? state_slot[b] : b;
+  if (slot < 0) return;
+  if (slot >= num_slots) {
+    if (threadIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
+    return;
+  }
+  if (status != nullptr && (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT))
+    return;
+  const int kh = h / (Hv / Hk);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* S = state + ((size_t)slot * Hv + h) * (size_t)dv * 128 +
+             (size_t)chunk0 * kBulkRows * 128;
+
+  if (tid == 0) {
+    for (int c = 0; c < nchunks; ++c) mbar_init(&bars[c], 1);
+    fence_mbar_init();
+    for (int c = 0; c < nchunks; ++c) {
+      mbar_arrive_expect_tx(&bars[c], kBulkChunkBytes);
+      bulk_g2s(smem + c * kBulkChunkBytes, S + (size_t)c * kBulkRows * 128, kBulkChunkBytes,
+               &bars[c]);
+    }
+  }
+  const float4 kf = load_bf16x4(k + ((size_t)b * Hk + kh) * 128 + 4 * lane);
+  const float4 qf = load_bf16x4(q + ((size_t)b * Hk + kh) * 128 + 4 * lane);
+  const float decay = g[bh], bt = beta[bh];
+  __syncthreads();  // barrier initialisation is visible before anyone waits
+
+  int ok = 1;
+  for (int c = 0; c < nchunks; ++c) {
+    if (ok && !mbar_wait_bounded(&bars[c], 0, status)) ok = 0;
+    if (ok) {
+      float4* rows = reinterpret_cast<float4*>(smem + c * kBulkChunkBytes);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int lr = 8 * warp + r;
+        float4 s4 = rows[lr * 32 + lane];
+        s4.x *= decay;
+        s4.y *= decay;
+        s4.z *= decay;
+        s4.w *= decay;
+        float pred = s4.x * kf.x + s4.y * kf.y + s4.z * kf.z + s4.w * kf.w;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) pred += __shfl_xor_sync(0xffffffffu, pred, off);
+        const int row = (chunk0 + c) * kBulkRows + lr;
+        const float delta = bt * (bf16_to_f(v[(size_t)bh * dv + row]) - pred);
+        s4.x = fmaf(delta, kf.x, s4.x);
+        s4.y = fmaf(delta, kf.y, s4.y);
+        s4.z = fmaf(delta, kf.z, s4.z);
+        s4.w = fmaf(delta, kf.w, s4.w);
+        float o = s4.x * qf.x + s4.y * qf.y + s4.z * qf.z + s4.w * qf.w;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) o += __shfl_xor_sync(0xffffffffu, o, off);
+        rows[lr * 32 + lane] = s4;
+        if (lane == 0) out[(size_t)bh * dv + row] = f_to_bf16(o);
+      }
+    }
+    fence_proxy_async_smem();  // this thread's smem writes are visible to the bulk store
+    __syncthreads();
+    if (tid == 0 && ok) {
+      bulk_s2g(S + (size_t)c * kBulkRows * 128, smem + c * kBulkChunkBytes, kBulkChunkBytes);
+      bulk_commit();
+    }
+  }
+  if (tid == 0) {
+    if (!ok) {
+      // A load never arrived (flagged): let the copies still in flight land
+      // before the CTA's shared memory is released.
+      for (int c = 0; c < nchunks; ++c) mbar_wait_bounded(&bars[c], 0, status);
+    }
+    bulk_wait_read_all();
+  }
+}
+
 template <typename ST>
 int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       const float* g, const float* beta, ST* state, const int32_t* slot,
@@ -171,6 +278,25 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
   SC_REQUIRE((long long)B * Hv < (1LL << 31), SC_ERR_INVALID, "%s: B*Hv too large", name);
   if (B == 0) return SC_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if constexpr (std::is_same<ST, float>::value) {
+    if (dk == 128 && dv % (kBulkRows * kBulkChunksPerCta) == 0) {
+      const int smem = kBulkChunksPerCta * (kBulkChunkBytes + 8);
+      static int configured[64] = {};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t err = cudaFuncSetAttribute(
+            gdn_decode_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (err != cudaSuccess)
+          return set_error(SC_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(err));
+        configured[dev] = 1;
+      }
+      dim3 grid(B * Hv, dv / (kBulkRows * kBulkChunksPerCta));
+      gdn_decode_bulk_kernel<<<grid, 128, smem, s>>>(q, k, v, g, beta, state, slot, out, Hk, Hv,
+                                                    dv, num_slots, device_status_word());
+      return check_launch(name);
+    }
+  }
   dim3 block(kWarps * 32);
 #define SC_GDN_CASE(DK_)                                                                     \
   case DK_: {                                                                                \

@@ -298,8 +298,15 @@ __global__ void combine_kernel(const float* __restrict__ part_out,
     lse_out[row] = M == -CUDART_INF_F ? -CUDART_INF_F : M + logf(wsum);
 }
 
-constexpr int kWarpsPerCta = 4;
-constexpr int kStages = 2;
+// Launch shape: warps per CTA and shared-memory stages (one page each) per warp.
+#ifndef SC_ATTN_WARPS
+#define SC_ATTN_WARPS 4
+#endif
+#ifndef SC_ATTN_STAGES
+#define SC_ATTN_STAGES 3
+#endif
+constexpr int kWarpsPerCta = SC_ATTN_WARPS;
+constexpr int kStages = SC_ATTN_STAGES;
 
 template <int D>
 int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* block_table,

@@ -44,7 +44,7 @@ class HybridConfig:
     num_pages: int = 150_000
     max_context: int = 16_384 + 2_048 + 1_024
     state_dtype: torch.dtype = torch.float32
-    pages_per_split: int = 64
+    pages_per_split: int | None = None   # None: adapt to the batch (paged.split_plan)
 
     def is_attention(self, layer: int) -> bool:
         return layer % self.attention_every == self.attention_every - 1
@@ -101,10 +101,12 @@ class HybridCacheEngine:
         self._staged = torch.cuda.Event()
         self._staged.record()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
-        pps, nsplit = paged.split_plan(cfg.max_pages_per_seq, cfg.pages_per_split)
+        # Scratch for the smallest split size the plan can pick (16 pages).
+        _, nsplit = paged.split_plan(cfg.max_pages_per_seq, cfg.pages_per_split or 16)
         self.workspace = paged.AttentionWorkspace(cfg.max_seqs, cfg.q_heads, cfg.head_dim, nsplit,
                                                   device=dev)
         self.max_pages_in_batch = 1
+        self.total_pages = 0
 
     # ------------------------------------------------------------ lifecycle
     def admit(self, owner, prompt_len: int) -> int:
@@ -171,6 +173,7 @@ class HybridCacheEngine:
         state_slot[active] = active
         self._h_state_slot.numpy()[:] = state_slot
         self.max_pages_in_batch = max(1, int(blocks.pages_for(blocks.lengths.max())))
+        self.total_pages = int(np.ceil(blocks.lengths[active] / self.cfg.page_size).sum())
         self.table.copy_(self._h_table, non_blocking=True)
         self.ctx_len.copy_(self._h_ctx, non_blocking=True)
         self.slot_map.copy_(self._h_slot_map, non_blocking=True)
@@ -189,6 +192,7 @@ class HybridCacheEngine:
         paged.paged_decode_attention(q, pool, self.table, self.ctx_len, self.scale,
                                      max_pages_in_batch=self.max_pages_in_batch,
                                      pages_per_split=self.cfg.pages_per_split,
+                                     total_pages=self.total_pages,
                                      workspace=self.workspace, out=out)
 
     def decode_step(self, inputs: dict, outputs: dict) -> None:

@@ -78,14 +78,35 @@ def kv_copy_pages(kv_pool: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -
                page, num_pages, stream_of(kv_pool))
 
 
-def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None) -> tuple:
+_SM_COUNT: dict = {}
+
+
+def sm_count(device) -> int:
+    index = torch.device(device).index or 0
+    if index not in _SM_COUNT:
+        _SM_COUNT[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    return _SM_COUNT[index]
+
+
+def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
+               total_work: int | None = None, sms: int = 148) -> tuple:
     """(pages_per_split, num_splits) for a batch whose longest sequence has that many pages.
 
-    A split of 64 pages streams 1 MiB of K/V per kv head (D = 256): small
-    enough that a ragged batch has no long tail on 148 SMs, large enough that
-    the partials (8 heads x D fp32) stay under 1% of the K/V bytes.
+    Without an explicit size, a split is the largest power of two of pages,
+    at most 256 (4 MiB of K/V per kv head at D = 256), that still leaves at
+    least 4 CTAs per SM for `total_work` = sum over sequences of pages x kv
+    heads x head groups. Large splits keep the partials and their combine
+    small; the floor keeps a single long sequence spread over every SM.
     """
-    pps = pages_per_split or 64
+    if pages_per_split:
+        pps = pages_per_split
+    elif total_work:
+        target = max(1, total_work // (4 * sms))
+        pps = 16
+        while pps * 2 <= min(256, target):
+            pps *= 2
+    else:
+        pps = 64
     return pps, max(1, math.ceil(max(1, max_pages_in_batch) / pps))
 
 
@@ -102,13 +123,21 @@ class AttentionWorkspace:
 
     def fits(self, batch: int, q_heads: int, head_dim: int, num_splits: int) -> bool:
         b, h, s, d = self.part_out.shape
-        return b >= batch and h == q_heads and d == head_dim and s == num_splits
+        return b >= batch and h == q_heads and d == head_dim and s >= num_splits
+
+    def views(self, batch: int, num_splits: int) -> tuple:
+        """Contiguous [batch, Hq, num_splits, D] / [batch, Hq, num_splits] views of the scratch."""
+        b, h, s, d = self.part_out.shape
+        n = batch * h * num_splits
+        return (self.part_out.view(-1)[:n * d].view(batch, h, num_splits, d),
+                self.part_lse.view(-1)[:n].view(batch, h, num_splits))
 
 
 def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: torch.Tensor,
                            ctx_len: torch.Tensor, scale: float, *,
                            max_pages_in_batch: int | None = None,
                            pages_per_split: int | None = None,
+                           total_pages: int | None = None,
                            workspace: AttentionWorkspace | None = None,
                            out: torch.Tensor | None = None,
                            lse_out: torch.Tensor | None = None) -> torch.Tensor:
@@ -116,7 +145,8 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
 
     block_table [B, max_pages] int32 lists each sequence's pages in token
     order. max_pages_in_batch (host-known) sizes the grid; when omitted the
-    block-table width is used, which never syncs the device.
+    block-table width is used, which never syncs the device. total_pages
+    (host-known sum of the sequences' pages) lets the split size adapt.
     """
     num_pages, hkv, page, dim = _pool_dims(kv_pool)
     require_cuda("q", q, torch.bfloat16, 3)
@@ -126,7 +156,10 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     if d != dim or hq % hkv or block_table.shape[0] != B or ctx_len.shape[0] != B:
         raise ValueError("paged_decode_attention: inconsistent shapes")
     max_pages = block_table.shape[1]
-    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split)
+    groups = hkv * ((hq // hkv + 7) // 8)
+    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
+                             None if total_pages is None else total_pages * groups,
+                             sm_count(q.device))
     if out is None:
         out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)
     require_cuda("out", out, torch.bfloat16, 3)
@@ -136,7 +169,7 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     if nsplit > 1:
         if workspace is None or not workspace.fits(B, hq, dim, nsplit):
             workspace = AttentionWorkspace(B, hq, dim, nsplit, device=q.device)
-        part_out, part_lse = workspace.part_out, workspace.part_lse
+        part_out, part_lse = workspace.views(B, nsplit)
     _capi.call("sc_paged_decode_attention", ptr(q), ptr(kv_pool), num_pages, ptr(block_table),
                ptr(ctx_len), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
                ptr(part_out), ptr(part_lse), ptr(out), ptr(lse_out), stream_of(q))
