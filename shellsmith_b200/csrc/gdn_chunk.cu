@@ -47,7 +47,8 @@ constexpr uint32_t OFF_XYH = 114688;    // [X rows 0-63 | Y rows 64-127][128 B] 
 constexpr uint32_t OFF_XYL = 131072;    // lo
 constexpr uint32_t OFF_WH = 147456;     // W^T hi, later (U^T r) hi [128 rows][128 B]
 constexpr uint32_t OFF_WL = 163840;     // lo
-constexpr uint32_t OFF_SMALL = 180224;  // lg, beta, decay, r [64] floats; barriers; TMEM base
+constexpr uint32_t OFF_KQ2 = 180224;    // second [K | Q] buffer: chunk c uses KQ[c & 1]
+constexpr uint32_t OFF_SMALL = 212992;  // lg, beta, decay, r [64] floats; barriers; TMEM base
 // Aliases used while a chunk is prepared (regions free at that time):
 constexpr uint32_t OFF_MH = OFF_SH;            // m hi [128 rows (0-63 used)][128 B]
 constexpr uint32_t OFF_ML = OFF_SH + 16384;    // m lo
@@ -56,7 +57,7 @@ constexpr uint32_t OFF_TBUF = OFF_SH + 50176;  // inverse scratch fp32 [32][32]
 constexpr uint32_t OFF_XTH = OFF_WH;           // X^T rows hi [64 rows][128 B]
 constexpr uint32_t OFF_XTL = OFF_WL;           // lo
 constexpr int kAStride = 68;                   // fp32 row stride of A (conflict-free float4 rows)
-constexpr uint32_t SMEM_BYTES = OFF_SMALL + 4 * 64 * 4 + 32 + 1024;  // + 1024 alignment slack
+constexpr uint32_t SMEM_BYTES = OFF_SMALL + 5 * 64 * 4 + 64 + 1024;  // + 1024 alignment slack
 
 // TMEM columns (512 allocated).
 constexpr uint32_t T_S = 0, T_P = 128, T_KK = 256, T_Y = 320;
@@ -109,8 +110,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* s_beta = s_lg + 64;
   float* s_decay = s_beta + 64;
   float* s_r = s_decay + 64;
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(s_r + 64);
-  uint64_t* bar_mma = bar_tma + 1;
+  float* s_inv = s_r + 64;  // 2^(lg_0 - lg_j): the column factor of the decay ratios
+  uint64_t* bar_kq = reinterpret_cast<uint64_t*>(s_inv + 64);  // [2]: K/Q tiles of a buffer
+  uint64_t* bar_v = bar_kq + 2;                               // V tile
+  uint64_t* bar_mma = bar_v + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_mma + 1);
   float* Xf = reinterpret_cast<float*>(sm + OFF_AMAT);  // A, inverted in place into X
   float* Tbuf = reinterpret_cast<float*>(sm + OFF_TBUF);
@@ -141,7 +144,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t lane = (uint32_t)(quarter * 32) << 16;
 
   if (tid == 0) {
-    mbar_init(bar_tma, 1);
+    mbar_init(&bar_kq[0], 1);
+    mbar_init(&bar_kq[1], 1);
+    mbar_init(bar_v, 1);
     mbar_init(bar_mma, 1);
     fence_mbar_init();
   }
@@ -168,10 +173,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc::tmem_wait_st();
 
-  uint32_t tma_phase = 0, mma_phase = 0;
+  uint32_t mma_phase = 0;
   int ok = 1;
-  int pending_tma = 0, pending_mma = 0;
+  int pending_mma = 0;
+  // Loads in flight, for the drain on the error path: bit b = K/Q buffer b,
+  // bit 2 = V; kq_last[b] / v_last = the chunk last loaded there.
+  int pending_loads = 0;
+  int kq_last[2] = {-1, -1};
+  int v_last = -1;
   const int nchunks = (len + kC - 1) / kC;
+  auto issue_kq = [&](int chunk) {  // thread 0 only
+    uint8_t* buf = sm + ((chunk & 1) ? OFF_KQ2 : OFF_KQ);
+    const int t0 = start + chunk * kC;
+    mbar_arrive_expect_tx(&bar_kq[chunk & 1], 4 * 8192);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tc::tma_load_3d(buf + half * 16384, &tm_k, half * 64, kh, t0, &bar_kq[chunk & 1]);
+      tc::tma_load_3d(buf + half * 16384 + 8192, &tm_q, half * 64, kh, t0, &bar_kq[chunk & 1]);
+    }
+  };
+  auto issue_v = [&](int chunk) {  // thread 0 only
+    const int t0 = start + chunk * kC;
+    mbar_arrive_expect_tx(bar_v, 2 * 8192);
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+      tc::tma_load_3d(sm + OFF_V + half * 8192, &tm_v, half * 64, h, t0, bar_v);
+  };
+  // Gates of the next chunk are read from global memory a chunk ahead.
+  float g_next = 1.f, b_next = 0.f;
+  auto fetch_gates = [&](int chunk) {  // threads 0-63
+    const int n = min(kC, len - chunk * kC);
+    const bool on = tid < n;
+    const size_t at = (size_t)(start + chunk * kC + tid) * Hv + h;
+    g_next = on ? g[at] : 1.f;
+    b_next = on ? beta[at] : 0.f;
+  };
+  if (tid == 0) {
+    issue_kq(0);
+    issue_v(0);
+  }
+  pending_loads = 1 | 4;
+  kq_last[0] = 0;
+  v_last = 0;
+  if (tid < 64) fetch_gates(0);
   auto wait_mma = [&]() {
     const int done = mbar_wait_bounded(bar_mma, mma_phase, status) ? 1 : 0;
     if (done) mma_phase ^= 1;
@@ -186,22 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tok0 = start + c * kC;
     const int valid = min(kC, len - c * kC);
 
-    // ---- (1) chunk tiles by TMA; gates (log2 domain) on the CUDA cores meanwhile.
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_tma, 6 * 8192);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tc::tma_load_3d(sm + OFF_KQ + half * 16384, &tm_k, half * 64, kh, tok0, bar_tma);
-        tc::tma_load_3d(sm + OFF_KQ + half * 16384 + 8192, &tm_q, half * 64, kh, tok0, bar_tma);
-        tc::tma_load_3d(sm + OFF_V + half * 8192, &tm_v, half * 64, h, tok0, bar_tma);
-      }
-    }
-    pending_tma = 1;
+    const uint32_t off_kq = (c & 1) ? OFF_KQ2 : OFF_KQ;
+    // ---- (1) gates (log2 domain) from the values fetched a chunk ahead.
     if (tid < 64) {
-      const bool on = tid < valid;
-      const float gv = on ? g[(size_t)(tok0 + tid) * Hv + h] : 1.f;
-      s_beta[tid] = on ? beta[(size_t)(tok0 + tid) * Hv + h] : 0.f;
-      float lg = log2f(fminf(fmaxf(gv, 1e-6f), 1.f));
+      s_beta[tid] = b_next;
+      float lg = log2f(fminf(fmaxf(g_next, 1e-6f), 1.f));
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const float y = __shfl_up_sync(0xffffffffu, lg, off);
@@ -215,13 +248,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid < 64) {
       s_decay[tid] = exp2f(s_lg[tid]);
       s_r[tid] = exp2f(s_lg[63] - s_lg[tid]);
+      s_inv[tid] = exp2f(s_lg[0] - s_lg[tid]);
+      if (c + 1 < nchunks) fetch_gates(c + 1);
     }
     {
-      const int done = mbar_wait_bounded(bar_tma, tma_phase, status) ? 1 : 0;
-      if (done) tma_phase ^= 1;
+      const int done = mbar_wait_bounded(&bar_kq[c & 1], (c >> 1) & 1, status) ? 1 : 0;
       ok = __syncthreads_and(done && ok);
       if (!ok) break;
-      pending_tma = 0;
+      pending_loads &= ~(1 << (c & 1));
+    }
+    // The other K/Q buffer was last read by the previous chunk's GS, which has
+    // completed: fetch the next chunk's tiles into it now.
+    if (c + 1 < nchunks) {
+      if (tid == 0) issue_kq(c + 1);
+      pending_loads |= 1 << ((c + 1) & 1);
+      kq_last[(c + 1) & 1] = c + 1;
     }
 
     // ---- (2) G0: [K;Q] K^T -> TMEM cols T_KK (lanes 0-63 KK^T, 64-127 QK^T).
@@ -232,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          const uint32_t a = smem_addr(sm + OFF_KQ + kb * 16384) + ks * 32;
+          const uint32_t a = smem_addr(sm + off_kq + kb * 16384) + ks * 32;
           tc::mma_bf16(tmem + T_KK, tc::desc_kmajor(a), tc::desc_kmajor(a), id, (kb | ks) != 0);
         }
       tc::commit(bar_mma);
@@ -247,6 +288,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tmem_ld32(tmem + lane + T_KK + 32 * hf, v);
       const int t = row & 63;
       const float lgt = s_lg[t];
+      // R_tj = 2^(lg_t - lg_j). When the chunk's decay spans < 2^-100, write it
+      // as 2^(lg_t - lg_0) * 2^(lg_0 - lg_j): both factors stay in range and the
+      // per-element exponentials become one multiply.
+      const bool factor = s_lg[0] - s_lg[63] < 100.f;
+      const float at = exp2f(lgt - s_lg[0]);
+      float rr[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float lgj = s_lg[32 * hf + e];
+        rr[e] = factor ? at * s_inv[32 * hf + e] : exp2f(lgt - lgj);
+      }
       if (quarter < 2) {
         const float bt = s_beta[t];
         float4* arow = reinterpret_cast<float4*>(Xf + t * kAStride + 32 * hf);
@@ -256,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = 32 * hf + 4 * j4 + e;
-            a[e] = j < t ? bt * exp2f(lgt - s_lg[j]) * v[4 * j4 + e] : 0.f;
+            a[e] = j < t ? bt * rr[4 * j4 + e] * v[4 * j4 + e] : 0.f;
           }
           arow[j4] = make_float4(a[0], a[1], a[2], a[3]);
         }
@@ -264,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int j = 32 * hf + e;
-          v[e] = j <= t ? exp2f(lgt - s_lg[j]) * v[e] : 0.f;
+          v[e] = j <= t ? rr[e] * v[e] : 0.f;
         }
         store_chunks_hilo(sm + OFF_MH, sm + OFF_ML, t, 4 * hf, v);
       }
@@ -276,13 +328,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp < 4) {
       const int c16 = lane_id & 15;
       const float* Ab = Xf + (16 * warp) * kAStride + 16 * warp;
+      // Right-looking substitution: once x[k] is final it updates every later
+      // row, so the loads of column k do not wait on the x chain.
       float x[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        float acc = (r == c16) ? 1.f : 0.f;
+      for (int r = 0; r < 16; ++r) x[r] = (r == c16) ? 1.f : 0.f;
 #pragma unroll
-        for (int k = 0; k < r; ++k) acc = fmaf(-Ab[r * kAStride + k], x[k], acc);
-        x[r] = acc;
+      for (int k = 0; k < 15; ++k) {
+        float col[16];
+#pragma unroll
+        for (int r = k + 1; r < 16; ++r) col[r] = Ab[r * kAStride + k];
+#pragma unroll
+        for (int r = k + 1; r < 16; ++r) x[r] = fmaf(-col[r], x[k], x[r]);
       }
       __syncwarp();
       if (lane_id < 16) {
@@ -325,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = tid >> 3, c0 = (tid & 7) * 4;
       const float* Arow = Xf + (32 + r) * kAStride;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
+#pragma unroll
       for (int k = 0; k < 32; ++k) {
         const float a = Arow[k];
         const float4 xk = *reinterpret_cast<const float4*>(Xf + k * kAStride + c0);
@@ -338,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       const float* Drow = Xf + (32 + r) * kAStride + 32;
       float4 xo = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
+#pragma unroll
       for (int k = 0; k < 32; ++k) {
         const float d = Drow[k];
         const float4 tk = *reinterpret_cast<const float4*>(Tbuf + k * 32 + c0);
@@ -429,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint32_t a = smem_addr(sm + (part ? OFF_SL : OFF_SH) + kb * 16384) + ks * 32;
-            const uint32_t bb = smem_addr(sm + OFF_KQ + kb * 16384) + ks * 32;
+            const uint32_t bb = smem_addr(sm + off_kq + kb * 16384) + ks * 32;
             tc::mma_bf16(tmem + T_P, tc::desc_kmajor(a), tc::desc_kmajor(bb), id,
                          (part | kb | ks) != 0);
           }
@@ -440,6 +497,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- (8) W^T row i for tokens [32 hf, +32); zero those U^T columns;
     //          decay * P2^T in the matching O^T columns.
+    {
+      const int done = mbar_wait_bounded(bar_v, c & 1, status) ? 1 : 0;
+      ok = __syncthreads_and(done && ok);
+      if (!ok) break;
+      pending_loads &= ~4;
+    }
     {
       float p[32];
       tc::tmem_ld32(tmem + lane + T_P + 32 * hf, p);
@@ -465,6 +528,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     tc::fence_before();
     __syncthreads();
+    if (c + 1 < nchunks) {  // every thread has read this chunk's V
+      if (tid == 0) issue_v(c + 1);
+      pending_loads |= 4;
+      v_last = c + 1;
+    }
 
     // ---- (9) G34: W^T [X;Y]^T accumulated -> U^T | O^T.
     if (tid == 0) {
@@ -508,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id = tc::idesc_bf16(128, 128, false, true);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        const uint64_t kd = tc::desc_mnmajor(smem_addr(sm + OFF_KQ) + ks * 2048, 16384);
+        const uint64_t kd = tc::desc_mnmajor(smem_addr(sm + off_kq) + ks * 2048, 16384);
         tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WH) + ks * 32), kd, id, true);
         tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WL) + ks * 32), kd, id, true);
       }
@@ -521,7 +589,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!ok) {
     // A bounded wait gave up (already flagged): let this CTA's own copies and
     // MMAs in flight finish, within limits, before the TMEM is released.
-    if (pending_tma) mbar_wait_bounded(bar_tma, tma_phase, status);
+    if (tid == 0) {
+      for (int b2 = 0; b2 < 2; ++b2)
+        if ((pending_loads & (1 << b2)) && kq_last[b2] >= 0)
+          mbar_wait_bounded(&bar_kq[b2], (kq_last[b2] >> 1) & 1, status);
+      if ((pending_loads & 4) && v_last >= 0) mbar_wait_bounded(bar_v, v_last & 1, status);
+    }
     if (pending_mma) mbar_wait_bounded(bar_mma, mma_phase, status);
   } else {
 #pragma unroll 1
