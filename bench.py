@@ -71,6 +71,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-config1", action="store_true",
                     help="skip the config-1 chunked-prefill measurement")
+    ap.add_argument("--config", type=int, choices=(3, 4), default=3,
+                    help="3: ragged batch decode step (default); 4: one long sequence with its "
+                         "KV pages split across the GPUs")
+    ap.add_argument("--ctx4", type=int, default=131_072, help="config-4 context length")
     return ap.parse_args()
 
 
@@ -591,6 +595,121 @@ def cpu_baseline(args, wl):
                       f"float64/fp32 NumPy oracle, {threads} threads"}
 
 
+def run_config4(args, world, rank, local):
+    """Config 4: one sequence of --ctx4 tokens; its KV pages are split evenly across the
+    ranks (contiguous ranges), the GDN state (32 heads) is updated on every rank, and each
+    attention layer all-gathers the per-rank (out, lse) partials over NCCL."""
+    import torch
+    import torch.distributed as dist
+
+    from shellsmith_b200 import _build, _capi, numerics, paged
+    from shellsmith_b200.longctx import ShardedSequence
+    from shellsmith_b200.workloads import gdn_token_inputs_device
+
+    _build.build()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    L, n_attn = 48, 12
+    hq, hkv, d = 16, 2, 256
+    shard = ShardedSequence(args.ctx4, rank, world, attention_layers=n_attn, kv_heads=hkv,
+                            head_dim=d, q_heads=hq, headroom_pages=8, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4)
+    block = torch.randn(1 << 26, generator=gen, device=device).to(torch.bfloat16)
+    flat = shard.kv.view(-1)
+    for start in range(0, flat.numel(), block.numel()):
+        part = flat[start:start + block.numel()]
+        part.copy_(block[:part.numel()])
+    del block
+    state = torch.zeros((36, 1, 32, 128, 128), dtype=torch.float32, device=device)
+    gdn_in = [gdn_token_inputs_device(gen, 1, 16, 32, 128, 128, device=device) for _ in range(36)]
+    gdn_out = torch.empty((1, 32, 128), dtype=torch.bfloat16, device=device)
+    attn_in = [(torch.randn((1, hq, d), generator=gen, device=device).to(torch.bfloat16),
+                torch.randn((1, hkv, d), generator=gen, device=device).to(torch.bfloat16),
+                torch.randn((1, hkv, d), generator=gen, device=device).to(torch.bfloat16))
+               for _ in range(n_attn)]
+    gather = None
+    if world == 1:
+        def gather(dst, src):
+            dst[0].copy_(src)
+    stream = torch.cuda.current_stream(device)
+
+    def layers():
+        g_i = a_i = 0
+        for layer in range(L):
+            if layer % 4 == 3:
+                q, k, v = attn_in[a_i]
+                shard.attention(a_i, q, k, v, 1 / 16, all_gather=gather)
+                a_i += 1
+            else:
+                numerics.gdn_decode(*gdn_in[g_i], state[g_i], out=gdn_out)
+                g_i += 1
+
+    for _ in range(args.warmup):
+        shard.begin_token()
+        layers()
+    torch.cuda.synchronize()
+    # The step is launch-bound (~100 small kernels for ~0.5 ms of HBM time at
+    # 1 GPU): capture the 48 layers, all-gathers included, in one CUDA graph.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layers()
+    torch.cuda.synchronize()
+    def step():
+        shard.begin_token()
+        graph.replay()
+
+    step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    local_ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(local_ms, world)
+    # The exchange alone: the all-gather of one layer's packed partial.
+    ag_ms = None
+    if world > 1:
+        for _ in range(5):
+            dist.all_gather_into_tensor(shard.gathered, shard.packed)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(50):
+            dist.all_gather_into_tensor(shard.gathered, shard.packed)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ag_ms = max_over_ranks(a0.elapsed_time(a1) / 50, world)
+    _capi.check_device()
+    del graph  # release the graph (it holds NCCL work) before the process group goes
+    bytes_rank = n_attn * (shard.local_tokens * hkv * d * 2 * 2) + 36 * 4210944
+    bytes_all = sum_over_ranks(float(bytes_rank), world)
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    per_step = ms / 1e3 / args.steps
+    line = {
+        "metric": "config4 long-context decode tokens/sec (one 128k sequence, KV sharded)",
+        "value": round(1 / per_step, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 kv / fp32 gdn state", "data": "synthetic",
+        "config": {"workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN "
+                               f"replicated + 12 attention with KV pages split over {world} GPU)",
+                   "parallelism": f"KV-page sharding x{world}, NCCL all-gather of (out, lse)"},
+        "hbm": {"bytes_per_step_all_ranks": bytes_all,
+                "gbs_per_gpu": round(bytes_all / world / per_step / 1e9, 1),
+                "frac_per_gpu": round(bytes_all / world / per_step / 1e9 / peaks["hbm_gbs"], 4)},
+        "all_gather_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
+        "all_gather_bytes_per_rank": hq * (d + 1) * 4,
+    }
+    print(json.dumps(line), flush=True)
+    return line
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's CPU math (oracle port) on the host cores."""
     if rank != 0:
@@ -636,6 +755,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.config == 4:
+            run_config4(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -184,6 +184,26 @@ int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
                               float* part_out, float* part_lse, sc_bf16* out,
                               float* lse_out, void* stream);
 
+/* The same attention, writing each row's normalised fp32 output and its lse
+ * packed as packed[B * Hq][D + 1] (lse at index D): the per-device partial of
+ * a sequence whose KV pages are split across GPUs. Gather the parts of every
+ * device into [nparts][rows][D + 1] and merge them with
+ * sc_attention_combine_packed. No reference counterpart (the reference runs
+ * one device). */
+int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16* kv_pool,
+                                     int64_t num_pages, const int32_t* block_table,
+                                     const int32_t* ctx_len, int B, int Hq, int Hkv,
+                                     int D, int P, int max_pages, int pages_per_split,
+                                     int num_splits, float scale, float* part_out,
+                                     float* part_lse, float* packed, void* stream);
+
+/* Merges gathered packed parts [nparts][rows][D + 1] (as written by
+ * sc_paged_decode_attention_packed on each device) into out [rows, D] bf16
+ * and lse_out [rows] fp32 (or NULL). Parts with lse = -inf are ignored.
+ * D <= 512. */
+int sc_attention_combine_packed(const float* gathered, int nparts, int rows, int D,
+                                sc_bf16* out, float* lse_out, void* stream);
+
 /* Split-K decode attention that allocates nothing and takes no scratch.
  *
  * No counterpart in the reference: it exists for callers of this library
@@ -221,7 +241,7 @@ int sc_paged_decode_attention_noalloc(const sc_bf16* q, const sc_bf16* kv_pool,
  * over s < nparts (rows r = 0..rows-1, parts with lse = -inf ignored).
  * part_out [rows, nparts, D] fp32, part_lse [rows, nparts] fp32,
  * out [rows, D] bf16, lse_out [rows] fp32 or NULL.
- * This is the cross-GPU combine of a KV-sharded long sequence. */
+ * This is the cross-GPU combine of a KV-sharded long sequence. D <= 512. */
 int sc_attention_combine(const float* part_out, const float* part_lse,
                          int rows, int nparts, int D, sc_bf16* out,
                          float* lse_out, void* stream);

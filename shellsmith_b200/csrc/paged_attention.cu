@@ -48,7 +48,8 @@ __global__ void __launch_bounds__(NW * 32)
                         int max_pages, int pages_per_split, int num_splits, float scale_log2,
                         float* __restrict__ part_out, float* __restrict__ part_lse,
                         uint16_t* __restrict__ out, float* __restrict__ lse_out,
-                        long long num_pages, unsigned int* status) {
+                        float* __restrict__ packed, long long num_pages,
+                        unsigned int* status) {
   using S = AttnShape<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NW * NSTAGE * S::STAGE_BYTES);
@@ -68,7 +69,10 @@ __global__ void __launch_bounds__(NW * 32)
     for (int idx = threadIdx.x; idx < min(kHeadsPerTile, G - hg * kHeadsPerTile) * D;
          idx += blockDim.x) {
       const size_t row = (size_t)b * Hq + kvh * G + hg * kHeadsPerTile + idx / D;
-      if (num_splits == 1) {
+      if (num_splits == 1 && packed != nullptr) {
+        packed[row * (D + 1) + idx % D] = 0.f;
+        if (idx % D == 0) packed[row * (D + 1) + D] = -CUDART_INF_F;
+      } else if (num_splits == 1) {
         out[row * D + idx % D] = 0;
         if (idx % D == 0 && lse_out != nullptr) lse_out[row] = -CUDART_INF_F;
       }
@@ -257,7 +261,10 @@ __global__ void __launch_bounds__(NW * 32)
     const float val = acc / lsum;
     const float lse = (M + log2f(lsum)) * kLn2;
     const size_t row = (size_t)b * Hq + head0 + n;
-    if (num_splits == 1) {
+    if (num_splits == 1 && packed != nullptr) {
+      packed[row * (D + 1) + d] = val;
+      if (d == 0) packed[row * (D + 1) + D] = lse;
+    } else if (num_splits == 1) {
       out[row * D + d] = f_to_bf16(val);
       if (d == 0 && lse_out != nullptr) lse_out[row] = lse;
     } else {
@@ -267,35 +274,190 @@ __global__ void __launch_bounds__(NW * 32)
   }
 }
 
-// One CTA per output row: merges the split partials of that row.
-// With ctx_len != NULL only the splits the decode kernel wrote are read.
-__global__ void combine_kernel(const float* __restrict__ part_out,
-                               const float* __restrict__ part_lse,
-                               const int32_t* __restrict__ ctx_len, int Hq, int nparts,
-                               int pages_per_split, int D, uint16_t* __restrict__ out,
-                               float* __restrict__ lse_out) {
+// One CTA per output row: merges the partials of that row.
+// Part s of row r: value d at po[r * o_row + s * o_part + d], lse at
+// pl[r * l_row + s * l_part]. With ctx_len != NULL only the splits the decode
+// kernel wrote are read. Output: bf16 out[r][d] (+ lse_out[r]), or, when
+// `packed` is set, fp32 packed[r][0..D) with the lse at packed[r][D].
+// Each part's weight e^(lse_s - M) is computed once into shared memory (in
+// windows of kCombineWindow parts, rescaled as the running maximum grows).
+constexpr int kCombineThreads = 128;
+constexpr int kCombineWindow = 1024;
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+  for (int w = 1; w < kCombineThreads / 32; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < kCombineThreads / 32; ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kCombineThreads)
+    combine_kernel(const float* __restrict__ po, const float* __restrict__ pl, size_t o_row,
+                   size_t o_part, size_t l_row, size_t l_part,
+                   const int32_t* __restrict__ ctx_len, int Hq, int nparts, int pages_per_split,
+                   int D, uint16_t* __restrict__ out, float* __restrict__ lse_out,
+                   float* __restrict__ packed) {
+  __shared__ float w[kCombineWindow];
+  __shared__ float red[kCombineThreads / 32];
   const int row = blockIdx.x;
   int ns = nparts;
   if (ctx_len != nullptr) {
     const int npages = (ctx_len[row / Hq] + kPage - 1) / kPage;
     ns = min(nparts, (npages + pages_per_split - 1) / pages_per_split);
   }
-  const float* lse = part_lse + (size_t)row * nparts;
-  float M = -CUDART_INF_F;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, lse[s]);
-  float wsum = 0.f;
-  if (M != -CUDART_INF_F)
-    for (int s = 0; s < ns; ++s) wsum += lse[s] == -CUDART_INF_F ? 0.f : __expf(lse[s] - M);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.f;
-    if (M != -CUDART_INF_F)
-      for (int s = 0; s < ns; ++s)
-        if (lse[s] != -CUDART_INF_F)
-          acc = fmaf(__expf(lse[s] - M), part_out[((size_t)row * nparts + s) * D + d], acc);
-    out[(size_t)row * D + d] = f_to_bf16(M == -CUDART_INF_F ? 0.f : acc / wsum);
+  const float* lse = pl + (size_t)row * l_row;
+  const float* o = po + (size_t)row * o_row;
+  constexpr int kDims = 4;  // dims per thread (D <= 512)
+  float acc[kDims];
+#pragma unroll
+  for (int j = 0; j < kDims; ++j) acc[j] = 0.f;
+  float M = -CUDART_INF_F, wsum = 0.f;
+  for (int s0 = 0; s0 < ns; s0 += kCombineWindow) {
+    const int n = min(kCombineWindow, ns - s0);
+    float m = -CUDART_INF_F;
+    for (int s = threadIdx.x; s < n; s += kCombineThreads) m = fmaxf(m, lse[(s0 + s) * l_part]);
+    const float Mn = fmaxf(M, block_max(m, red));
+    if (Mn == -CUDART_INF_F) continue;  // every part so far is empty
+    float part = 0.f;
+    for (int s = threadIdx.x; s < n; s += kCombineThreads) {
+      const float ls = lse[(s0 + s) * l_part];
+      const float e = ls == -CUDART_INF_F ? 0.f : __expf(ls - Mn);
+      w[s] = e;
+      part += e;
+    }
+    const float rescale = M == -CUDART_INF_F ? 0.f : __expf(M - Mn);
+    wsum = wsum * rescale + block_sum(part, red);  // block_sum syncs: w[] is visible
+    M = Mn;
+#pragma unroll
+    for (int j = 0; j < kDims; ++j) {
+      const int d = threadIdx.x + j * kCombineThreads;
+      if (d < D) {
+        float a = acc[j] * rescale;
+        for (int s = 0; s < n; ++s) a = fmaf(w[s], o[(size_t)(s0 + s) * o_part + d], a);
+        acc[j] = a;
+      }
+    }
+    __syncthreads();  // w[] is rewritten by the next window
   }
-  if (threadIdx.x == 0 && lse_out != nullptr)
-    lse_out[row] = M == -CUDART_INF_F ? -CUDART_INF_F : M + logf(wsum);
+  const bool empty = M == -CUDART_INF_F;
+#pragma unroll
+  for (int j = 0; j < kDims; ++j) {
+    const int d = threadIdx.x + j * kCombineThreads;
+    if (d < D) {
+      const float val = empty ? 0.f : acc[j] / wsum;
+      if (packed != nullptr)
+        packed[(size_t)row * (D + 1) + d] = val;
+      else
+        out[(size_t)row * D + d] = f_to_bf16(val);
+    }
+  }
+  if (threadIdx.x == 0) {
+    const float l = empty ? -CUDART_INF_F : M + logf(wsum);
+    if (packed != nullptr)
+      packed[(size_t)row * (D + 1) + D] = l;
+    else if (lse_out != nullptr)
+      lse_out[row] = l;
+  }
+}
+
+// The same merge for rows with many parts (a long sequence cut into many
+// splits, or many devices): one CTA per (row, 32-dim tile), lane = dim, and
+// the four warps take every fourth part, so each part's 128-byte slice is one
+// coalesced load and the row's work spreads over D / 32 CTAs.
+__global__ void __launch_bounds__(kCombineThreads)
+    combine_tiled_kernel(const float* __restrict__ po, const float* __restrict__ pl,
+                         size_t o_row, size_t o_part, size_t l_row, size_t l_part,
+                         const int32_t* __restrict__ ctx_len, int Hq, int nparts,
+                         int pages_per_split, int D, uint16_t* __restrict__ out,
+                         float* __restrict__ lse_out, float* __restrict__ packed) {
+  __shared__ float w[kCombineWindow];
+  __shared__ float red[kCombineThreads / 32];
+  __shared__ float part_acc[kCombineThreads / 32][32];
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int d = blockIdx.y * 32 + lane;
+  int ns = nparts;
+  if (ctx_len != nullptr) {
+    const int npages = (ctx_len[row / Hq] + kPage - 1) / kPage;
+    ns = min(nparts, (npages + pages_per_split - 1) / pages_per_split);
+  }
+  const float* lse = pl + (size_t)row * l_row;
+  const float* o = po + (size_t)row * o_row;
+  float acc = 0.f, M = -CUDART_INF_F, wsum = 0.f;
+  for (int s0 = 0; s0 < ns; s0 += kCombineWindow) {
+    const int n = min(kCombineWindow, ns - s0);
+    float m = -CUDART_INF_F;
+    for (int s = threadIdx.x; s < n; s += kCombineThreads) m = fmaxf(m, lse[(s0 + s) * l_part]);
+    const float Mn = fmaxf(M, block_max(m, red));
+    if (Mn == -CUDART_INF_F) continue;
+    float part = 0.f;
+    for (int s = threadIdx.x; s < n; s += kCombineThreads) {
+      const float ls = lse[(s0 + s) * l_part];
+      const float e = ls == -CUDART_INF_F ? 0.f : __expf(ls - Mn);
+      w[s] = e;
+      part += e;
+    }
+    const float rescale = M == -CUDART_INF_F ? 0.f : __expf(M - Mn);
+    wsum = wsum * rescale + block_sum(part, red);
+    M = Mn;
+    float a = acc * rescale;
+    if (d < D)
+      for (int s = warp; s < n; s += kCombineThreads / 32)
+        a = fmaf(w[s], o[(size_t)(s0 + s) * o_part + d], a);
+    acc = a;
+    __syncthreads();
+  }
+  part_acc[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && d < D) {
+    float total = 0.f;
+#pragma unroll
+    for (int k = 0; k < kCombineThreads / 32; ++k) total += part_acc[k][lane];
+    const bool empty = M == -CUDART_INF_F;
+    const float val = empty ? 0.f : total / wsum;
+    if (packed != nullptr)
+      packed[(size_t)row * (D + 1) + d] = val;
+    else
+      out[(size_t)row * D + d] = f_to_bf16(val);
+    if (blockIdx.y == 0 && lane == 0) {
+      const float l = empty ? -CUDART_INF_F : M + logf(wsum);
+      if (packed != nullptr)
+        packed[(size_t)row * (D + 1) + D] = l;
+      else if (lse_out != nullptr)
+        lse_out[row] = l;
+    }
+  }
+}
+
+// Launches the merge of `rows` rows of `nparts` parts: per-row CTAs for few
+// parts, (row, dim-tile) CTAs for many.
+void launch_combine(const float* po, const float* pl, size_t o_row, size_t o_part, size_t l_row,
+                    size_t l_part, const int32_t* ctx_len, int Hq, int nparts,
+                    int pages_per_split, int D, int rows, uint16_t* out, float* lse_out,
+                    float* packed, cudaStream_t s) {
+  if (nparts >= 16) {
+    dim3 grid(rows, (D + 31) / 32);
+    combine_tiled_kernel<<<grid, kCombineThreads, 0, s>>>(po, pl, o_row, o_part, l_row, l_part,
+                                                          ctx_len, Hq, nparts, pages_per_split,
+                                                          D, out, lse_out, packed);
+  } else {
+    combine_kernel<<<rows, kCombineThreads, 0, s>>>(po, pl, o_row, o_part, l_row, l_part,
+                                                    ctx_len, Hq, nparts, pages_per_split, D, out,
+                                                    lse_out, packed);
+  }
 }
 
 // Launch shape: warps per CTA and shared-memory stages (one page each) per warp.
@@ -312,8 +474,8 @@ template <int D>
 int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* block_table,
                   const int32_t* ctx_len, int B, int Hq, int Hkv, int max_pages,
                   int pages_per_split, int num_splits, float scale, float* part_out,
-                  float* part_lse, uint16_t* out, float* lse_out, long long num_pages,
-                  cudaStream_t s) {
+                  float* part_lse, uint16_t* out, float* lse_out, float* packed,
+                  long long num_pages, cudaStream_t s) {
   using S = AttnShape<D>;
   constexpr int NW = kWarpsPerCta, NST = kStages;
   const size_t smem = (size_t)NW * NST * S::STAGE_BYTES + NW * NST * sizeof(uint64_t);
@@ -335,11 +497,11 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
   dim3 grid(num_splits, Hkv * HG, B);
   kernel<<<grid, NW * 32, smem, s>>>(q, kv_pool, block_table, ctx_len, Hq, Hkv, G, HG, max_pages,
                                      pages_per_split, num_splits, scale_log2, part_out, part_lse,
-                                     out, lse_out, num_pages, device_status_word());
+                                     out, lse_out, packed, num_pages, device_status_word());
   if (int rc = check_launch("sc_paged_decode_attention")) return rc;
   if (num_splits > 1) {
-    combine_kernel<<<B * Hq, 128, 0, s>>>(part_out, part_lse, ctx_len, Hq, num_splits,
-                                         pages_per_split, D, out, lse_out);
+    launch_combine(part_out, part_lse, (size_t)num_splits * D, D, num_splits, 1, ctx_len, Hq,
+                   num_splits, pages_per_split, D, B * Hq, out, lse_out, packed, s);
     return check_launch("sc_paged_decode_attention(combine)");
   }
   return SC_OK;
@@ -348,16 +510,15 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
 }  // namespace
 }  // namespace sc
 
-extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
-                                         int64_t num_pages, const int32_t* block_table,
-                                         const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
-                                         int P, int max_pages, int pages_per_split,
-                                         int num_splits, float scale,
-                                         float* part_out, float* part_lse, sc_bf16* out,
-                                         float* lse_out, void* stream) {
-  const char* name = "sc_paged_decode_attention";
-  SC_REQUIRE(q && kv_pool && block_table && ctx_len && out, SC_ERR_INVALID, "%s: null pointer",
-             name);
+namespace sc {
+namespace {
+int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int64_t num_pages,
+                 const int32_t* block_table, const int32_t* ctx_len, int B, int Hq, int Hkv,
+                 int D, int P, int max_pages, int pages_per_split, int num_splits, float scale,
+                 float* part_out, float* part_lse, sc_bf16* out, float* lse_out, float* packed,
+                 void* stream) {
+  SC_REQUIRE(q && kv_pool && block_table && ctx_len && (out || packed), SC_ERR_INVALID,
+             "%s: null pointer", name);
   SC_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, SC_ERR_INVALID,
              "%s: bad heads Hq=%d Hkv=%d", name, Hq, Hkv);
   SC_REQUIRE(P == sc::kPage, SC_ERR_UNSUPPORTED, "%s: page size %d != 16", name, P);
@@ -373,20 +534,63 @@ extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_poo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (D) {
     case 64:
-      return sc::launch_decode<64>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+      return launch_decode<64>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
                                    pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                   lse_out, num_pages, s);
+                                   lse_out, packed, num_pages, s);
     case 128:
-      return sc::launch_decode<128>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+      return launch_decode<128>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                    lse_out, num_pages, s);
+                                    lse_out, packed, num_pages, s);
     case 256:
-      return sc::launch_decode<256>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+      return launch_decode<256>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                    lse_out, num_pages, s);
+                                    lse_out, packed, num_pages, s);
     default:
-      return sc::set_error(SC_ERR_UNSUPPORTED, "%s: D=%d not in {64,128,256}", name, D);
+      return set_error(SC_ERR_UNSUPPORTED, "%s: D=%d not in {64,128,256}", name, D);
   }
+}
+}  // namespace
+}  // namespace sc
+
+extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
+                                         int64_t num_pages, const int32_t* block_table,
+                                         const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
+                                         int P, int max_pages, int pages_per_split,
+                                         int num_splits, float scale,
+                                         float* part_out, float* part_lse, sc_bf16* out,
+                                         float* lse_out, void* stream) {
+  SC_REQUIRE(out != nullptr, SC_ERR_INVALID, "sc_paged_decode_attention: null pointer");
+  return sc::decode_entry("sc_paged_decode_attention", q, kv_pool, num_pages, block_table,
+                          ctx_len, B, Hq, Hkv, D, P, max_pages, pages_per_split, num_splits,
+                          scale, part_out, part_lse, out, lse_out, nullptr, stream);
+}
+
+extern "C" int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16* kv_pool,
+                                                int64_t num_pages, const int32_t* block_table,
+                                                const int32_t* ctx_len, int B, int Hq, int Hkv,
+                                                int D, int P, int max_pages,
+                                                int pages_per_split, int num_splits, float scale,
+                                                float* part_out, float* part_lse, float* packed,
+                                                void* stream) {
+  SC_REQUIRE(packed != nullptr, SC_ERR_INVALID, "sc_paged_decode_attention_packed: null pointer");
+  return sc::decode_entry("sc_paged_decode_attention_packed", q, kv_pool, num_pages,
+                          block_table, ctx_len, B, Hq, Hkv, D, P, max_pages, pages_per_split,
+                          num_splits, scale, part_out, part_lse, nullptr, nullptr, packed,
+                          stream);
+}
+
+extern "C" int sc_attention_combine_packed(const float* gathered, int nparts, int rows, int D,
+                                           sc_bf16* out, float* lse_out, void* stream) {
+  const char* name = "sc_attention_combine_packed";
+  SC_REQUIRE(gathered && out, SC_ERR_INVALID, "%s: null pointer", name);
+  SC_REQUIRE(rows >= 0 && nparts > 0 && D > 0 && D <= 512, SC_ERR_INVALID,
+             "%s: rows=%d nparts=%d D=%d (D <= 512)", name, rows, nparts, D);
+  if (rows == 0) return SC_OK;
+  const size_t stride = (size_t)D + 1;
+  sc::launch_combine(gathered, gathered + D, stride, (size_t)rows * stride, stride,
+                     (size_t)rows * stride, nullptr, 1, nparts, 1, D, rows, out, lse_out, nullptr,
+                     static_cast<cudaStream_t>(stream));
+  return sc::check_launch(name);
 }
 
 extern "C" int sc_attention_combine(const float* part_out, const float* part_lse, int rows,
@@ -394,11 +598,11 @@ extern "C" int sc_attention_combine(const float* part_out, const float* part_lse
                                     void* stream) {
   const char* name = "sc_attention_combine";
   SC_REQUIRE(part_out && part_lse && out, SC_ERR_INVALID, "%s: null pointer", name);
-  SC_REQUIRE(rows >= 0 && nparts > 0 && D > 0, SC_ERR_INVALID, "%s: rows=%d nparts=%d D=%d", name,
-             rows, nparts, D);
+  SC_REQUIRE(rows >= 0 && nparts > 0 && D > 0 && D <= 512, SC_ERR_INVALID,
+             "%s: rows=%d nparts=%d D=%d (D <= 512)", name, rows, nparts, D);
   if (rows == 0) return SC_OK;
-  sc::combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      part_out, part_lse, nullptr, 1, nparts, 1, D, out, lse_out);
+  sc::launch_combine(part_out, part_lse, (size_t)nparts * D, D, nparts, 1, nullptr, 1, nparts, 1,
+                     D, rows, out, lse_out, nullptr, static_cast<cudaStream_t>(stream));
   return sc::check_launch(name);
 }
 

@@ -93,15 +93,16 @@ def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
     """(pages_per_split, num_splits) for a batch whose longest sequence has that many pages.
 
     Without an explicit size, a split is the largest power of two of pages,
-    at most 256 (4 MiB of K/V per kv head at D = 256), that still leaves at
-    least 4 CTAs per SM for `total_work` = sum over sequences of pages x kv
-    heads x head groups. Large splits keep the partials and their combine
-    small; the floor keeps a single long sequence spread over every SM.
+    at most 256 (4 MiB of K/V per kv head at D = 256), that still gives at
+    least two waves of CTAs (one CTA per SM) for `total_work` = sum over
+    sequences of pages x kv heads x head groups. Large splits keep the
+    partials and their combine small; the floor keeps a single long sequence
+    spread over every SM.
     """
     if pages_per_split:
         pps = pages_per_split
     elif total_work:
-        target = max(1, total_work // (4 * sms))
+        target = max(1, total_work // (2 * sms))
         pps = 16
         while pps * 2 <= min(256, target):
             pps *= 2
@@ -191,4 +192,54 @@ def attention_combine(part_out: torch.Tensor, part_lse: torch.Tensor,
         lse_out = torch.empty((rows,), dtype=torch.float32, device=part_out.device)
     _capi.call("sc_attention_combine", ptr(part_out), ptr(part_lse), rows, nparts, dim, ptr(out),
                ptr(lse_out), stream_of(part_out))
+    return out, lse_out
+
+
+def paged_decode_attention_packed(q: torch.Tensor, kv_pool: torch.Tensor,
+                                  block_table: torch.Tensor, ctx_len: torch.Tensor, scale: float,
+                                  *, packed: torch.Tensor | None = None,
+                                  max_pages_in_batch: int | None = None,
+                                  pages_per_split: int | None = None,
+                                  total_pages: int | None = None,
+                                  workspace: AttentionWorkspace | None = None) -> torch.Tensor:
+    """Like paged_decode_attention, but returns fp32 packed [B * Hq, D + 1]: each row's
+    normalised output and, at index D, its natural-log lse (a device's partial)."""
+    num_pages, hkv, page, dim = _pool_dims(kv_pool)
+    require_cuda("q", q, torch.bfloat16, 3)
+    require_cuda("block_table", block_table, torch.int32, 2, align=4)
+    require_cuda("ctx_len", ctx_len, torch.int32, 1, align=4)
+    B, hq, d = q.shape
+    if d != dim or hq % hkv or block_table.shape[0] != B or ctx_len.shape[0] != B:
+        raise ValueError("paged_decode_attention_packed: inconsistent shapes")
+    max_pages = block_table.shape[1]
+    groups = hkv * ((hq // hkv + 7) // 8)
+    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
+                             None if total_pages is None else total_pages * groups,
+                             sm_count(q.device))
+    if packed is None:
+        packed = torch.empty((B * hq, dim + 1), dtype=torch.float32, device=q.device)
+    require_cuda("packed", packed, torch.float32, 2, align=4)
+    part_out = part_lse = None
+    if nsplit > 1:
+        if workspace is None or not workspace.fits(B, hq, dim, nsplit):
+            workspace = AttentionWorkspace(B, hq, dim, nsplit, device=q.device)
+        part_out, part_lse = workspace.views(B, nsplit)
+    _capi.call("sc_paged_decode_attention_packed", ptr(q), ptr(kv_pool), num_pages,
+               ptr(block_table), ptr(ctx_len), B, hq, hkv, dim, page, max_pages, pps, nsplit,
+               float(scale), ptr(part_out), ptr(part_lse), ptr(packed), stream_of(q))
+    return packed
+
+
+def attention_combine_packed(gathered: torch.Tensor, out: torch.Tensor | None = None,
+                             lse_out: torch.Tensor | None = None) -> tuple:
+    """Merge gathered packed parts [nparts, rows, D + 1] -> (out [rows, D] bf16, lse [rows])."""
+    require_cuda("gathered", gathered, torch.float32, 3, align=4)
+    nparts, rows, width = gathered.shape
+    dim = width - 1
+    if out is None:
+        out = torch.empty((rows, dim), dtype=torch.bfloat16, device=gathered.device)
+    if lse_out is None:
+        lse_out = torch.empty((rows,), dtype=torch.float32, device=gathered.device)
+    _capi.call("sc_attention_combine_packed", ptr(gathered), nparts, rows, dim, ptr(out),
+               ptr(lse_out), stream_of(gathered))
     return out, lse_out

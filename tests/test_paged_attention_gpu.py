@@ -127,9 +127,11 @@ def test_empty_sequence_gives_zero(cuda):
         assert torch.count_nonzero(out[0]) == 0 and torch.isfinite(out[1].float()).all()
 
 
-def test_combine_matches_oracle(cuda):
-    rng = np.random.default_rng(11)
-    rows, parts, D = 7, 5, 256
+@pytest.mark.parametrize("parts", [5, 40, 1500])
+def test_combine_matches_oracle(cuda, parts):
+    """Few parts (per-row kernel), many parts (tiled kernel), > 1024 parts (windows)."""
+    rng = np.random.default_rng(11 + parts)
+    rows, D = 7, 256
     po = rng.standard_normal((rows, parts, D)).astype(np.float32)
     pl = (rng.standard_normal((rows, parts)) * 3).astype(np.float32)
     pl[2, 1] = -np.inf
