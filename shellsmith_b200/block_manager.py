@@ -10,6 +10,9 @@ placement (which page, which slot) is this build's own, deterministic:
 
   * pages come from a LIFO free list seeded with a permutation of the pool
     (seeded RNG), and a release pushes the pages back in reverse order;
+  * a page has a reference count: prefix snapshots and forked sequences share
+    full pages, and a page returns to the free list when its last owner
+    drops it;
   * state slots come from a LIFO list of [0, max_seqs); a sequence's slot is
     also its batch row, its block-table row and its GDN state row;
   * a sequence of n tokens holds ceil(n / P) pages; the token at position t
@@ -43,6 +46,7 @@ class BlockManager:
         self._free_pages = [int(p) for p in order[::-1]]
         self._free_slots = list(range(max_seqs - 1, -1, -1))
         self.table = np.zeros((max_seqs, max_pages_per_seq), np.int32)
+        self.refcount = np.zeros(num_pages, np.int32)
         self.lengths = np.zeros(max_seqs, np.int64)
         self.active = np.zeros(max_seqs, bool)
         self.pages: dict[int, list] = {}
@@ -81,7 +85,7 @@ class BlockManager:
         if need > len(self._free_pages):
             raise OutOfPages(f"{need} pages needed, {len(self._free_pages)} free")
         slot = self._free_slots.pop()
-        pages = [self._free_pages.pop() for _ in range(need)]
+        pages = self.take_pages(need)
         self.pages[slot] = pages
         self.owner[slot] = owner
         self.table[slot, :need] = pages
@@ -115,7 +119,7 @@ class BlockManager:
         for i, (slot, length, new_page) in enumerate(zip(slots.tolist(), lengths.tolist(),
                                                          needs_page.tolist())):
             if new_page:
-                page = self._free_pages.pop()
+                page = self.take_pages(1)[0]
                 self.pages[slot].append(page)
                 self.table[slot, length // self.page_size] = page
                 self.dirty_rows.add(slot)
@@ -124,10 +128,65 @@ class BlockManager:
         self.lengths[slots] = lengths + 1
         return out
 
+    # ------------------------------------------------------------ shared pages
+    def take_pages(self, n: int) -> list:
+        """Pop n free pages (LIFO), each with reference count 1."""
+        if n > len(self._free_pages):
+            raise OutOfPages(f"{n} pages needed, {len(self._free_pages)} free")
+        pages = [self._free_pages.pop() for _ in range(n)]
+        self.refcount[pages] = 1
+        return pages
+
+    def share(self, pages) -> None:
+        """One more owner (a prefix snapshot or a forked sequence) for each page."""
+        for p in pages:
+            self.refcount[p] += 1
+
+    def drop(self, pages) -> None:
+        """One owner fewer; pages nobody owns go back to the free list (reverse order)."""
+        for p in reversed(list(pages)):
+            self.refcount[p] -= 1
+            if self.refcount[p] == 0:
+                self._free_pages.append(int(p))
+            elif self.refcount[p] < 0:
+                raise RuntimeError(f"page {p} released more often than it was owned")
+
+    def adopt(self, owner, pages: list, tokens: int) -> int:
+        """Open a sequence slot over pages the caller already owns (a fork)."""
+        if not self._free_slots:
+            raise OutOfPages("no free sequence slot")
+        if len(pages) > self.max_pages_per_seq or self.pages_for(tokens) != len(pages):
+            raise ValueError("adopt: page count does not match the token count")
+        slot = self._free_slots.pop()
+        self.pages[slot] = list(pages)
+        self.owner[slot] = owner
+        self.table[slot, :len(pages)] = pages
+        self.table[slot, len(pages):] = 0
+        self.lengths[slot] = tokens
+        self.active[slot] = True
+        self.dirty_rows.add(slot)
+        return slot
+
+    def extend(self, slot: int, tokens: int) -> None:
+        """Grow a sequence to `tokens` cached tokens (the rest of a prompt after a
+        prefix-cache hit); takes the extra pages before changing anything."""
+        have = self.pages[slot]
+        need = self.pages_for(tokens) - len(have)
+        if tokens < self.lengths[slot]:
+            raise ValueError("extend cannot shrink a sequence")
+        if len(have) + need > self.max_pages_per_seq:
+            raise OutOfPages(f"{tokens} tokens exceed {self.max_pages_per_seq} pages per sequence")
+        if need > 0:
+            fresh = self.take_pages(need)
+            self.table[slot, len(have):len(have) + need] = fresh
+            have.extend(fresh)
+        self.lengths[slot] = tokens
+        self.dirty_rows.add(slot)
+
     def release(self, slot: int) -> None:
-        """Return a sequence's pages (reverse order) and its slot to the free lists."""
+        """Drop a sequence's pages (freed when no snapshot shares them) and free its slot."""
         pages = self.pages.pop(slot)
-        self._free_pages.extend(reversed(pages))
+        self.drop(pages)
         self.owner.pop(slot, None)
         self.lengths[slot] = 0
         self.active[slot] = False

@@ -45,6 +45,7 @@ class HybridConfig:
     max_context: int = 16_384 + 2_048 + 1_024
     state_dtype: torch.dtype = torch.float32
     pages_per_split: int | None = None   # None: adapt to the batch (paged.split_plan)
+    snapshot_rows: int = 0               # extra GDN state rows for prefix snapshots
 
     def is_attention(self, layer: int) -> bool:
         return layer % self.attention_every == self.attention_every - 1
@@ -81,8 +82,10 @@ class HybridCacheEngine:
         n_gdn, n_attn = len(cfg.gdn_layers), len(cfg.attention_layers)
         self.gdn_index = {l: i for i, l in enumerate(cfg.gdn_layers)}
         self.attn_index = {l: i for i, l in enumerate(cfg.attention_layers)}
-        self.state = torch.zeros((n_gdn, cfg.max_seqs, cfg.gdn_value_heads, cfg.value_dim,
-                                  cfg.key_dim), dtype=cfg.state_dtype, device=dev)
+        self.state = torch.zeros((n_gdn, cfg.max_seqs + cfg.snapshot_rows, cfg.gdn_value_heads,
+                                  cfg.value_dim, cfg.key_dim), dtype=cfg.state_dtype, device=dev)
+        self._free_snapshot_rows = list(range(cfg.max_seqs + cfg.snapshot_rows - 1,
+                                              cfg.max_seqs - 1, -1))
         self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads, 2, cfg.page_size,
                                cfg.head_dim), dtype=torch.bfloat16, device=dev)
         self.blocks = BlockManager(cfg.num_pages, cfg.page_size, cfg.max_seqs,
@@ -118,25 +121,105 @@ class HybridCacheEngine:
     def release(self, slot: int) -> None:
         self.blocks.release(slot)
 
+    def extend(self, slot: int, tokens: int) -> None:
+        """Hold `tokens` cached tokens in a sequence (pages for a prompt's remainder)."""
+        self.blocks.extend(slot, tokens)
+
+    # ------------------------------------------------------------ prefix snapshots
+    def _copy_pages(self, src: list, dst: list) -> None:
+        """Copy pages src[i] -> dst[i] in every attention layer's pool (one launch)."""
+        if not src:
+            return
+        n_attn, num_pages = self.kv.shape[0], self.kv.shape[1]
+        offs = np.arange(n_attn, dtype=np.int64)[:, None] * num_pages
+        s = torch.from_numpy((offs + np.asarray(src)[None]).astype(np.int32).ravel())
+        d = torch.from_numpy((offs + np.asarray(dst)[None]).astype(np.int32).ravel())
+        flat = self.kv.view(n_attn * num_pages, *self.kv.shape[2:])
+        paged.kv_copy_pages(flat, s.to(self.device), d.to(self.device))
+
+    def _share_prefix(self, pages: list, tokens: int, copy_partial: bool) -> list:
+        """Own the pages of a `tokens`-long prefix: full pages shared, the partial
+        last page shared or copied into a fresh page."""
+        P = self.cfg.page_size
+        full = tokens // P
+        owned = list(pages[:full])
+        self.blocks.share(owned)
+        if tokens % P:
+            if copy_partial:
+                fresh = self.blocks.take_pages(1)
+                self._copy_pages([pages[full]], fresh)
+                owned += fresh
+            else:
+                self.blocks.share([pages[full]])
+                owned.append(pages[full])
+        return owned
+
+    def snapshot(self, slot: int) -> "PagedSnapshot":
+        """An immutable copy of a live sequence's cache: full pages shared, the partial
+        last page (which the sequence keeps writing) and the GDN state copied."""
+        if not self._free_snapshot_rows:
+            raise MemoryError("no free snapshot state row")
+        tokens = int(self.blocks.lengths[slot])
+        pages = self._share_prefix(self.blocks.pages[slot], tokens, copy_partial=True)
+        row = self._free_snapshot_rows.pop()
+        self.state[:, row].copy_(self.state[:, slot])
+        return PagedSnapshot(self, pages, tokens, row)
+
+    def fork(self, snap: "PagedSnapshot", owner=None) -> int:
+        """A new sequence slot holding the snapshot's prefix: full pages shared, the
+        partial last page copied (the fork appends to it), the GDN state copied."""
+        pages = self._share_prefix(snap.pages, snap.tokens, copy_partial=True)
+        slot = self.blocks.adopt(owner, pages, snap.tokens)
+        self.state[:, slot].copy_(self.state[:, snap.row])
+        return slot
+
+    def copy_snapshot(self, snap: "PagedSnapshot") -> "PagedSnapshot":
+        """Another owner of the same immutable prefix (every page shared)."""
+        if not self._free_snapshot_rows:
+            raise MemoryError("no free snapshot state row")
+        pages = self._share_prefix(snap.pages, snap.tokens, copy_partial=False)
+        row = self._free_snapshot_rows.pop()
+        self.state[:, row].copy_(self.state[:, snap.row])
+        return PagedSnapshot(self, pages, snap.tokens, row)
+
+    def drop_snapshot(self, snap: "PagedSnapshot") -> None:
+        if snap.row is None:
+            return
+        self.blocks.drop(snap.pages)
+        self._free_snapshot_rows.append(snap.row)
+        snap.row = None
+
+    def cache_bytes(self, tokens: int) -> int:
+        """Bytes a cache of `tokens` tokens holds: K/V of every attention layer plus the
+        GDN state of every GDN layer (what a prefix snapshot is charged)."""
+        c = self.cfg
+        kv = tokens * c.kv_heads * c.head_dim * 2 * 2 * len(c.attention_layers)
+        elem = torch.finfo(c.state_dtype).bits // 8
+        st = c.gdn_value_heads * c.value_dim * c.key_dim * elem * len(c.gdn_layers)
+        return int(kv + st)
+
     def prefill(self, new: list, gdn_inputs, kv_inputs, out=None) -> int:
         """Run admitted prompts through every layer's cache work.
 
         new: [(slot, prompt_len)] of sequences admitted this step (their GDN
-        state rows start at zero). gdn_inputs(layer, ntok) -> (q, k, v, decay,
-        beta) packed [ntok, ...] in `new` order; kv_inputs(layer, ntok) -> (k, v)
+        state rows start at zero), or [(slot, start, stop)] to continue a prompt
+        from position `start` (a prefix-cache fork: its state row holds the state
+        after `start` tokens). gdn_inputs(layer, ntok) -> (q, k, v, decay, beta)
+        packed [ntok, ...] in `new` order; kv_inputs(layer, ntok) -> (k, v)
         [ntok, Hkv, D]. GDN layers run the chunked prefill kernel over all
         prompts at once (one launch per layer, varlen); attention layers write
         the prompts' K/V into their pages. Returns the kernels launched.
         """
         if not new:
             return 0
-        lengths = [n for _, n in new]
+        spans = [(e[0], 0, e[1]) if len(e) == 2 else tuple(e) for e in new]
+        lengths = [stop - start for _, start, stop in spans]
         total = int(sum(lengths))
         cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32),
                           device=self.device)
-        slots = torch.tensor([s for s, _ in new], dtype=torch.int32, device=self.device)
+        slots = torch.tensor([s for s, _, _ in spans], dtype=torch.int32, device=self.device)
         kv_slots = torch.from_numpy(np.concatenate(
-            [self.blocks.prompt_slots(s, 0, n) for s, n in new])).to(self.device)
+            [self.blocks.prompt_slots(s, a, b) for s, a, b in spans])).to(self.device)
         launched = 0
         for layer in range(self.cfg.layers):
             if self.cfg.is_attention(layer):
@@ -223,3 +306,14 @@ class HybridCacheEngine:
         return {"gdn": float(gdn), "attention_per_layer": attn_layer,
                 "attention": attn_layer * len(c.attention_layers),
                 "total": float(gdn) + attn_layer * len(c.attention_layers)}
+
+
+class PagedSnapshot:
+    """A prefix cache entry: shared pages, a GDN state row and a token count."""
+
+    def __init__(self, engine: HybridCacheEngine, pages: list, tokens: int, row: int):
+        self.engine, self.pages, self.tokens, self.row = engine, pages, tokens, row
+
+    @property
+    def nbytes(self) -> int:
+        return self.engine.cache_bytes(self.tokens)

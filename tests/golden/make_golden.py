@@ -11,6 +11,8 @@ It executes, without copying, these reference functions and classes:
   scripts/mlx_attention_qualify.py `numpy_attention` -- causal GQA oracle.
   src/studio_compute/mlx_racing.py `ContinuousBatcher` -- the scheduler.
   src/studio_compute/cache.py `PrefixCache` -- the prefix snapshot pool.
+  src/studio_compute/inference.py `create_request`, `release_request` -- the
+      admission, deferral, failure and release rules of a request.
 Inputs are seeded NumPy draws (the reference tests draw with mx.random,
 whose bits are not reproducible without MLX), rounded to bf16 where the
 reference feeds bf16. Outputs are written as .npz / .json next to this file.
@@ -355,6 +357,126 @@ def main():
     print("attention:", make_attention(ref))
     print("scheduler:", make_scheduler(ref))
     print("prefix:", make_prefix(ref))
+    print("lifecycle:", make_lifecycle(ref))
+
+
+
+# ---------------------------------------------------------------- request lifecycle
+class _Lease:
+    def __init__(self, log, name, fail):
+        self.log, self.name, self.fail = log, name, fail
+
+    def __enter__(self):
+        if self.fail:
+            raise MemoryError("policy reload does not fit")
+        self.log.append(("enter", self.name))
+        return {"factors": self.name}
+
+    def __exit__(self, *exc):
+        self.log.append(("exit", self.name))
+        return False
+
+
+def lifecycle_engine(spec, log):
+    """A fake engine with the attributes inference.create_request reads."""
+    state = {"persistent": spec["persistent"]}
+    prefix_hit = spec.get("prefix_hit")
+
+    def estimate(length, batch=1, **options):
+        return spec["per_token"] * length * batch + spec["base"]
+
+    def admit(needed):
+        log.append(("admit", needed))
+        if needed > spec["admit_limit"]:
+            raise MemoryError("live memory pressure")
+
+    def get(identity, policy, precision, tokens, fork=False):
+        log.append(("prefix_get", identity, policy, precision, len(tokens), fork))
+        if spec.get("prefix_error"):
+            raise ValueError("corrupt cache")
+        if prefix_hit is None or prefix_hit > len(tokens):
+            return None
+        return (["snapshot"], "logits", prefix_hit)
+
+    mx = SimpleNamespace(uint32="uint32", array=lambda v, t: ("key", tuple(v)),
+                         random=SimpleNamespace(key=lambda seed: ("seed", seed)))
+    return SimpleNamespace(
+        resident=SimpleNamespace(estimate_inference=estimate),
+        prefixes=SimpleNamespace(limit=spec["prefix_limit"], bytes=spec["prefix_bytes"], get=get),
+        policies=dict.fromkeys(spec["policies"], {}),
+        idle_factors={"a": SimpleNamespace(nbytes=spec["idle_bytes"])},
+        reserved=dict(spec["reserved"]),
+        persistent_bytes=lambda: state["persistent"],
+        admission_budget_bytes=lambda: spec["budget"],
+        admit=admit,
+        _borrow_policy=lambda ref: _Lease(log, ref, spec.get("lease_fail", False)),
+        prefix_identity="ident",
+        lm=SimpleNamespace(make_cache=lambda: ["fresh"]),
+        mx=mx,
+    )
+
+
+def lifecycle_scenarios(n=160, seed=8):
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(n):
+        prompt = int(rng.integers(1, 60))
+        body = {"policy": ["p", "q"][int(rng.integers(0, 2))],
+                "prompt_token_ids": [int(t) for t in rng.integers(0, 9, size=prompt)],
+                "max_tokens": int(rng.integers(1, 40))}
+        if rng.random() < 0.3:
+            body["target_token_ids"] = [1] * int(rng.integers(1, 10))
+        if rng.random() < 0.3:
+            body["use_prefix_cache"] = bool(rng.integers(0, 2))
+        if rng.random() < 0.2:
+            body["cache_precision"] = "8bit"
+        if rng.random() < 0.5:
+            body["rng_key"] = [int(rng.integers(0, 99)), 1]
+        else:
+            body["seed"] = int(rng.integers(0, 99))
+        spec = {
+            "per_token": int(rng.integers(1, 4)), "base": int(rng.integers(0, 20)),
+            "persistent": int(rng.integers(20, 120)), "budget": int(rng.integers(80, 260)),
+            "admit_limit": int(rng.integers(0, 200)), "prefix_limit": int(rng.integers(0, 80)),
+            "prefix_bytes": int(rng.integers(0, 20)), "idle_bytes": int(rng.integers(0, 30)),
+            "policies": ["p"] if rng.random() < 0.6 else [],
+            "reserved": {"replay": int(rng.integers(1, 80))} if rng.random() < 0.5 else {},
+            "lease_fail": bool(rng.random() < 0.1),
+            "prefix_error": bool(rng.random() < 0.05),
+            "prefix_hit": (int(rng.integers(0, prompt + 1)) if rng.random() < 0.5 else None),
+        }
+        out.append({"id": f"r{i}", "body": body, "spec": spec})
+    return out
+
+
+def run_lifecycle(create_request, release_request, scenario):
+    log = []
+    engine = lifecycle_engine(scenario["spec"], log)
+    try:
+        request = create_request(engine, scenario["id"], scenario["body"])
+    except Exception as error:  # noqa: BLE001 -- recorded as the outcome
+        return {"outcome": f"{type(error).__name__}: {error}", "log": log,
+                "reserved": engine.reserved}
+    if request is None:
+        return {"outcome": "defer", "log": log, "reserved": engine.reserved}
+    record = {"outcome": "request", "offset": request.offset,
+              "cached_tokens": request.cached_tokens, "has_logits": request.logits is not None,
+              "cache": list(request.cache), "rng": list(request.rng)}
+    release_request(engine, request)
+    return {**record, "log": log, "reserved": engine.reserved}
+
+
+def make_lifecycle(ref: Path):
+    sys.path.insert(0, str(ref / "src"))
+    from studio_compute.inference import create_request, release_request
+
+    result = []
+    for scenario in lifecycle_scenarios():
+        result.append({"scenario": scenario,
+                       "trace": run_lifecycle(create_request, release_request, scenario)})
+    (HERE / "lifecycle_traces.json").write_text(
+        json.dumps(result, separators=(",", ":"), default=list))
+    return len(result)
 
 
 if __name__ == "__main__":
