@@ -358,6 +358,7 @@ def main():
     print("scheduler:", make_scheduler(ref))
     print("prefix:", make_prefix(ref))
     print("lifecycle:", make_lifecycle(ref))
+    print("admission:", make_admission(ref))
 
 
 
@@ -476,6 +477,191 @@ def make_lifecycle(ref: Path):
                        "trace": run_lifecycle(create_request, release_request, scenario)})
     (HERE / "lifecycle_traces.json").write_text(
         json.dumps(result, separators=(",", ":"), default=list))
+    return len(result)
+
+
+
+# ---------------------------------------------------------------- byte admission
+def load_methods(path: Path, cls: str, names, new_name: str, bases, scope: dict):
+    """Compile chosen methods of a reference class into a new class (AST only, so
+    the module's own imports -- MLX among them -- are never executed)."""
+    tree = ast.parse(path.read_text())
+    node = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == cls)
+    body = [n for n in node.body if isinstance(n, ast.FunctionDef) and n.name in names]
+    assert len(body) == len(names), (cls, names)
+    new = ast.ClassDef(name=new_name, bases=[ast.Name(b, ast.Load()) for b in bases],
+                       keywords=[], body=body, decorator_list=[], type_params=[])
+    module = ast.fix_missing_locations(ast.Module(body=[new], type_ignores=[]))
+    exec(compile(module, str(path), "exec"), scope)
+    return scope[new_name]
+
+
+def reference_admission_classes(ref: Path):
+    src = ref / "src/studio_compute"
+    scope = {"math": __import__("math")}
+    resident = load_methods(src / "model.py", "Qwen27Model", ["estimate_inference", "admit"],
+                            "Resident", [], scope)
+    engine = load_methods(src / "engine.py", "ResidentEngine",
+                          ["_evict_policy", "admission_budget_bytes", "admit"], "Engine", [],
+                          scope)
+    runtime = load_methods(src / "runtime.py", "RuntimeEngine",
+                           ["_cache_capacity", "admit", "inference_batch_capacity"], "Runtime",
+                           ["Engine"], scope)
+    return resident, runtime
+
+
+class AdmissionPrefixes:
+    """Snapshot pool stand-in: bytes, limit, and trim() dropping the oldest first."""
+
+    def __init__(self, limit, sizes, log):
+        self.limit, self.sizes, self.log = limit, list(sizes), log
+
+    @property
+    def bytes(self):
+        return sum(self.sizes)
+
+    def trim(self, limit_bytes):
+        self.log.append(["trim", limit_bytes])
+        target = max(0, min(self.limit, limit_bytes))
+        while self.bytes > target and self.sizes:
+            self.sizes.pop(0)
+
+
+def admission_engine(classes, spec, log):
+    """A fake runtime engine with the attributes the admission methods read."""
+    resident_cls, runtime_cls = classes
+    engine = runtime_cls()
+    every = spec["attention_every"]
+    layers = [SimpleNamespace(
+        is_linear=l % every != every - 1,
+        self_attn=SimpleNamespace(num_key_value_heads=spec["kv_heads"],
+                                  head_dim=spec["head_dim"]),
+        linear_attn=SimpleNamespace(num_v_heads=spec["v_heads"], head_v_dim=spec["dv"],
+                                    head_k_dim=spec["dk"])) for l in range(spec["layers"])]
+    policies = OrderedDict((name, {"factors": SimpleNamespace(name=name, nbytes=size)})
+                           for name, size, _ in spec["policies"])
+    idle = SimpleNamespace(name="idle", nbytes=spec["idle_bytes"])
+
+    def policy_bytes():
+        return sum(p["factors"].nbytes for p in engine.policies.values())
+
+    def active():
+        return spec["base_active"] + policy_bytes() + engine.prefixes.bytes
+
+    mx = SimpleNamespace(get_active_memory=active)
+    resident = resident_cls()
+    resident.lm = SimpleNamespace(layers=layers)
+    resident.mx = mx
+    resident.budget = spec["budget"]
+    resident.selected = (policies[spec["selected"]]["factors"] if spec["selected"] else
+                         {"idle": idle})
+    resident.select = lambda factors: (log.append(["select", sorted(factors)]),
+                                       setattr(resident, "selected", factors))
+    resident.spec = spec
+    engine.resident = resident
+    engine.mx = mx
+    engine.policies = policies
+    engine.policy_users = {name: users for name, _, users in spec["policies"] if users}
+    engine.idle_factors = {"idle": idle}
+    engine.reserved = dict(spec["reserved"])
+    engine.prefixes = AdmissionPrefixes(spec["prefix_limit"], spec["prefix_sizes"], log)
+    engine.execution_profile = spec["profile"]
+    engine.capabilities = ({"recommended_working_set_bytes": spec["recommended"]}
+                           if spec["recommended"] is not None else {})
+    engine.persistent_bytes = lambda: (spec["base_persistent"] + spec["idle_bytes"]
+                                       + policy_bytes() + engine.prefixes.bytes)
+    if spec["concurrency"] is not None:
+        engine.inference_concurrency = spec["concurrency"]
+    return engine
+
+
+def admission_scenarios(n=60, seed=12):
+    rng = np.random.default_rng(seed)
+    gib = 1 << 30
+    out = []
+    for i in range(n):
+        npol = int(rng.integers(0, 4))
+        policies = [[f"p{j}", int(rng.integers(1, 6)) * gib // 4, int(rng.integers(0, 2))]
+                    for j in range(npol)]
+        spec = {
+            "layers": int(rng.choice([8, 48, 64])), "attention_every": int(rng.choice([2, 4])),
+            "kv_heads": int(rng.choice([2, 4])), "head_dim": int(rng.choice([128, 256])),
+            "v_heads": int(rng.choice([16, 32, 48])), "dv": 128, "dk": 128,
+            "base_active": int(rng.integers(10, 60)) * gib,
+            "base_persistent": int(rng.integers(10, 60)) * gib,
+            "idle_bytes": int(rng.integers(0, 3)) * gib // 2,
+            "policies": policies,
+            "selected": (policies[int(rng.integers(0, npol))][0]
+                         if npol and rng.random() < 0.7 else None),
+            "budget": int(rng.integers(60, 180)) * gib,
+            "recommended": (int(rng.integers(50, 200)) * gib if rng.random() < 0.4 else None),
+            "profile": ["bf16-fast", "legacy"][int(rng.random() < 0.3)],
+            "reserved": ({"replay": int(rng.integers(1, 30)) * gib} if rng.random() < 0.5
+                         else {}),
+            "prefix_limit": int(rng.integers(0, 40)) * gib,
+            "prefix_sizes": [int(x) * gib // 2 for x in rng.integers(1, 8, size=int(
+                rng.integers(0, 6)))],
+            "concurrency": int(rng.integers(1, 12)) if rng.random() < 0.7 else None,
+        }
+        ops = []
+        for _ in range(14):
+            kind = rng.choice(["estimate", "admit", "capacity", "batch", "reserve", "unreserve"],
+                              p=[.2, .3, .15, .15, .1, .1])
+            precision = ["bf16", "8bit", "fp8"][int(rng.choice(3, p=[.6, .3, .1]))]
+            if kind == "estimate":
+                ops.append(["estimate", int(rng.integers(0, 300_000)),
+                            int(rng.integers(1, 9)), precision])
+            elif kind == "admit":
+                ops.append(["admit", int(rng.integers(0, 80)) * gib // 2])
+            elif kind == "capacity":
+                ops.append(["capacity", int(rng.integers(0, 20)) * gib // 2,
+                            int(rng.integers(0, 20)) * gib // 2])
+            elif kind == "batch":
+                ops.append(["batch", int(rng.integers(1, 40_000)), int(rng.integers(1, 40_000)),
+                            ["bf16", "8bit"][int(rng.random() < 0.3)], int(rng.integers(1, 16))])
+            elif kind == "reserve":
+                ops.append(["reserve", f"r{len(ops)}", int(rng.integers(1, 20)) * gib])
+            else:
+                ops.append(["unreserve"])
+        out.append({"id": f"a{i}", "spec": spec, "ops": ops})
+    return out
+
+
+def run_admission(classes, scenario):
+    log = []
+    engine = admission_engine(classes, scenario["spec"], log)
+    steps = []
+    for op in scenario["ops"]:
+        start = len(log)
+        try:
+            if op[0] == "estimate":
+                result = engine.resident.estimate_inference(op[1], op[2], cache_precision=op[3])
+            elif op[0] == "admit":
+                result = engine.admit(op[1])
+            elif op[0] == "capacity":
+                result = engine._cache_capacity(op[1], additional=op[2])
+            elif op[0] == "batch":
+                body = {"prompt_token_ids": [0] * op[1], "max_tokens": op[2],
+                        "cache_precision": op[3]}
+                result = engine.inference_batch_capacity(body, op[4])
+            elif op[0] == "reserve":
+                engine.reserved[op[1]] = op[2]
+                result = None
+            else:
+                result = engine.reserved.popitem()[0] if engine.reserved else None
+        except Exception as error:  # noqa: BLE001 -- recorded as the outcome
+            result = f"{type(error).__name__}: {error}"
+        steps.append({"result": result, "log": log[start:], "policies": list(engine.policies),
+                      "prefix_sizes": list(engine.prefixes.sizes),
+                      "reserved": sorted(engine.reserved.items())})
+    return steps
+
+
+def make_admission(ref: Path):
+    classes = reference_admission_classes(ref)
+    result = [{"scenario": sc, "trace": run_admission(classes, sc)}
+              for sc in admission_scenarios()]
+    (HERE / "admission_traces.json").write_text(json.dumps(result, separators=(",", ":")))
     return len(result)
 
 
