@@ -119,6 +119,61 @@ int sc_gdn_chunk_prefill(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
                          int dk, int dv, int num_slots, void* stream);
 
 /* --------------------------------------------------------------------------
+ * (a) GDN layer glue: conv taps, SiLU, q/k norm, gates, gated RMS norm.
+ *
+ * Replaces the decode-time GDN layer between its projections and out_proj:
+ * studio_compute/numerics/bf16.py:44-139 `gdn_inner` (decode_one=True branch)
+ * called from `_decode_gdn_token` (bf16.py:191-210), which runs
+ * conv1d + SiLU, `_normalize_qk`, the gates of bf16.py:98-102,
+ * gated_delta_token and rms_norm(y) * silu(z) as separate MLX ops.
+ * Every value is rounded to bf16 where the reference's ops round.
+ *
+ * Shapes (C = 2*Hk*128 + Hv*128 channels, q | k | v; dk = dv = 128):
+ * qkv  [B, C] bf16 (in_proj_qkv output)   z [B, Hv*128] bf16 (in_proj_z)
+ * a, b [B, Hv] bf16 (in_proj_a / in_proj_b)
+ * conv_w [C, 4] bf16 (the depthwise conv1d weight [C, 4, 1]), 8-byte aligned
+ * A_log, dt_bias [Hv] fp32; norm_w [128] bf16; eps of the gated norm
+ * taps [num_slots, 4, C] bf16 in/out: a ring of the last inputs; the token at
+ *        absolute position t reads rows (t-3..t-1) & 3 and writes row t & 3.
+ *        The reference's taps[B, 3, C] are rows (t-3..t-1) & 3 in order; a new
+ *        sequence's ring starts at zero.
+ * position [B] int32: absolute position t of each row's token (>= 0)
+ * state, state_slot, num_slots: as sc_gdn_decode (fp32 state, -1 skips a row)
+ * out  [B, Hv*128] bf16: rms_norm(y, norm_w, eps) * silu(z)
+ * Launches one 2-CTA cluster per (row, value head). */
+int sc_gdn_decode_fused(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
+                        const sc_bf16* b, const sc_bf16* conv_w, const float* A_log,
+                        const float* dt_bias, const sc_bf16* norm_w, float eps,
+                        sc_bf16* taps, const int32_t* position, float* state,
+                        const int32_t* state_slot, sc_bf16* out, int B, int Hk, int Hv,
+                        int num_slots, void* stream);
+
+/* The same front for the packed prompt tokens of a prefill (bf16.py:44-102 with
+ * L > 1): sequence s is tokens cu_seqlens[s]..cu_seqlens[s+1] of qkv [tokens, C],
+ * a, b [tokens, Hv]; it continues from position seq_start[s] of state slot
+ * seq_slot[s], reading that slot's tap ring for the first three tokens.
+ * Writes the inputs of sc_gdn_chunk_prefill: q, k [tokens, Hk, 128],
+ * v [tokens, Hv, 128] bf16, g, beta [tokens, Hv] fp32. Does not write taps. */
+int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const sc_bf16* b,
+                         const sc_bf16* conv_w, const float* A_log, const float* dt_bias,
+                         const sc_bf16* taps, const int32_t* cu_seqlens,
+                         const int32_t* seq_slot, const int32_t* seq_start, sc_bf16* q,
+                         sc_bf16* k, sc_bf16* v, float* g, float* beta, int nseq,
+                         int total_tokens, int Hk, int Hv, int num_slots, void* stream);
+
+/* After a prefill (stream-ordered after sc_gdn_prefill_front): each sequence's
+ * last min(3, n) inputs into its tap ring (the new taps of bf16.py:137). */
+int sc_gdn_taps_store(const sc_bf16* qkv, sc_bf16* taps, const int32_t* cu_seqlens,
+                      const int32_t* seq_slot, const int32_t* seq_start, int nseq,
+                      int channels, int num_slots, void* stream);
+
+/* out = rms_norm(y, w, eps) * silu(z) over rows of `width` (a multiple of 128):
+ * bf16.py:129-135 for any number of rows (the prefill output). y, z, out
+ * [rows, width] bf16, w [width] bf16, all 8-byte aligned. */
+int sc_gated_rmsnorm(const sc_bf16* y, const sc_bf16* z, const sc_bf16* w, float eps,
+                     sc_bf16* out, long long rows, int width, void* stream);
+
+/* --------------------------------------------------------------------------
  * (b) KV append: scatter new keys/values into the paged pool.
  *
  * Replaces the KV write of mlx-vlm KVCache.update_and_fetch and

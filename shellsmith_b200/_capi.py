@@ -26,6 +26,12 @@ SIGNATURES = {
     "sc_gdn_decode_bf16": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "sc_gdn_chunk_prefill": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
                              _I, _P],
+    "sc_gdn_decode_fused": [_P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I,
+                            _I, _P],
+    "sc_gdn_prefill_front": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,
+                             _I, _I, _I, _P],
+    "sc_gdn_taps_store": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "sc_gated_rmsnorm": [_P, _P, _P, _F, _P, _I64, _I, _P],
     "sc_kv_append": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_gather": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_copy_pages": [_P, _P, _P, _I, _I, _I, _I, _I64, _P],

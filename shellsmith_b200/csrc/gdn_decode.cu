@@ -197,17 +197,20 @@ __global__ void __launch_bounds__(128)
     if (threadIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
     return;
   }
-  if (status != nullptr && (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT))
-    return;
   const int kh = h / (Hv / Hk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* S = state + ((size_t)slot * Hv + h) * (size_t)dv * 128 +
              (size_t)chunk0 * kBulkRows * 128;
+  // One thread decides whether an earlier wait timed out, so the whole CTA
+  // either streams its chunks or skips them.
+  unsigned int* aborted = reinterpret_cast<unsigned int*>(bars + nchunks);
 
   if (tid == 0) {
+    *aborted = status != nullptr &&
+               (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT);
     for (int c = 0; c < nchunks; ++c) mbar_init(&bars[c], 1);
     fence_mbar_init();
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = 0; c < nchunks && !*aborted; ++c) {
       mbar_arrive_expect_tx(&bars[c], kBulkChunkBytes);
       bulk_g2s(smem + c * kBulkChunkBytes, S + (size_t)c * kBulkRows * 128, kBulkChunkBytes,
                &bars[c]);
@@ -217,6 +220,7 @@ __global__ void __launch_bounds__(128)
   const float4 qf = load_bf16x4(q + ((size_t)b * Hk + kh) * 128 + 4 * lane);
   const float decay = g[bh], bt = beta[bh];
   __syncthreads();  // barrier initialisation is visible before anyone waits
+  if (*aborted) return;
 
   int ok = 1;
   for (int c = 0; c < nchunks; ++c) {
@@ -280,7 +284,7 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if constexpr (std::is_same<ST, float>::value) {
     if (dk == 128 && dv % (kBulkRows * kBulkChunksPerCta) == 0) {
-      const int smem = kBulkChunksPerCta * (kBulkChunkBytes + 8);
+      const int smem = kBulkChunksPerCta * (kBulkChunkBytes + 8) + 8;
       static int configured[64] = {};
       int dev = 0;
       cudaGetDevice(&dev);

@@ -1,0 +1,224 @@
+"""GDN layer glue on the GPU (conv taps, SiLU, q/k norm, gates, gated RMS norm)
+against the CPU restatement in oracle.front.
+
+Bars. Tap rings are bit-exact (they are copies of the inputs). The front's
+q, k, v, g, beta are bf16 values that the kernel computes in fp32 and the
+oracle in float64 before the same roundings, so an element may land one bf16
+step (2^-8 relative) away: at most 1% of elements may differ and none by more
+than 2 steps. The layer output (after the recurrence and the gated norm) is
+within rtol 3e-2 / atol 3e-2 of the oracle, the fp32 state within 2e-2
+absolute (a one-step difference in v moves a state row by beta * 2^-8 |v|).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import front as ofront
+from oracle import gdn as ogdn
+from shellsmith_b200 import gdn_layer
+from shellsmith_b200.gdn_layer import GDNWeights
+
+pytestmark = pytest.mark.gpu
+
+bf = ofront.bf
+
+
+def _weights(rng, Hk, Hv, cuda):
+    C = (2 * Hk + Hv) * 128
+    conv_w = bf((rng.standard_normal((C, 4)) * 0.5).astype(np.float32))
+    a_log = np.log(rng.uniform(1, 16, Hv)).astype(np.float32)
+    dt_bias = bf(rng.standard_normal(Hv).astype(np.float32))
+    norm_w = bf((1 + 0.1 * rng.standard_normal(128)).astype(np.float32))
+    w = GDNWeights(conv_w=torch.from_numpy(conv_w).to(cuda, torch.bfloat16),
+                   a_log=torch.from_numpy(a_log).to(cuda),
+                   dt_bias=torch.from_numpy(dt_bias).to(cuda),
+                   norm_w=torch.from_numpy(norm_w).to(cuda, torch.bfloat16), eps=1e-6,
+                   key_heads=Hk, value_heads=Hv)
+    return w, (conv_w, a_log, dt_bias, norm_w)
+
+
+def _inputs(rng, shape_prefix, Hk, Hv):
+    C = (2 * Hk + Hv) * 128
+    qkv = bf(rng.standard_normal((*shape_prefix, C)).astype(np.float32))
+    z = bf(rng.standard_normal((*shape_prefix, Hv * 128)).astype(np.float32))
+    a = bf(rng.standard_normal((*shape_prefix, Hv)).astype(np.float32))
+    b = bf(rng.standard_normal((*shape_prefix, Hv)).astype(np.float32))
+    return qkv, z, a, b
+
+
+def _dev(x, cuda, dtype=torch.bfloat16):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(cuda, dtype)
+
+
+def _close_bf16(got, want, name):
+    """At most 1% of elements one or two bf16 steps apart, none further."""
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    step = np.maximum(np.abs(want), 1e-30) * 2.0 ** -7
+    far = np.abs(got - want) > 2.01 * step
+    near = np.abs(got - want) > 0
+    assert not far.any(), (name, np.abs(got - want).max())
+    assert near.mean() <= 0.01, (name, near.mean())
+
+
+@pytest.mark.parametrize("Hk,Hv,B", [(2, 4, 3), (16, 32, 5)])
+def test_decode_fused_matches_oracle_over_steps(cuda, Hk, Hv, B):
+    rng = np.random.default_rng(Hk * 10 + Hv)
+    w, (conv_w, a_log, dt_bias, norm_w) = _weights(rng, Hk, Hv, cuda)
+    slots = B + 2
+    perm = rng.permutation(slots)[:B].astype(np.int32)
+    taps = gdn_layer.new_taps(slots, w, device=cuda)
+    state = torch.zeros((slots, Hv, 128, 128), dtype=torch.float32, device=cuda)
+    ref_taps = np.zeros((B, 3, w.channels), np.float32)
+    ref_state = np.zeros((B, Hv, 128, 128))
+    slot_t = _dev(perm, cuda, torch.int32)
+    for step in range(5):
+        qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
+        pos = torch.full((B,), step, dtype=torch.int32, device=cuda)
+        out = gdn_layer.gdn_decode_fused(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda),
+                                         _dev(b, cuda), w, taps, pos, state, slot_t)
+        want, ref_taps, ref_state = ofront.decode_layer(qkv, z, a, b, ref_taps, ref_state, conv_w,
+                                                        a_log, dt_bias, norm_w, 1e-6, Hk, Hv)
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=3e-2, atol=3e-2)
+        for r in range(B):
+            window = gdn_layer.ring_window(taps, int(perm[r]), step + 1)
+            assert np.array_equal(window.float().cpu().numpy(), ref_taps[r])
+    got_state = state[perm.astype(np.int64)].cpu().numpy()
+    assert np.abs(got_state - ref_state).max() <= 2e-2
+    assert torch.count_nonzero(state[np.setdiff1d(np.arange(slots), perm)]) == 0
+
+
+def test_decode_fused_skips_rows_and_keeps_others(cuda):
+    rng = np.random.default_rng(4)
+    Hk, Hv, B = 2, 4, 3
+    w, _ = _weights(rng, Hk, Hv, cuda)
+    taps = gdn_layer.new_taps(4, w, device=cuda)
+    state = torch.randn((4, Hv, 128, 128), device=cuda)
+    before_state, before_taps = state.clone(), taps.clone()
+    qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
+    slot_t = torch.tensor([2, -1, 0], dtype=torch.int32, device=cuda)
+    pos = torch.tensor([7, 7, 9], dtype=torch.int32, device=cuda)
+    gdn_layer.gdn_decode_fused(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda), w,
+                               taps, pos, state, slot_t)
+    torch.cuda.synchronize()
+    for s in (1, 3):
+        assert torch.equal(state[s], before_state[s]) and torch.equal(taps[s], before_taps[s])
+    # Only the write rows of positions 7 (slot 2) and 9 (slot 0) changed.
+    assert torch.equal(taps[2, [0, 1, 2]], before_taps[2, [0, 1, 2]])
+    assert torch.equal(taps[2, 3], _dev(qkv[0], cuda))
+    assert torch.equal(taps[0, 1], _dev(qkv[2], cuda))
+
+
+def _oracle_prefill(qkv, z, a, b, taps3, s0, weights_np, Hk, Hv):
+    """Per-sequence oracle: front over the run, float64 recurrence, gated norm."""
+    conv_w, a_log, dt_bias, norm_w = weights_np
+    q, k, v, g, beta, new_taps = ofront.front(qkv[None], a[None], b[None], taps3[None], conv_w,
+                                              a_log, dt_bias, Hk, Hv)
+    y, s = ogdn.sequential(q, k, v, g, beta, s0[None])
+    y = bf(np.asarray(y, np.float32))
+    L = qkv.shape[0]
+    out = ofront.gated_rms_norm(y[0], z.reshape(L, Hv, 128), norm_w, 1e-6)
+    return (q[0], k[0], v[0], g[0], beta[0]), out.reshape(L, -1), new_taps[0], s[0]
+
+
+def test_prefill_front_and_layer_match_oracle_ragged_with_history(cuda):
+    """Two prompts (100 and 37 tokens), the second continuing at position 5 of a
+    slot whose ring holds history; then the taps, the state and the output."""
+    rng = np.random.default_rng(8)
+    Hk, Hv = 2, 4
+    w, weights_np = _weights(rng, Hk, Hv, cuda)
+    C = w.channels
+    lengths, starts, slots = [100, 37], [0, 5], [3, 1]
+    taps = gdn_layer.new_taps(4, w, device=cuda)
+    hist = bf(rng.standard_normal((3, C)).astype(np.float32))    # positions 2, 3, 4 of slot 1
+    for p, row in zip((2, 3, 4), hist):
+        taps[1, p % 4] = _dev(row, cuda)
+    s0 = (rng.standard_normal((Hv, 128, 128)) * 0.1).astype(np.float32)
+    state = torch.zeros((4, Hv, 128, 128), dtype=torch.float32, device=cuda)
+    state[1] = torch.from_numpy(s0).to(cuda)
+    qkv, z, a, b = _inputs(rng, (sum(lengths),), Hk, Hv)
+    cu = torch.tensor([0, 100, 137], dtype=torch.int32, device=cuda)
+    slot_t = torch.tensor(slots, dtype=torch.int32, device=cuda)
+    start_t = torch.tensor(starts, dtype=torch.int32, device=cuda)
+    front = gdn_layer.gdn_prefill_front(_dev(qkv, cuda), _dev(a, cuda), _dev(b, cuda), w, taps,
+                                        cu, slot_t, start_t)
+    out = gdn_layer.gdn_prefill(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda), w,
+                                taps, state, cu, slot_t, start_t)
+    torch.cuda.synchronize()
+    offs = [0, 100, 137]
+    for i, (L, start, slot) in enumerate(zip(lengths, starts, slots)):
+        sl = slice(offs[i], offs[i + 1])
+        t3 = np.zeros((3, C), np.float32) if start == 0 else hist
+        s_init = np.zeros((Hv, 128, 128)) if start == 0 else s0
+        want_front, want_out, want_taps, want_s = _oracle_prefill(
+            qkv[sl], z[sl], a[sl], b[sl], t3, s_init, weights_np, Hk, Hv)
+        for name, got, want in zip("q k v g beta".split(), front, want_front):
+            _close_bf16(got[sl].float().cpu().numpy(), want, name)
+        np.testing.assert_allclose(out[sl].float().cpu().numpy(), want_out, rtol=3e-2,
+                                   atol=3e-2)
+        window = gdn_layer.ring_window(taps, slot, start + L).float().cpu().numpy()
+        assert np.array_equal(window, want_taps)
+        assert np.abs(state[slot].cpu().numpy() - want_s).max() <= 2e-2
+
+
+def test_prefill_then_decode_equals_longer_prefill(cuda):
+    """Prefill 70 tokens then decode 3 == prefill 73 tokens (taps exact, state and
+    the last outputs within tolerance)."""
+    rng = np.random.default_rng(12)
+    Hk, Hv = 2, 4
+    w, _ = _weights(rng, Hk, Hv, cuda)
+    qkv, z, a, b = (_dev(x, cuda) for x in _inputs(rng, (73,), Hk, Hv))
+    zero = torch.tensor([0], dtype=torch.int32, device=cuda)
+    taps = gdn_layer.new_taps(2, w, device=cuda)
+    state = torch.zeros((2, Hv, 128, 128), dtype=torch.float32, device=cuda)
+    slot0 = torch.tensor([0], dtype=torch.int32, device=cuda)
+    slot1 = torch.tensor([1], dtype=torch.int32, device=cuda)
+    gdn_layer.gdn_prefill(qkv[:70], z[:70], a[:70], b[:70], w, taps, state,
+                          torch.tensor([0, 70], dtype=torch.int32, device=cuda), slot0, zero)
+    outs = []
+    for t in range(70, 73):
+        pos = torch.tensor([t], dtype=torch.int32, device=cuda)
+        outs.append(gdn_layer.gdn_decode_fused(qkv[t:t + 1], z[t:t + 1], a[t:t + 1],
+                                               b[t:t + 1], w, taps, pos, state, slot0))
+    full = gdn_layer.gdn_prefill(qkv, z, a, b, w, taps, state,
+                                 torch.tensor([0, 73], dtype=torch.int32, device=cuda), slot1,
+                                 zero)
+    torch.cuda.synchronize()
+    assert torch.equal(gdn_layer.ring_window(taps, 0, 73), gdn_layer.ring_window(taps, 1, 73))
+    assert (state[0] - state[1]).abs().max().item() <= 2e-3
+    np.testing.assert_allclose(torch.cat(outs).float().cpu().numpy(),
+                               full[70:].float().cpu().numpy(), rtol=3e-2, atol=3e-2)
+
+
+def test_gdn_inner_reference_call_site(cuda):
+    """The reference signature: taps [B, 3, C] in and out, L = 1 and L > 1."""
+    rng = np.random.default_rng(21)
+    Hk, Hv, B = 2, 4, 2
+    w, weights_np = _weights(rng, Hk, Hv, cuda)
+    C = w.channels
+    for L in (1, 9):
+        qkv, z, a, b = _inputs(rng, (B, L), Hk, Hv)
+        taps3 = bf(rng.standard_normal((B, 3, C)).astype(np.float32))
+        s0 = (rng.standard_normal((B, Hv, 128, 128)) * 0.1).astype(np.float32)
+        state = torch.from_numpy(s0).to(cuda)
+        mixed, taps_out, nxt = gdn_layer.gdn_inner(
+            None, _dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda),
+            _dev(taps3, cuda), state, decode_one=L == 1, weights=w)
+        assert nxt is state and mixed.shape == (B, L, Hv * 128)
+        for r in range(B):
+            _, want_out, want_taps, want_s = _oracle_prefill(qkv[r], z[r], a[r], b[r], taps3[r],
+                                                             s0[r], weights_np, Hk, Hv)
+            assert np.array_equal(taps_out[r].float().cpu().numpy(), want_taps)
+            np.testing.assert_allclose(mixed[r].float().cpu().numpy(), want_out, rtol=3e-2,
+                                       atol=3e-2)
+            assert np.abs(state[r].cpu().numpy() - want_s).max() <= 2e-2
+
+
+@pytest.mark.parametrize("width", [128, 256])
+def test_gated_rmsnorm_matches_oracle(cuda, width):
+    rng = np.random.default_rng(width)
+    y = bf(rng.standard_normal((1000, width)).astype(np.float32) * 3)
+    z = bf(rng.standard_normal((1000, width)).astype(np.float32))
+    wt = bf((1 + 0.1 * rng.standard_normal(width)).astype(np.float32))
+    got = gdn_layer.gated_rmsnorm(_dev(y, cuda), _dev(z, cuda), _dev(wt, cuda), 1e-6)
+    _close_bf16(got.float().cpu().numpy(), ofront.gated_rms_norm(y, z, wt, 1e-6), "gated")
