@@ -70,7 +70,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-config1", action="store_true",
-                    help="skip the config-1 chunked-prefill measurement")
+                    help="skip the config-1 chunked-prefill and GDN-front measurements")
+    ap.add_argument("--front-only", action="store_true",
+                    help="only time one GDN layer run from its projections (fused glue) "
+                         "against the plain state update, with --batch rows; prints a JSON "
+                         "object (a profiling entry, not a bench line)")
     ap.add_argument("--config", type=int, choices=(3, 4), default=3,
                     help="3: ragged batch decode step (default); 4: one long sequence with its "
                          "KV pages split across the GPUs")
@@ -389,9 +393,10 @@ def run_ours(args, world, rank, local):
     peaks = measured_peaks()
     hbm = peaks["hbm_gbs"]
 
-    prefill_c1 = None
+    prefill_c1 = front = None
     if not args.no_config1 and rank == 0:
         prefill_c1 = config1_prefill(device)
+        front = gdn_front_layer(device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -452,10 +457,84 @@ def run_ours(args, world, rank, local):
         line["e2e"] = e2e
     if prefill_c1 is not None:
         line["config1_prefill"] = prefill_c1
+    if front is not None:
+        line["gdn_front"] = front
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
     return line
+
+
+def gdn_front_layer(device, batch: int = 256, rounds: int = 5) -> dict:
+    """A config-3 GDN layer run from its projections: the fused front kernel
+    (conv taps + SiLU + q/k norm + gates + state update + gated norm, one launch)
+    beside the plain state update over the same rows. Four layers' states rotate
+    (2 GiB > L2). Algorithmic bytes per fused launch: per row the state read and
+    written, qkv, z, a, b, three tap rows read and one written, the output; plus
+    the layer's weights once."""
+    import torch
+
+    from shellsmith_b200 import gdn_layer, numerics
+    from shellsmith_b200.workloads import gdn_token_inputs_device
+
+    B, Hk, Hv, d, layers = batch, 16, 32, 128, 4
+    C = (2 * Hk + Hv) * d
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5)
+    states = [torch.zeros((B, Hv, d, d), dtype=torch.float32, device=device)
+              for _ in range(layers)]
+    taps = [torch.zeros((B, gdn_layer.RING, C), dtype=torch.bfloat16, device=device)
+            for _ in range(layers)]
+    weights = [gdn_layer.GDNWeights(
+        conv_w=(torch.randn((C, 4), generator=gen, device=device) * 0.5).to(torch.bfloat16),
+        a_log=torch.rand(Hv, generator=gen, device=device) * 2.7,
+        dt_bias=torch.randn(Hv, generator=gen, device=device),
+        norm_w=torch.ones(d, dtype=torch.bfloat16, device=device), eps=1e-6,
+        key_heads=Hk, value_heads=Hv) for _ in range(layers)]
+    qkv = torch.randn((B, C), generator=gen, device=device).to(torch.bfloat16)
+    z = torch.randn((B, Hv * d), generator=gen, device=device).to(torch.bfloat16)
+    a = torch.randn((B, Hv), generator=gen, device=device).to(torch.bfloat16)
+    b = torch.randn((B, Hv), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((B, Hv * d), dtype=torch.bfloat16, device=device)
+    q, k, v, decay, beta = gdn_token_inputs_device(gen, B, Hk, Hv, d, d, device=device)
+    out3 = out.view(B, Hv, d)
+    pos = torch.full((B,), 5, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def fused(i):
+        gdn_layer.gdn_decode_fused(qkv, z, a, b, weights[i], taps[i], pos, states[i], out=out)
+
+    def plain(i):
+        numerics.gdn_decode(q, k, v, decay, beta, states[i], out=out3)
+
+    result = {}
+    for name, fn in (("fused", fused), ("plain", plain)):
+        for i in range(layers):
+            fn(i)
+        events = []
+        for _ in range(rounds):
+            for i in range(layers):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn(i)
+                e1.record(stream)
+                events.append((e0, e1))
+        torch.cuda.synchronize()
+        result[name] = statistics.median(x.elapsed_time(y) for x, y in events)
+    state_rw = 2 * Hv * d * d * 4
+    fused_bytes = B * (state_rw + C * 2 + Hv * d * 2 + 2 * Hv * 2 + 4 * C * 2 + Hv * d * 2) + (
+        C * 4 * 2 + Hv * 8 + d * 2)
+    plain_bytes = B * (state_rw + (2 * Hk * d + 2 * Hv * d) * 2 + 2 * Hv * 4)
+    peaks = measured_peaks()
+    gbs = fused_bytes / (result["fused"] / 1e3) / 1e9
+    return {"workload": f"config3 GDN layer from projections, B={B}, Hk16/Hv32 128x128 fp32 "
+                        f"state, conv K=4 tap ring",
+            "fused_ms": round(result["fused"], 4), "plain_update_ms": round(result["plain"], 4),
+            "fused_gbs": round(gbs, 1), "fused_frac": round(gbs / peaks["hbm_gbs"], 4),
+            "plain_gbs": round(plain_bytes / (result["plain"] / 1e3) / 1e9, 1),
+            "bytes_per_launch": fused_bytes, "launches": rounds * layers,
+            "note": "fused = the whole GDN glue of bf16.py:44-139 around the update in one "
+                    "launch; plain = the state update alone on pre-made q/k/v/g/beta"}
 
 
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:
@@ -755,6 +834,11 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.front_only:
+            import torch
+
+            print(json.dumps(gdn_front_layer(torch.device("cuda", local), batch=args.batch)),
+                  flush=True)
         elif args.config == 4:
             run_config4(args, world, rank, local)
         else:

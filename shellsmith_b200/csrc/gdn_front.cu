@@ -148,7 +148,19 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(128)
     }
   }
 
-  // ---- front, while the state chunks land
+  // ---- front, while the state chunks land. Every global load of the CTA is
+  // issued here, so under a saturated memory system it pays one round trip.
+  constexpr int kRowsCta = kFChunks * kFRows;
+  const int row_out = half * kRowsCta + (tid & (kRowsCta - 1));
+  const float z_row = bf16_to_f(z[(size_t)bh * kHead + row_out]);
+  const float w_row = bf16_to_f(norm_w[row_out]);
+  float ga = 0.f, gb = 0.f, galog = 0.f, gdt = 0.f;
+  if (tid == 0) {
+    ga = bf16_to_f(a_in[bh]);
+    gb = bf16_to_f(b_in[bh]);
+    galog = a_log[h];
+    gdt = dt_bias[h];
+  }
   const uint16_t* xrow = qkv + (size_t)b * C;
   uint16_t* ring = taps + (size_t)slot * kRing * C;
   const size_t r0 = (size_t)((t - 3) & 3) * C, r1 = (size_t)((t - 2) & 3) * C,
@@ -175,8 +187,7 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(128)
     ring[rw + cv] = xv;
     sm.o[tid] = 0.f;
   }
-  if (tid == 0) make_gates(bf16_to_f(a_in[bh]), bf16_to_f(b_in[bh]), a_log[h], dt_bias[h],
-                           sm.gate[0], sm.gate[1]);
+  if (tid == 0) make_gates(ga, gb, galog, gdt, sm.gate[0], sm.gate[1]);
   {
     const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
     if (lane == 0) {
@@ -243,12 +254,10 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(128)
   cluster_wait();
   const float total = sm.part + ld_peer_f32(&sm.part, cluster_rank() ^ 1u);
   cluster_arrive();  // this CTA is done reading the peer's shared memory
-  if (tid < kFChunks * kFRows) {
-    const int row = half * kFChunks * kFRows + tid;
+  if (tid < kRowsCta) {
     const float rstd = 1.f / sqrtf(total * (1.f / kHead) + eps);
-    const float nrm = bfr(sm.o[tid] * rstd * bf16_to_f(norm_w[row]));
-    const float gate = silu_bf(bf16_to_f(z[(size_t)bh * kHead + row]));
-    out[(size_t)bh * kHead + row] = f_to_bf16(nrm * gate);
+    const float nrm = bfr(sm.o[tid] * rstd * w_row);
+    out[(size_t)bh * kHead + row_out] = f_to_bf16(nrm * silu_bf(z_row));
   }
   if (tid == 0) {
     if (!ok && !aborted) {

@@ -24,7 +24,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from . import numerics, paged
+from . import gdn_layer, numerics, paged
 from .block_manager import BlockManager
 
 
@@ -46,6 +46,7 @@ class HybridConfig:
     state_dtype: torch.dtype = torch.float32
     pages_per_split: int | None = None   # None: adapt to the batch (paged.split_plan)
     snapshot_rows: int = 0               # extra GDN state rows for prefix snapshots
+    gdn_taps: bool = False               # keep conv tap rings (layers run with their glue)
 
     def is_attention(self, layer: int) -> bool:
         return layer % self.attention_every == self.attention_every - 1
@@ -86,6 +87,10 @@ class HybridCacheEngine:
                                   cfg.value_dim, cfg.key_dim), dtype=cfg.state_dtype, device=dev)
         self._free_snapshot_rows = list(range(cfg.max_seqs + cfg.snapshot_rows - 1,
                                               cfg.max_seqs - 1, -1))
+        # Conv tap rings [n_gdn, rows, 4, C] (gdn_layer): rows as the state's.
+        channels = (2 * cfg.gdn_key_heads * cfg.key_dim + cfg.gdn_value_heads * cfg.value_dim)
+        self.taps = (torch.zeros((n_gdn, self.state.shape[1], gdn_layer.RING, channels),
+                                 dtype=torch.bfloat16, device=dev) if cfg.gdn_taps else None)
         self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads, 2, cfg.page_size,
                                cfg.head_dim), dtype=torch.bfloat16, device=dev)
         self.blocks = BlockManager(cfg.num_pages, cfg.page_size, cfg.max_seqs,
@@ -97,10 +102,12 @@ class HybridCacheEngine:
         self._h_ctx = torch.zeros(cfg.max_seqs, dtype=torch.int32, pin_memory=True)
         self._h_slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, pin_memory=True)
         self._h_state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, pin_memory=True)
+        self._h_position = torch.zeros(cfg.max_seqs, dtype=torch.int32, pin_memory=True)
         self.table = torch.zeros_like(self._h_table, device=dev)
         self.ctx_len = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
         self.slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, device=dev)
         self.state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, device=dev)
+        self.position = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
         self._staged = torch.cuda.Event()
         self._staged.record()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
@@ -116,7 +123,15 @@ class HybridCacheEngine:
         """Reserve a slot and pages for a prompt; its GDN state starts at zero."""
         slot = self.blocks.admit(owner, prompt_len)
         self.state[:, slot].zero_()
+        if self.taps is not None:
+            self.taps[:, slot].zero_()
         return slot
+
+    def _copy_rows(self, dst: int, src: int) -> None:
+        """GDN state (and tap ring) row src -> dst in every GDN layer."""
+        self.state[:, dst].copy_(self.state[:, src])
+        if self.taps is not None:
+            self.taps[:, dst].copy_(self.taps[:, src])
 
     def release(self, slot: int) -> None:
         self.blocks.release(slot)
@@ -162,7 +177,7 @@ class HybridCacheEngine:
         tokens = int(self.blocks.lengths[slot])
         pages = self._share_prefix(self.blocks.pages[slot], tokens, copy_partial=True)
         row = self._free_snapshot_rows.pop()
-        self.state[:, row].copy_(self.state[:, slot])
+        self._copy_rows(row, slot)
         return PagedSnapshot(self, pages, tokens, row)
 
     def fork(self, snap: "PagedSnapshot", owner=None) -> int:
@@ -170,7 +185,7 @@ class HybridCacheEngine:
         partial last page copied (the fork appends to it), the GDN state copied."""
         pages = self._share_prefix(snap.pages, snap.tokens, copy_partial=True)
         slot = self.blocks.adopt(owner, pages, snap.tokens)
-        self.state[:, slot].copy_(self.state[:, snap.row])
+        self._copy_rows(slot, snap.row)
         return slot
 
     def copy_snapshot(self, snap: "PagedSnapshot") -> "PagedSnapshot":
@@ -179,7 +194,7 @@ class HybridCacheEngine:
             raise MemoryError("no free snapshot state row")
         pages = self._share_prefix(snap.pages, snap.tokens, copy_partial=False)
         row = self._free_snapshot_rows.pop()
-        self.state[:, row].copy_(self.state[:, snap.row])
+        self._copy_rows(row, snap.row)
         return PagedSnapshot(self, pages, snap.tokens, row)
 
     def drop_snapshot(self, snap: "PagedSnapshot") -> None:
@@ -196,6 +211,8 @@ class HybridCacheEngine:
         kv = tokens * c.kv_heads * c.head_dim * 2 * 2 * len(c.attention_layers)
         elem = torch.finfo(c.state_dtype).bits // 8
         st = c.gdn_value_heads * c.value_dim * c.key_dim * elem * len(c.gdn_layers)
+        if self.taps is not None:
+            st += self.taps.shape[2] * self.taps.shape[3] * 2 * len(c.gdn_layers)
         return int(kv + st)
 
     def prefill(self, new: list, gdn_inputs, kv_inputs, out=None) -> int:
@@ -255,12 +272,14 @@ class HybridCacheEngine:
         state_slot = np.full(self.cfg.max_seqs, -1, np.int32)
         state_slot[active] = active
         self._h_state_slot.numpy()[:] = state_slot
+        self._h_position.numpy()[:] = np.maximum(blocks.lengths - 1, 0).astype(np.int32)
         self.max_pages_in_batch = max(1, int(blocks.pages_for(blocks.lengths.max())))
         self.total_pages = int(np.ceil(blocks.lengths[active] / self.cfg.page_size).sum())
         self.table.copy_(self._h_table, non_blocking=True)
         self.ctx_len.copy_(self._h_ctx, non_blocking=True)
         self.slot_map.copy_(self._h_slot_map, non_blocking=True)
         self.state_slot.copy_(self._h_state_slot, non_blocking=True)
+        self.position.copy_(self._h_position, non_blocking=True)
         self._staged.record()
         return len(active)
 
@@ -268,6 +287,42 @@ class HybridCacheEngine:
     def gdn_layer(self, layer: int, q, k, v, decay, beta, out) -> None:
         numerics.gdn_decode(q, k, v, decay, beta, self.state[self.gdn_index[layer]],
                             self.state_slot, out=out)
+
+    def gdn_layer_front(self, layer: int, qkv, z, a, b, weights, out) -> None:
+        """A GDN layer from its projections: conv taps, q/k norm, gates, state update
+        and gated norm in one launch (gdn_layer.gdn_decode_fused)."""
+        i = self.gdn_index[layer]
+        gdn_layer.gdn_decode_fused(qkv, z, a, b, weights, self.taps[i], self.position,
+                                   self.state[i], self.state_slot, out=out)
+
+    def prefill_front(self, new: list, front_inputs, kv_inputs, out=None) -> int:
+        """prefill() for layers run from their projections: front_inputs(layer, ntok)
+        -> (qkv, z, a, b, weights) packed in `new` order; GDN layers run front,
+        chunked recurrence, gated norm and tap store (gdn_layer.gdn_prefill)."""
+        if not new:
+            return 0
+        spans = [(e[0], 0, e[1]) if len(e) == 2 else tuple(e) for e in new]
+        lengths = [stop - start for _, start, stop in spans]
+        total = int(sum(lengths))
+        dev = self.device
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32), device=dev)
+        slots = torch.tensor([s for s, _, _ in spans], dtype=torch.int32, device=dev)
+        starts = torch.tensor([a for _, a, _ in spans], dtype=torch.int32, device=dev)
+        kv_slots = torch.from_numpy(np.concatenate(
+            [self.blocks.prompt_slots(s, a, b) for s, a, b in spans])).to(dev)
+        launched = 0
+        for layer in range(self.cfg.layers):
+            if self.cfg.is_attention(layer):
+                k, v = kv_inputs(layer, total)
+                paged.kv_append(k, v, self.kv[self.attn_index[layer]], kv_slots)
+                launched += 1
+            else:
+                qkv, z, a, b, weights = front_inputs(layer, total)
+                i = self.gdn_index[layer]
+                gdn_layer.gdn_prefill(qkv, z, a, b, weights, self.taps[i], self.state[i], cu,
+                                      slots, starts, out=None if out is None else out[:total])
+                launched += 4
+        return launched
 
     def attention_layer(self, layer: int, q, k_new, v_new, out) -> None:
         pool = self.kv[self.attn_index[layer]]

@@ -193,6 +193,9 @@ def gated_rmsnorm(y: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: f
     require_cuda("weight", weight, torch.bfloat16, 1, align=8)
     if out is None:
         out = torch.empty_like(y)
+    if (out.dtype != torch.bfloat16 or not out.is_cuda or not out.is_contiguous()
+            or out.numel() != y.numel()):
+        raise ValueError("gated_rmsnorm: out must be a contiguous CUDA bf16 tensor like y")
     _capi.call("sc_gated_rmsnorm", ptr(y), ptr(z), ptr(weight), float(eps), ptr(out),
                y.numel() // width, width, stream_of(y))
     return out

@@ -222,3 +222,91 @@ def test_gated_rmsnorm_matches_oracle(cuda, width):
     wt = bf((1 + 0.1 * rng.standard_normal(width)).astype(np.float32))
     got = gdn_layer.gated_rmsnorm(_dev(y, cuda), _dev(z, cuda), _dev(wt, cuda), 1e-6)
     _close_bf16(got.float().cpu().numpy(), ofront.gated_rms_norm(y, z, wt, 1e-6), "gated")
+
+
+def test_engine_runs_layers_from_projections_and_forks_taps(cuda):
+    """HybridCacheEngine with tap rings: prefill two prompts from their projections,
+    decode two steps, snapshot one sequence and fork it; the fork's next step equals
+    the original's next step on the same inputs (state, taps and output)."""
+    from shellsmith_b200.engine import HybridCacheEngine, HybridConfig
+
+    rng = np.random.default_rng(33)
+    Hk, Hv = 2, 4
+    cfg = HybridConfig(layers=4, gdn_key_heads=Hk, gdn_value_heads=Hv, q_heads=8, kv_heads=2,
+                       head_dim=128, max_seqs=4, num_pages=32, max_context=256,
+                       snapshot_rows=2, gdn_taps=True)
+    eng = HybridCacheEngine(cfg, device=cuda)
+    weights = {l: _weights(rng, Hk, Hv, cuda) for l in cfg.gdn_layers}
+    lengths = [21, 40]
+    slots = [eng.admit(f"s{i}", L) for i, L in enumerate(lengths)]
+    total = sum(lengths)
+    proj = {l: tuple(_dev(x, cuda) for x in _inputs(rng, (total,), Hk, Hv))
+            for l in cfg.gdn_layers}
+    kvs = {l: (torch.randn((total, 2, 128), device=cuda).to(torch.bfloat16),
+               torch.randn((total, 2, 128), device=cuda).to(torch.bfloat16))
+           for l in cfg.attention_layers}
+    eng.prefill_front(list(zip(slots, lengths)), lambda l, n: (*proj[l], weights[l][0]),
+                      lambda l, n: kvs[l])
+    ref = {}
+    offs = [0, 21, 61]
+    for l in cfg.gdn_layers:
+        for i, slot in enumerate(slots):
+            sl = slice(offs[i], offs[i + 1])
+            qkv, z, a, b = (x[sl].float().cpu().numpy() for x in proj[l])
+            _, _, taps3, s = _oracle_prefill(qkv, z, a, b, np.zeros((3, (2 * Hk + Hv) * 128),
+                                                                    np.float32),
+                                             np.zeros((Hv, 128, 128)), weights[l][1], Hk, Hv)
+            ref[l, slot] = (taps3, s)
+
+    def step(rows):
+        """One decode step: inputs for every active row; returns GDN outputs per layer."""
+        eng.begin_step()
+        outs = {}
+        for l in range(cfg.layers):
+            if cfg.is_attention(l):
+                q = torch.randn((cfg.max_seqs, 8, 128), device=cuda).to(torch.bfloat16)
+                kn = torch.randn((cfg.max_seqs, 2, 128), device=cuda).to(torch.bfloat16)
+                out = torch.empty_like(q)
+                eng.attention_layer(l, q, kn, kn, out)
+            else:
+                qkv, z, a, b = (_dev(x, cuda) for x in rows[l])
+                out = torch.empty((cfg.max_seqs, Hv * 128), dtype=torch.bfloat16, device=cuda)
+                eng.gdn_layer_front(l, qkv, z, a, b, weights[l][0], out)
+                outs[l] = out
+        return outs
+
+    for _ in range(2):
+        rows = {l: _inputs(rng, (cfg.max_seqs,), Hk, Hv) for l in cfg.gdn_layers}
+        outs = step(rows)
+        for l in cfg.gdn_layers:
+            for slot in slots:
+                taps3, s = ref[l, slot]
+                r = [x[slot:slot + 1] for x in rows[l]]
+                want, taps3, s = ofront.decode_layer(*r, taps3[None], s[None], *weights[l][1],
+                                                     1e-6, Hk, Hv)
+                ref[l, slot] = (taps3[0], s[0])
+                np.testing.assert_allclose(outs[l][slot].float().cpu().numpy(), want[0],
+                                           rtol=3e-2, atol=3e-2)
+    torch.cuda.synchronize()
+    for l in cfg.gdn_layers:
+        i = eng.gdn_index[l]
+        for slot in slots:
+            pos = int(eng.blocks.lengths[slot])
+            assert np.array_equal(gdn_layer.ring_window(eng.taps[i], slot, pos).float().cpu()
+                                  .numpy(), ref[l, slot][0])
+            assert np.abs(eng.state[i, slot].cpu().numpy() - ref[l, slot][1]).max() <= 2e-2
+
+    # Fork sequence 1 and advance both on identical inputs.
+    snap = eng.snapshot(slots[1])
+    fork = eng.fork(snap)
+    rows = {l: _inputs(rng, (cfg.max_seqs,), Hk, Hv) for l in cfg.gdn_layers}
+    for l in cfg.gdn_layers:
+        for x in rows[l]:
+            x[fork] = x[slots[1]]
+    outs = step(rows)
+    torch.cuda.synchronize()
+    for l in cfg.gdn_layers:
+        i = eng.gdn_index[l]
+        assert torch.equal(outs[l][fork], outs[l][slots[1]])
+        assert torch.equal(eng.state[i, fork], eng.state[i, slots[1]])
+        assert torch.equal(eng.taps[i, fork], eng.taps[i, slots[1]])
