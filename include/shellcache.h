@@ -28,6 +28,7 @@
 #ifndef SHELLCACHE_H
 #define SHELLCACHE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -148,21 +149,42 @@ int sc_gdn_decode_fused(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
                         const int32_t* state_slot, sc_bf16* out, int B, int Hk, int Hv,
                         int num_slots, void* stream);
 
+/* The same layer step as sc_gdn_decode_fused, in three kernels: the front over
+ * the rows (which also stores the new tap rows), the bulk-copy state update
+ * (launched as a programmatic dependent of the front, so its state loads
+ * overlap it) and the gated norm. Same arguments, plus a device workspace of
+ * at least sc_gdn_decode_glue_workspace(B, Hk, Hv) bytes, 256-byte aligned,
+ * that holds q/k/v/g/beta and the pre-norm output between the kernels.
+ * Slots must be distinct across rows (state_slot NULL: row b uses slot b). */
+size_t sc_gdn_decode_glue_workspace(int B, int Hk, int Hv);
+int sc_gdn_decode_glue(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
+                       const sc_bf16* b, const sc_bf16* conv_w, const float* A_log,
+                       const float* dt_bias, const sc_bf16* norm_w, float eps,
+                       sc_bf16* taps, const int32_t* position, float* state,
+                       const int32_t* state_slot, sc_bf16* out, void* workspace,
+                       size_t workspace_bytes, int B, int Hk, int Hv, int num_slots,
+                       void* stream);
+
 /* The same front for the packed prompt tokens of a prefill (bf16.py:44-102 with
  * L > 1): sequence s is tokens cu_seqlens[s]..cu_seqlens[s+1] of qkv [tokens, C],
  * a, b [tokens, Hv]; it continues from position seq_start[s] of state slot
  * seq_slot[s], reading that slot's tap ring for the first three tokens.
  * Writes the inputs of sc_gdn_chunk_prefill: q, k [tokens, Hk, 128],
- * v [tokens, Hv, 128] bf16, g, beta [tokens, Hv] fp32. Does not write taps. */
+ * v [tokens, Hv, 128] bf16, g, beta [tokens, Hv] fp32. With cu_seqlens it does
+ * not write taps (sc_gdn_taps_store does, afterwards). cu_seqlens may be NULL
+ * when every sequence is one token (nseq == tokens: a decode batch, seq_start =
+ * each row's position, distinct slots); then it also stores each row's input
+ * into ring row position & 3, completing the step's taps. seq_slot -1 skips. */
 int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const sc_bf16* b,
                          const sc_bf16* conv_w, const float* A_log, const float* dt_bias,
-                         const sc_bf16* taps, const int32_t* cu_seqlens,
+                         sc_bf16* taps, const int32_t* cu_seqlens,
                          const int32_t* seq_slot, const int32_t* seq_start, sc_bf16* q,
                          sc_bf16* k, sc_bf16* v, float* g, float* beta, int nseq,
                          int total_tokens, int Hk, int Hv, int num_slots, void* stream);
 
 /* After a prefill (stream-ordered after sc_gdn_prefill_front): each sequence's
- * last min(3, n) inputs into its tap ring (the new taps of bf16.py:137). */
+ * last min(3, n) inputs into its tap ring (the new taps of bf16.py:137).
+ * cu_seqlens NULL: sequence s is token s; seq_slot -1 skips a sequence. */
 int sc_gdn_taps_store(const sc_bf16* qkv, sc_bf16* taps, const int32_t* cu_seqlens,
                       const int32_t* seq_slot, const int32_t* seq_start, int nseq,
                       int channels, int num_slots, void* stream);

@@ -28,6 +28,9 @@ SIGNATURES = {
                              _I, _P],
     "sc_gdn_decode_fused": [_P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I,
                             _I, _P],
+    "sc_gdn_decode_glue_workspace": [_I, _I, _I],
+    "sc_gdn_decode_glue": [_P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P, _P, _P,
+                           ctypes.c_size_t, _I, _I, _I, _I, _P],
     "sc_gdn_prefill_front": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,
                              _I, _I, _I, _P],
     "sc_gdn_taps_store": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
@@ -44,6 +47,9 @@ SIGNATURES = {
     "sc_paged_decode_attention_noalloc": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                           _F, _P, _P, _P],
 }
+
+
+RESTYPES = {"sc_gdn_decode_glue_workspace": ctypes.c_size_t}
 
 
 class ShellcacheError(RuntimeError):
@@ -74,7 +80,7 @@ def lib() -> ctypes.CDLL:
         for name, argtypes in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         _lib = handle
     return _lib
 

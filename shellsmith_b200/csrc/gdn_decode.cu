@@ -16,6 +16,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "gdn_internal.cuh"
 
 namespace sc {
 namespace {
@@ -216,6 +217,10 @@ __global__ void __launch_bounds__(128)
                &bars[c]);
     }
   }
+  // Launched as a programmatic dependent of the kernel that makes q/k/v/g/beta,
+  // the state loads above overlap that kernel; its outputs are read only after
+  // this wait (a no-op in an ordinary launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float4 kf = load_bf16x4(k + ((size_t)b * Hk + kh) * 128 + 4 * lane);
   const float4 qf = load_bf16x4(q + ((size_t)b * Hk + kh) * 128 + 4 * lane);
   const float decay = g[bh], bt = beta[bh];
@@ -283,23 +288,9 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
   if (B == 0) return SC_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if constexpr (std::is_same<ST, float>::value) {
-    if (dk == 128 && dv % (kBulkRows * kBulkChunksPerCta) == 0) {
-      const int smem = kBulkChunksPerCta * (kBulkChunkBytes + 8) + 8;
-      static int configured[64] = {};
-      int dev = 0;
-      cudaGetDevice(&dev);
-      if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t err = cudaFuncSetAttribute(
-            gdn_decode_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (err != cudaSuccess)
-          return set_error(SC_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(err));
-        configured[dev] = 1;
-      }
-      dim3 grid(B * Hv, dv / (kBulkRows * kBulkChunksPerCta));
-      gdn_decode_bulk_kernel<<<grid, 128, smem, s>>>(q, k, v, g, beta, state, slot, out, Hk, Hv,
-                                                    dv, num_slots, device_status_word());
-      return check_launch(name);
-    }
+    if (gdn_bulk_supported(dk, dv))
+      return gdn_bulk_launch(name, q, k, v, g, beta, state, slot, out, B, Hk, Hv, dv, num_slots,
+                             s, false);
   }
   dim3 block(kWarps * 32);
 #define SC_GDN_CASE(DK_)                                                                     \
@@ -323,6 +314,43 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
 }
 
 }  // namespace
+
+bool gdn_bulk_supported(int dk, int dv) {
+  return dk == 128 && dv % (kBulkRows * kBulkChunksPerCta) == 0;
+}
+
+int gdn_bulk_launch(const char* name, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                    const float* g, const float* beta, float* state, const int32_t* slot,
+                    uint16_t* out, int B, int Hk, int Hv, int dv, int num_slots, cudaStream_t s,
+                    bool programmatic) {
+  const int smem = kBulkChunksPerCta * (kBulkChunkBytes + 8) + 8;
+  static int configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(gdn_decode_bulk_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess)
+      return set_error(SC_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(err));
+    configured[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(B * Hv, dv / (kBulkRows * kBulkChunksPerCta));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = programmatic ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, gdn_decode_bulk_kernel, q, k, v, g, beta, state, slot,
+                                       out, Hk, Hv, dv, num_slots, device_status_word());
+  if (err != cudaSuccess)
+    return set_error(SC_ERR_CUDA, "%s: launch: %s", name, cudaGetErrorString(err));
+  return check_launch(name);
+}
+
 }  // namespace sc
 
 extern "C" int sc_gdn_decode(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v, const float* g,

@@ -30,6 +30,7 @@
 // three inputs into its ring afterwards; K11 gated_rmsnorm is the output norm
 // for any number of rows.
 #include "common.cuh"
+#include "gdn_internal.cuh"
 
 namespace sc {
 namespace {
@@ -40,6 +41,7 @@ constexpr int kFRows = 32;                       // state rows per bulk chunk
 constexpr int kFChunkBytes = kFRows * kHead * 4;  // 16 KiB
 constexpr int kFChunks = 2;                      // 64 value rows per CTA
 constexpr int kTokTile = 16;                     // prefill tokens per CTA
+constexpr int kTokTileDecode = 4;                // one-token rows per CTA (decode batches)
 
 __device__ __forceinline__ float bfr(float x) { return bf16_to_f(f_to_bf16(x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
@@ -58,6 +60,17 @@ __device__ __forceinline__ float warp_sum(float x) {
 __device__ __forceinline__ float conv_silu(const uint16_t* __restrict__ w, int c, float h0,
                                            float h1, float h2, float x) {
   const uint2 wv = __ldg(reinterpret_cast<const uint2*>(w + (size_t)c * 4));
+  float y = bf16_lo(wv.x) * h0;
+  y = fmaf(bf16_hi(wv.x), h1, y);
+  y = fmaf(bf16_lo(wv.y), h2, y);
+  y = fmaf(bf16_hi(wv.y), x, y);
+  return silu_bf(bfr(y));
+}
+
+// The same with the weight row in shared memory.
+__device__ __forceinline__ float conv_silu_smem(const uint16_t* w, int c, float h0, float h1,
+                                                float h2, float x) {
+  const uint2 wv = *reinterpret_cast<const uint2*>(w + (size_t)c * 4);
   float y = bf16_lo(wv.x) * h0;
   y = fmaf(bf16_hi(wv.x), h1, y);
   y = fmaf(bf16_lo(wv.y), h2, y);
@@ -284,38 +297,60 @@ __device__ __forceinline__ Seq find_seq(const int32_t* __restrict__ cu, int nseq
 }
 
 // grid (token tiles, 2*Hk + Hv channel blocks of 128), 128 threads: thread =
-// channel of the block, looping over kTokTile tokens.
+// channel of the block, looping over TILE tokens. Without cu_seqlens (a decode
+// batch: row i is a one-token sequence at position seq_start[i], each row its
+// own slot) the kernel also stores each row's input into ring row
+// position & 3 of its slot; the reads of that row are of rows position-3..-1.
+template <int TILE>
 __global__ void __launch_bounds__(128)
     gdn_prefill_front_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ a_in,
                              const uint16_t* __restrict__ b_in,
                              const uint16_t* __restrict__ conv_w,
                              const float* __restrict__ a_log, const float* __restrict__ dt_bias,
-                             const uint16_t* __restrict__ taps, const int32_t* __restrict__ cu,
+                             uint16_t* __restrict__ taps, const int32_t* __restrict__ cu,
                              const int32_t* __restrict__ seq_slot,
                              const int32_t* __restrict__ seq_start, uint16_t* __restrict__ q_out,
                              uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out,
                              float* __restrict__ g_out, float* __restrict__ beta_out, int nseq,
                              int total, int Hk, int Hv, int num_slots, unsigned int* status) {
-  __shared__ float red[4][kTokTile];
+  __shared__ float red[4][TILE];
+  // A state update launched as this kernel's programmatic dependent may start
+  // streaming its state now; it reads this kernel's outputs only after they land.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int blk = blockIdx.y;
   const int c = blk * kHead + tid;
   const size_t C = (size_t)(2 * Hk + Hv) * kHead;
-  const int i0 = blockIdx.x * kTokTile;
+  const int i0 = blockIdx.x * TILE;
   const int kind = blk < Hk ? 0 : (blk < 2 * Hk ? 1 : 2);  // q, k, v block
-  float val[kTokTile];
+  float val[TILE];
+  // Sequence of the tile's first token by binary search, then a forward walk;
+  // without cu_seqlens token i is sequence i (a decode batch).
+  int seq = 0, seq_end = 0;
+  if (cu != nullptr && i0 < total) {
+    seq = find_seq(cu, nseq, i0).index;
+    seq_end = __ldg(cu + seq + 1);
+  }
 #pragma unroll
-  for (int j = 0; j < kTokTile; ++j) {
+  for (int j = 0; j < TILE; ++j) {
     const int i = i0 + j;
     val[j] = 0.f;
     if (i >= total) continue;
-    const Seq sq = find_seq(cu, nseq, i);
-    const int slot = __ldg(seq_slot + sq.index), start = __ldg(seq_start + sq.index);
-    if (slot < 0 || slot >= num_slots || start < 0) {
+    Seq sq;
+    if (cu == nullptr) {
+      sq = {i, 0};
+    } else {
+      while (i >= seq_end) seq_end = __ldg(cu + (++seq) + 1);
+      sq = {seq, i - __ldg(cu + seq)};
+    }
+    const int slot = seq_slot != nullptr ? __ldg(seq_slot + sq.index) : sq.index;
+    const int start = __ldg(seq_start + sq.index);
+    if (slot < 0) continue;  // an inactive row (decode batches): no history, outputs unused
+    if (slot >= num_slots || start < 0) {
       if (tid == 0) flag_device(status, DEV_BAD_INDEX);
       continue;
     }
-    const uint16_t* ring = taps + (size_t)slot * kRing * C;
+    uint16_t* ring = taps + (size_t)slot * kRing * C;
     float hist[3];
 #pragma unroll
     for (int d = 3; d >= 1; --d) {
@@ -323,16 +358,18 @@ __global__ void __launch_bounds__(128)
                         ? bf16_to_f(qkv[(size_t)(i - d) * C + c])
                         : bf16_to_f(ring[(size_t)((start + sq.pos - d) & 3) * C + c]);
     }
-    val[j] = conv_silu(conv_w, c, hist[0], hist[1], hist[2], bf16_to_f(qkv[(size_t)i * C + c]));
+    const uint16_t x = qkv[(size_t)i * C + c];
+    val[j] = conv_silu(conv_w, c, hist[0], hist[1], hist[2], bf16_to_f(x));
+    if (cu == nullptr) ring[(size_t)(start & 3) * C + c] = x;
   }
   if (kind == 2) {
     const int h = blk - 2 * Hk;
 #pragma unroll
-    for (int j = 0; j < kTokTile; ++j) {
+    for (int j = 0; j < TILE; ++j) {
       const int i = i0 + j;
       if (i < total) v_out[((size_t)i * Hv + h) * kHead + tid] = f_to_bf16(val[j]);
     }
-    if (tid < kTokTile && i0 + tid < total) {
+    if (tid < TILE && i0 + tid < total) {
       const size_t e = (size_t)(i0 + tid) * Hv + h;
       float g, beta;
       make_gates(bf16_to_f(a_in[e]), bf16_to_f(b_in[e]), a_log[h], dt_bias[h], g, beta);
@@ -342,7 +379,7 @@ __global__ void __launch_bounds__(128)
     return;
   }
 #pragma unroll
-  for (int j = 0; j < kTokTile; ++j) {
+  for (int j = 0; j < TILE; ++j) {
     const float s = warp_sum(val[j] * val[j]);
     if (lane == 0) red[warp][j] = s;
   }
@@ -351,7 +388,7 @@ __global__ void __launch_bounds__(128)
   uint16_t* dst = kind == 0 ? q_out : k_out;
   const float scale = kind == 0 ? bfr(1.f / kHead) : bfr(0.08838834764831845f);
 #pragma unroll
-  for (int j = 0; j < kTokTile; ++j) {
+  for (int j = 0; j < TILE; ++j) {
     const int i = i0 + j;
     if (i >= total) continue;
     const float m = (red[0][j] + red[1][j] + red[2][j] + red[3][j]) * (1.f / kHead);
@@ -369,12 +406,14 @@ __global__ void gdn_taps_store_kernel(const uint16_t* __restrict__ qkv, uint16_t
   const int s = blockIdx.x;
   const int c = blockIdx.y * blockDim.x + threadIdx.x;
   if (c >= C) return;
-  const int slot = seq_slot[s], start = seq_start[s];
-  if (slot < 0 || slot >= num_slots || start < 0) {
+  const int slot = seq_slot != nullptr ? seq_slot[s] : s, start = seq_start[s];
+  if (slot < 0) return;  // an inactive row
+  if (slot >= num_slots || start < 0) {
     if (c == 0) flag_device(status, DEV_BAD_INDEX);
     return;
   }
-  const int first = cu[s], n = cu[s + 1] - first;
+  const int first = cu != nullptr ? cu[s] : s;
+  const int n = cu != nullptr ? cu[s + 1] - first : 1;
   uint16_t* ring = taps + (size_t)slot * kRing * C;
   for (int p = n - 3 < 0 ? 0 : n - 3; p < n; ++p)
     ring[(size_t)((start + p) & 3) * C + c] = qkv[(size_t)(first + p) * C + c];
@@ -463,7 +502,7 @@ extern "C" int sc_gdn_decode_fused(const sc_bf16* qkv, const sc_bf16* z, const s
 
 extern "C" int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const sc_bf16* b,
                                     const sc_bf16* conv_w, const float* A_log,
-                                    const float* dt_bias, const sc_bf16* taps,
+                                    const float* dt_bias, sc_bf16* taps,
                                     const int32_t* cu_seqlens, const int32_t* seq_slot,
                                     const int32_t* seq_start, sc_bf16* q, sc_bf16* k, sc_bf16* v,
                                     float* g, float* beta, int nseq, int total_tokens, int Hk,
@@ -471,18 +510,29 @@ extern "C" int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const 
   using namespace sc;
   const char* name = "sc_gdn_prefill_front";
   if (int rc = check_heads(name, Hk, Hv)) return rc;
-  SC_REQUIRE(qkv && a && b && conv_w && A_log && dt_bias && taps && cu_seqlens && seq_slot &&
-                 seq_start && q && k && v && g && beta,
+  SC_REQUIRE(qkv && a && b && conv_w && A_log && dt_bias && taps && seq_start && q && k && v &&
+                 g && beta,
              SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE(nseq > 0 && total_tokens >= 0 && num_slots > 0, SC_ERR_INVALID,
              "%s: nseq=%d total_tokens=%d num_slots=%d", name, nseq, total_tokens, num_slots);
+  SC_REQUIRE(cu_seqlens != nullptr || nseq == total_tokens, SC_ERR_INVALID,
+             "%s: without cu_seqlens every sequence is one token (nseq=%d, tokens=%d)", name,
+             nseq, total_tokens);
   SC_REQUIRE((reinterpret_cast<uintptr_t>(conv_w) & 7) == 0, SC_ERR_INVALID,
              "%s: conv_w must be 8-byte aligned", name);
   if (total_tokens == 0) return SC_OK;
-  dim3 grid((total_tokens + kTokTile - 1) / kTokTile, 2 * Hk + Hv);
-  gdn_prefill_front_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      qkv, a, b, conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g, beta,
-      nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cu_seqlens == nullptr) {
+    dim3 grid((total_tokens + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
+    gdn_prefill_front_kernel<kTokTileDecode><<<grid, 128, 0, s>>>(
+        qkv, a, b, conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g,
+        beta, nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
+  } else {
+    dim3 grid((total_tokens + kTokTile - 1) / kTokTile, 2 * Hk + Hv);
+    gdn_prefill_front_kernel<kTokTile><<<grid, 128, 0, s>>>(
+        qkv, a, b, conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g,
+        beta, nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
+  }
   return check_launch(name);
 }
 
@@ -491,8 +541,7 @@ extern "C" int sc_gdn_taps_store(const sc_bf16* qkv, sc_bf16* taps, const int32_
                                  int channels, int num_slots, void* stream) {
   using namespace sc;
   const char* name = "sc_gdn_taps_store";
-  SC_REQUIRE(qkv && taps && cu_seqlens && seq_slot && seq_start, SC_ERR_INVALID,
-             "%s: null pointer", name);
+  SC_REQUIRE(qkv && taps && seq_start, SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE(nseq >= 0 && channels > 0 && num_slots > 0, SC_ERR_INVALID,
              "%s: nseq=%d channels=%d num_slots=%d", name, nseq, channels, num_slots);
   if (nseq == 0) return SC_OK;
@@ -516,5 +565,66 @@ extern "C" int sc_gated_rmsnorm(const sc_bf16* y, const sc_bf16* z, const sc_bf1
   const long long blocks = (rows + 7) / 8;
   gated_rmsnorm_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       y, z, w, eps, out, rows, width);
+  return check_launch(name);
+}
+
+namespace {
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+}  // namespace
+
+extern "C" size_t sc_gdn_decode_glue_workspace(int B, int Hk, int Hv) {
+  if (B <= 0 || Hk <= 0 || Hv <= 0) return 0;
+  const size_t qk = align256((size_t)B * Hk * 128 * 2), vy = align256((size_t)B * Hv * 128 * 2);
+  const size_t gb = align256((size_t)B * Hv * 4);
+  return 2 * qk + 2 * vy + 2 * gb;
+}
+
+extern "C" int sc_gdn_decode_glue(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
+                                  const sc_bf16* b, const sc_bf16* conv_w, const float* A_log,
+                                  const float* dt_bias, const sc_bf16* norm_w, float eps,
+                                  sc_bf16* taps, const int32_t* position, float* state,
+                                  const int32_t* state_slot, sc_bf16* out, void* workspace,
+                                  size_t workspace_bytes, int B, int Hk, int Hv, int num_slots,
+                                  void* stream) {
+  using namespace sc;
+  const char* name = "sc_gdn_decode_glue";
+  if (int rc = check_heads(name, Hk, Hv)) return rc;
+  SC_REQUIRE(qkv && z && a && b && conv_w && A_log && dt_bias && norm_w && taps && position &&
+                 state && out && workspace,
+             SC_ERR_INVALID, "%s: null pointer", name);
+  SC_REQUIRE(B >= 0 && num_slots > 0 && (state_slot != nullptr || num_slots >= B), SC_ERR_INVALID,
+             "%s: B=%d num_slots=%d", name, B, num_slots);
+  SC_REQUIRE(eps >= 0.f, SC_ERR_INVALID, "%s: eps=%g", name, (double)eps);
+  SC_REQUIRE((reinterpret_cast<uintptr_t>(conv_w) & 7) == 0 &&
+                 ((reinterpret_cast<uintptr_t>(z) | reinterpret_cast<uintptr_t>(norm_w) |
+                   reinterpret_cast<uintptr_t>(out)) & 7) == 0,
+             SC_ERR_INVALID, "%s: conv_w, z, norm_w and out must be 8-byte aligned", name);
+  SC_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, SC_ERR_INVALID,
+             "%s: workspace must be 256-byte aligned", name);
+  if (B == 0) return SC_OK;
+  const size_t need = sc_gdn_decode_glue_workspace(B, Hk, Hv);
+  SC_REQUIRE(workspace_bytes >= need, SC_ERR_INVALID, "%s: workspace %zu bytes < %zu", name,
+             workspace_bytes, need);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  const size_t qk = align256((size_t)B * Hk * 128 * 2), vy = align256((size_t)B * Hv * 128 * 2);
+  const size_t gb = align256((size_t)B * Hv * 4);
+  uint16_t* q = reinterpret_cast<uint16_t*>(w);
+  uint16_t* k = reinterpret_cast<uint16_t*>(w + qk);
+  uint16_t* v = reinterpret_cast<uint16_t*>(w + 2 * qk);
+  uint16_t* y = reinterpret_cast<uint16_t*>(w + 2 * qk + vy);
+  float* g = reinterpret_cast<float*>(w + 2 * qk + 2 * vy);
+  float* beta = reinterpret_cast<float*>(w + 2 * qk + 2 * vy + gb);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dim3 grid((B + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
+  gdn_prefill_front_kernel<kTokTileDecode><<<grid, 128, 0, s>>>(
+      qkv, a, b, conv_w, A_log, dt_bias, taps, nullptr, state_slot, position, q, k, v, g, beta, B,
+      B, Hk, Hv, num_slots, device_status_word());
+  if (int rc = check_launch(name)) return rc;
+  if (int rc = gdn_bulk_launch(name, q, k, v, g, beta, state, state_slot, y, B, Hk, Hv, 128,
+                               num_slots, s, true))
+    return rc;
+  const long long rows = (long long)B * Hv;
+  gated_rmsnorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(y, z, norm_w, eps, out, rows,
+                                                                  128);
   return check_launch(name);
 }

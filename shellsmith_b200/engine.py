@@ -47,6 +47,7 @@ class HybridConfig:
     pages_per_split: int | None = None   # None: adapt to the batch (paged.split_plan)
     snapshot_rows: int = 0               # extra GDN state rows for prefix snapshots
     gdn_taps: bool = False               # keep conv tap rings (layers run with their glue)
+    gdn_glue_fused: bool = False         # one-launch cluster kernel instead of the 3-kernel step
 
     def is_attention(self, layer: int) -> bool:
         return layer % self.attention_every == self.attention_every - 1
@@ -91,6 +92,7 @@ class HybridCacheEngine:
         channels = (2 * cfg.gdn_key_heads * cfg.key_dim + cfg.gdn_value_heads * cfg.value_dim)
         self.taps = (torch.zeros((n_gdn, self.state.shape[1], gdn_layer.RING, channels),
                                  dtype=torch.bfloat16, device=dev) if cfg.gdn_taps else None)
+        self._glue_ws = None
         self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads, 2, cfg.page_size,
                                cfg.head_dim), dtype=torch.bfloat16, device=dev)
         self.blocks = BlockManager(cfg.num_pages, cfg.page_size, cfg.max_seqs,
@@ -290,10 +292,18 @@ class HybridCacheEngine:
 
     def gdn_layer_front(self, layer: int, qkv, z, a, b, weights, out) -> None:
         """A GDN layer from its projections: conv taps, q/k norm, gates, state update
-        and gated norm in one launch (gdn_layer.gdn_decode_fused)."""
+        and gated norm (gdn_layer.gdn_decode_split: three kernels, the state update
+        overlapping the front; or gdn_decode_fused, one launch)."""
         i = self.gdn_index[layer]
-        gdn_layer.gdn_decode_fused(qkv, z, a, b, weights, self.taps[i], self.position,
-                                   self.state[i], self.state_slot, out=out)
+        if self.cfg.gdn_glue_fused:
+            gdn_layer.gdn_decode_fused(qkv, z, a, b, weights, self.taps[i], self.position,
+                                       self.state[i], self.state_slot, out=out)
+            return
+        if self._glue_ws is None:
+            self._glue_ws = gdn_layer.SplitWorkspace(self.cfg.max_seqs, weights, self.device)
+        gdn_layer.gdn_decode_split(qkv, z, a, b, weights, self.taps[i], self.position,
+                                   self.state[i], self.state_slot, out=out,
+                                   workspace=self._glue_ws)
 
     def prefill_front(self, new: list, front_inputs, kv_inputs, out=None) -> int:
         """prefill() for layers run from their projections: front_inputs(layer, ntok)

@@ -86,6 +86,37 @@ def ring_window(taps: torch.Tensor, slot: int, position: int) -> torch.Tensor:
     return taps[slot, rows]
 
 
+def _check_decode(qkv, z, a, b, weights, taps, position, state, state_slot) -> tuple:
+    """Validate one decode step's operands; returns (B, C, Hk, Hv, slots)."""
+    weights.check()
+    B, C = qkv.shape
+    Hk, Hv = weights.key_heads, weights.value_heads
+    require_cuda("qkv", qkv, torch.bfloat16, 2, align=2)
+    require_cuda("z", z, torch.bfloat16, 2, align=2)
+    for name, t in (("a", a), ("b", b)):
+        require_cuda(name, t, torch.bfloat16, 2, align=2)
+        if tuple(t.shape) != (B, Hv):
+            raise ValueError(f"gdn decode: {name} must be [{B}, {Hv}]")
+    if C != weights.channels or tuple(z.shape) != (B, Hv * HEAD):
+        raise ValueError("gdn decode: qkv must be [B, C] and z [B, Hv*128]")
+    require_cuda("taps", taps, torch.bfloat16, 3, align=2)
+    require_cuda("state", state, torch.float32, 4)
+    slots = state.shape[0]
+    if tuple(taps.shape) != (slots, RING, C) or tuple(state.shape[1:]) != (Hv, HEAD, HEAD):
+        raise ValueError(f"gdn decode: taps must be [{slots}, 4, {C}], "
+                         f"state [{slots}, {Hv}, 128, 128]")
+    require_cuda("position", position, torch.int32, 1, align=4)
+    if position.shape[0] != B:
+        raise ValueError("gdn decode: one position per row")
+    if state_slot is not None:
+        require_cuda("state_slot", state_slot, torch.int32, 1, align=4)
+        if state_slot.shape[0] != B:
+            raise ValueError("gdn decode: one state slot per row")
+    elif slots < B:
+        raise ValueError("gdn decode: fewer state slots than rows")
+    return B, C, Hk, Hv, slots
+
+
 def gdn_decode_fused(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                      weights: GDNWeights, taps: torch.Tensor, position: torch.Tensor,
                      state: torch.Tensor, state_slot: torch.Tensor | None = None,
@@ -97,32 +128,8 @@ def gdn_decode_fused(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: tor
     (absolute position of each row's token); state_slot [B] int32 (-1 skips a
     row) or None (row b uses slot b). Returns out [B, Hv*128] bf16.
     """
-    weights.check()
-    B, C = qkv.shape
-    Hk, Hv = weights.key_heads, weights.value_heads
-    require_cuda("qkv", qkv, torch.bfloat16, 2, align=2)
-    require_cuda("z", z, torch.bfloat16, 2, align=2)
-    for name, t in (("a", a), ("b", b)):
-        require_cuda(name, t, torch.bfloat16, 2, align=2)
-        if tuple(t.shape) != (B, Hv):
-            raise ValueError(f"gdn_decode_fused: {name} must be [{B}, {Hv}]")
-    if C != weights.channels or tuple(z.shape) != (B, Hv * HEAD):
-        raise ValueError("gdn_decode_fused: qkv must be [B, C] and z [B, Hv*128]")
-    require_cuda("taps", taps, torch.bfloat16, 3, align=2)
-    require_cuda("state", state, torch.float32, 4)
-    slots = state.shape[0]
-    if tuple(taps.shape) != (slots, RING, C) or tuple(state.shape[1:]) != (Hv, HEAD, HEAD):
-        raise ValueError(f"gdn_decode_fused: taps must be [{slots}, 4, {C}], "
-                         f"state [{slots}, {Hv}, 128, 128]")
-    require_cuda("position", position, torch.int32, 1, align=4)
-    if position.shape[0] != B:
-        raise ValueError("gdn_decode_fused: one position per row")
-    if state_slot is not None:
-        require_cuda("state_slot", state_slot, torch.int32, 1, align=4)
-        if state_slot.shape[0] != B:
-            raise ValueError("gdn_decode_fused: one state slot per row")
-    elif slots < B:
-        raise ValueError("gdn_decode_fused: fewer state slots than rows")
+    B, C, Hk, Hv, slots = _check_decode(qkv, z, a, b, weights, taps, position, state,
+                                        state_slot)
     if out is None:
         out = torch.empty((B, Hv * HEAD), dtype=torch.bfloat16, device=qkv.device)
     require_cuda("out", out, torch.bfloat16, 2, align=2)
@@ -130,6 +137,40 @@ def gdn_decode_fused(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: tor
                ptr(weights.a_log), ptr(weights.dt_bias), ptr(weights.norm_w), weights.eps,
                ptr(taps), ptr(position), ptr(state), ptr(state_slot), ptr(out), B, Hk, Hv, slots,
                stream_of(qkv))
+    return out
+
+
+class SplitWorkspace:
+    """Device workspace of the three-kernel decode step for up to `rows` rows (reused
+    per call, so a captured CUDA graph sees fixed addresses)."""
+
+    def __init__(self, rows: int, weights: "GDNWeights", device="cuda"):
+        self.rows = rows
+        self.nbytes = int(_capi.lib().sc_gdn_decode_glue_workspace(rows, weights.key_heads,
+                                                                    weights.value_heads))
+        self.buffer = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+
+
+def gdn_decode_split(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                     weights: GDNWeights, taps: torch.Tensor, position: torch.Tensor,
+                     state: torch.Tensor, state_slot: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None,
+                     workspace: SplitWorkspace | None = None) -> torch.Tensor:
+    """gdn_decode_fused's result in three kernels (sc_gdn_decode_glue): the front over
+    the rows (each a one-token sequence at its position; it also stores the new tap
+    rows), the bulk-copy state update launched as its programmatic dependent (its
+    state loads overlap the front) and the gated norm. Rows' slots must differ."""
+    B, _, Hk, Hv, slots = _check_decode(qkv, z, a, b, weights, taps, position, state,
+                                        state_slot)
+    ws = workspace if workspace is not None and workspace.rows >= B else SplitWorkspace(
+        B, weights, qkv.device)
+    if out is None:
+        out = torch.empty((B, Hv * HEAD), dtype=torch.bfloat16, device=qkv.device)
+    require_cuda("out", out, torch.bfloat16, 2, align=8)
+    _capi.call("sc_gdn_decode_glue", ptr(qkv), ptr(z), ptr(a), ptr(b), ptr(weights.conv_w),
+               ptr(weights.a_log), ptr(weights.dt_bias), ptr(weights.norm_w), weights.eps,
+               ptr(taps), ptr(position), ptr(state), ptr(state_slot), ptr(out), ptr(ws.buffer),
+               ws.nbytes, B, Hk, Hv, slots, stream_of(qkv))
     return out
 
 
@@ -172,7 +213,8 @@ def gdn_prefill_front(qkv: torch.Tensor, a: torch.Tensor, b: torch.Tensor, weigh
 
 def gdn_taps_store(qkv: torch.Tensor, taps: torch.Tensor, cu_seqlens: torch.Tensor,
                    seq_slot: torch.Tensor, seq_start: torch.Tensor) -> None:
-    """Each prompt's last min(3, n) inputs into its slot's tap ring."""
+    """Each prompt's last min(3, n) inputs into its slot's tap ring (cu_seqlens None:
+    sequence s is token s, a decode batch)."""
     require_cuda("qkv", qkv, torch.bfloat16, 2, align=2)
     require_cuda("taps", taps, torch.bfloat16, 3, align=2)
     if taps.shape[2] != qkv.shape[1] or taps.shape[1] != RING:

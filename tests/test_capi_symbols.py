@@ -14,7 +14,7 @@ def _declared():
     names = set()
     for header in (ROOT / "include").glob("*.h"):
         text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
-        names.update(re.findall(r"\bint\s+(sc_\w+)\s*\(", text))
+        names.update(re.findall(r"\b(?:int|size_t)\s+(sc_\w+)\s*\(", text))
     return names
 
 
@@ -35,6 +35,15 @@ def test_every_declared_symbol_is_exported(library):
 
 def test_every_declared_symbol_has_a_binding():
     assert _declared() == set(_capi.SIGNATURES)
+
+
+def test_workspace_size_query_without_gpu(library):
+    """sc_gdn_decode_glue_workspace is pure arithmetic: 256-byte aligned buffers for
+    q, k, v, the pre-norm output, g and beta."""
+    n = library.sc_gdn_decode_glue_workspace(256, 16, 32)
+    qk, vy, gb = 256 * 16 * 128 * 2, 256 * 32 * 128 * 2, 256 * 32 * 4
+    assert n == 2 * qk + 2 * vy + 2 * gb
+    assert library.sc_gdn_decode_glue_workspace(0, 16, 32) == 0
 
 
 def test_version_and_error_text_without_gpu(library):

@@ -61,8 +61,12 @@ def _close_bf16(got, want, name):
     assert near.mean() <= 0.01, (name, near.mean())
 
 
-@pytest.mark.parametrize("Hk,Hv,B", [(2, 4, 3), (16, 32, 5)])
-def test_decode_fused_matches_oracle_over_steps(cuda, Hk, Hv, B):
+# B = 64 with 8 value heads: the fused form launches 1024 CTAs, more than are
+# resident at once.
+@pytest.mark.parametrize("Hk,Hv,B", [(2, 4, 3), (16, 32, 5), (2, 8, 64)])
+@pytest.mark.parametrize("path", ["fused", "split"])
+def test_decode_matches_oracle_over_steps(cuda, Hk, Hv, B, path):
+    decode = getattr(gdn_layer, f"gdn_decode_{path}")
     rng = np.random.default_rng(Hk * 10 + Hv)
     w, (conv_w, a_log, dt_bias, norm_w) = _weights(rng, Hk, Hv, cuda)
     slots = B + 2
@@ -75,8 +79,8 @@ def test_decode_fused_matches_oracle_over_steps(cuda, Hk, Hv, B):
     for step in range(5):
         qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
         pos = torch.full((B,), step, dtype=torch.int32, device=cuda)
-        out = gdn_layer.gdn_decode_fused(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda),
-                                         _dev(b, cuda), w, taps, pos, state, slot_t)
+        out = decode(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda), w, taps, pos,
+                     state, slot_t)
         want, ref_taps, ref_state = ofront.decode_layer(qkv, z, a, b, ref_taps, ref_state, conv_w,
                                                         a_log, dt_bias, norm_w, 1e-6, Hk, Hv)
         np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=3e-2, atol=3e-2)
@@ -88,9 +92,11 @@ def test_decode_fused_matches_oracle_over_steps(cuda, Hk, Hv, B):
     assert torch.count_nonzero(state[np.setdiff1d(np.arange(slots), perm)]) == 0
 
 
-def test_decode_fused_skips_rows_and_keeps_others(cuda):
+@pytest.mark.parametrize("path", ["fused", "split"])
+def test_decode_skips_rows_and_keeps_others(cuda, path):
+    Hv = 4
     rng = np.random.default_rng(4)
-    Hk, Hv, B = 2, 4, 3
+    Hk, B = 2, 3
     w, _ = _weights(rng, Hk, Hv, cuda)
     taps = gdn_layer.new_taps(4, w, device=cuda)
     state = torch.randn((4, Hv, 128, 128), device=cuda)
@@ -98,8 +104,8 @@ def test_decode_fused_skips_rows_and_keeps_others(cuda):
     qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
     slot_t = torch.tensor([2, -1, 0], dtype=torch.int32, device=cuda)
     pos = torch.tensor([7, 7, 9], dtype=torch.int32, device=cuda)
-    gdn_layer.gdn_decode_fused(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda), w,
-                               taps, pos, state, slot_t)
+    getattr(gdn_layer, f"gdn_decode_{path}")(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda),
+                                             _dev(b, cuda), w, taps, pos, state, slot_t)
     torch.cuda.synchronize()
     for s in (1, 3):
         assert torch.equal(state[s], before_state[s]) and torch.equal(taps[s], before_taps[s])
@@ -224,7 +230,8 @@ def test_gated_rmsnorm_matches_oracle(cuda, width):
     _close_bf16(got.float().cpu().numpy(), ofront.gated_rms_norm(y, z, wt, 1e-6), "gated")
 
 
-def test_engine_runs_layers_from_projections_and_forks_taps(cuda):
+@pytest.mark.parametrize("fused", [False, True])
+def test_engine_runs_layers_from_projections_and_forks_taps(cuda, fused):
     """HybridCacheEngine with tap rings: prefill two prompts from their projections,
     decode two steps, snapshot one sequence and fork it; the fork's next step equals
     the original's next step on the same inputs (state, taps and output)."""
@@ -234,7 +241,7 @@ def test_engine_runs_layers_from_projections_and_forks_taps(cuda):
     Hk, Hv = 2, 4
     cfg = HybridConfig(layers=4, gdn_key_heads=Hk, gdn_value_heads=Hv, q_heads=8, kv_heads=2,
                        head_dim=128, max_seqs=4, num_pages=32, max_context=256,
-                       snapshot_rows=2, gdn_taps=True)
+                       snapshot_rows=2, gdn_taps=True, gdn_glue_fused=fused)
     eng = HybridCacheEngine(cfg, device=cuda)
     weights = {l: _weights(rng, Hk, Hv, cuda) for l in cfg.gdn_layers}
     lengths = [21, 40]
