@@ -227,6 +227,37 @@ int sc_kv_copy_pages(sc_bf16* kv_pool, const int32_t* src, const int32_t* dst,
                      void* stream);
 
 /* --------------------------------------------------------------------------
+ * (b') 8-bit KV pages (cache_precision = "8bit").
+ *
+ * Replaces the 8-bit cache of studio_compute/inference.py:87-94 (each layer's
+ * cache made an mlx-vlm QuantizedKVCache: 8 bits, groups of 64 along D, a
+ * scale and bias per group, attention on the dequantised rows). Rule of this
+ * build (the library's own rounding is not in the reference tree):
+ *   scale = bf16((max - min) / 255), bias = bf16(min),
+ *   code = clamp(rint((w - bias) / scale), 0, 255), 0 when scale == 0.
+ * Pool: uint8 [num_pages][Hkv][34 * D] (sc_kv_q8_block_bytes(D) per page and
+ * kv head: K codes, V^T codes in the tensor-core fragment order, then K/V
+ * scale and bias [16][D/64] bf16). D in {128, 256}, P = 16. */
+int sc_kv_q8_block_bytes(int D);
+int sc_kv_append_q8(const sc_bf16* k, const sc_bf16* v, uint8_t* kv_pool,
+                    const int64_t* slot_mapping, int ntok, int Hkv, int D, int P,
+                    int64_t num_pages, void* stream);
+/* codes [ntok][Hkv][2][D] uint8 (K, V), scale_bias [ntok][Hkv][2][D/64][2] bf16. */
+int sc_kv_gather_q8(const uint8_t* kv_pool, const int64_t* slot_mapping, int ntok, int Hkv,
+                    int D, int P, int64_t num_pages, uint8_t* codes, sc_bf16* scale_bias,
+                    void* stream);
+int sc_kv_copy_pages_q8(uint8_t* kv_pool, const int32_t* src, const int32_t* dst, int npages,
+                        int Hkv, int D, int P, int64_t num_pages, void* stream);
+/* sc_paged_decode_attention over an 8-bit pool (same split plan, partials and
+ * combine); kv_pool 16-byte aligned. */
+int sc_paged_decode_attention_q8(const sc_bf16* q, const uint8_t* kv_pool, int64_t num_pages,
+                                 const int32_t* block_table, const int32_t* ctx_len, int B,
+                                 int Hq, int Hkv, int D, int P, int max_pages,
+                                 int pages_per_split, int num_splits, float scale,
+                                 float* part_out, float* part_lse, sc_bf16* out, float* lse_out,
+                                 void* stream);
+
+/* --------------------------------------------------------------------------
  * (c) Split-K paged decode attention (one query token per sequence).
  *
  * Replaces the per-request decode SDPA of studio_compute/mlx_decode.py:80-106

@@ -5,6 +5,14 @@ Restated from (paths relative to the shellsmith project root):
               (forward half): causal GQA, key j visible to query i when
               j <= query_offset + i, kv head of query head h is h // group,
               query_offset defaults to keys - queries.
+  quantize_q8 the 8-bit cache of the cache_precision="8bit" option
+              (src/studio_compute/inference.py:87-94, mlx-vlm
+              QuantizedKVCache: groups of 64 along D, scale and bias per
+              group, w = scale * code + bias). The library's own rounding is
+              not in the reference tree, so this is the build's stated rule
+              (parity unpinned): scale = bf16((max - min) / 255),
+              bias = bf16(min), code = clamp(rint((w - bias) / scale), 0, 255),
+              0 when scale == 0, each op in float32.
   The split-K partials, their combine and the paged-pool layout have no
   counterpart in the reference (it runs one request's SDPA at a time); they
   restate the algebra softmax(x) = sum_s e^{lse_s - M} softmax_s(x) / sum_s
@@ -122,3 +130,26 @@ def pool_read_pages(pool, pages, length, Hkv, P, D):
             row = pool[page, :, which, off].reshape(Hkv, D // 8, 8)
             dst[t] = row[:, perm].reshape(Hkv, D)
     return k, v
+
+
+def quantize_q8(x, group=64):
+    """x [..., D] (float32 values) -> codes uint8 [..., D], scale, bias [..., D/group]."""
+    from .gdn import bf16_round
+
+    x = np.asarray(x, np.float32)
+    g = x.reshape(*x.shape[:-1], x.shape[-1] // group, group)
+    mn, mx = g.min(axis=-1), g.max(axis=-1)
+    scale = bf16_round((mx - mn) / np.float32(255.0))
+    bias = bf16_round(mn)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        codes = np.rint((g - bias[..., None]) / scale[..., None])
+    codes = np.where(scale[..., None] > 0, np.clip(codes, 0, 255), 0).astype(np.uint8)
+    return codes.reshape(x.shape), scale, bias
+
+
+def dequantize_q8(codes, scale, bias, group=64):
+    """scale * code + bias per group, in float64."""
+    c = np.asarray(codes, np.float64)
+    g = c.reshape(*c.shape[:-1], c.shape[-1] // group, group)
+    out = g * np.asarray(scale, np.float64)[..., None] + np.asarray(bias, np.float64)[..., None]
+    return out.reshape(c.shape)

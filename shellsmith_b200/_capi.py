@@ -35,6 +35,12 @@ SIGNATURES = {
                              _I, _I, _I, _P],
     "sc_gdn_taps_store": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
     "sc_gated_rmsnorm": [_P, _P, _P, _F, _P, _I64, _I, _P],
+    "sc_kv_q8_block_bytes": [_I],
+    "sc_kv_append_q8": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
+    "sc_kv_gather_q8": [_P, _P, _I, _I, _I, _I, _I64, _P, _P, _P],
+    "sc_kv_copy_pages_q8": [_P, _P, _P, _I, _I, _I, _I, _I64, _P],
+    "sc_paged_decode_attention_q8": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
+                                     _P, _P, _P, _P, _P],
     "sc_kv_append": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_gather": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_copy_pages": [_P, _P, _P, _I, _I, _I, _I, _I64, _P],

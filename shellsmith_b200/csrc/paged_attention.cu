@@ -24,6 +24,7 @@
 
 #include <mutex>
 
+#include "attention_internal.cuh"
 #include "common.cuh"
 
 namespace sc {
@@ -442,6 +443,8 @@ __global__ void __launch_bounds__(kCombineThreads)
   }
 }
 
+}  // namespace
+
 // Launches the merge of `rows` rows of `nparts` parts: per-row CTAs for few
 // parts, (row, dim-tile) CTAs for many.
 void launch_combine(const float* po, const float* pl, size_t o_row, size_t o_part, size_t l_row,
@@ -459,6 +462,8 @@ void launch_combine(const float* po, const float* pl, size_t o_row, size_t o_par
                                                     lse_out, packed);
   }
 }
+
+namespace {
 
 // Launch shape: warps per CTA and shared-memory stages (one page each) per warp.
 #ifndef SC_ATTN_WARPS

@@ -12,6 +12,11 @@ block manager hands out pages, and these functions move and read them:
   paged_decode_attention  split-K attention of one query per sequence over
                           its ragged pages, then the (out, lse) combine
   attention_combine       merge per-part (out, lse), e.g. across GPUs
+
+8-bit pools (cache_precision "8bit"): uint8 [num_pages, Hkv, 34 * D], one
+quantised block per (page, kv head) (new_pool_q8); kv_append, kv_copy_pages
+and paged_decode_attention take either kind of pool and pick the kernels by
+its dtype; kv_gather_q8 reads codes and scales back.
 """
 
 from __future__ import annotations
@@ -33,7 +38,30 @@ def new_pool(num_pages: int, kv_heads: int, head_dim: int, page_size: int = PAGE
                        device=device)
 
 
+Q8_BYTES_PER_DIM = 34     # per (page, kv head): 2 x 16 x D codes + 4 x 16 x D/64 bf16
+
+
+def new_pool_q8(num_pages: int, kv_heads: int, head_dim: int,
+                device: str | torch.device = "cuda") -> torch.Tensor:
+    """One layer's 8-bit pool [num_pages, Hkv, 34 * D] uint8 (uninitialised)."""
+    if head_dim not in (128, 256):
+        raise ValueError("8-bit pages need D in {128, 256}")
+    return torch.empty((num_pages, kv_heads, Q8_BYTES_PER_DIM * head_dim), dtype=torch.uint8,
+                       device=device)
+
+
+def _q8_dims(kv_pool: torch.Tensor):
+    require_cuda("kv_pool", kv_pool, torch.uint8, 3, align=16)
+    num_pages, hkv, block = kv_pool.shape
+    dim = block // Q8_BYTES_PER_DIM
+    if block != Q8_BYTES_PER_DIM * dim or dim not in (128, 256):
+        raise ValueError("an 8-bit pool must be [num_pages, Hkv, 34 * D], D in {128, 256}")
+    return num_pages, hkv, PAGE_SIZE, dim
+
+
 def _pool_dims(kv_pool: torch.Tensor):
+    if kv_pool.dtype == torch.uint8:
+        return _q8_dims(kv_pool)
     require_cuda("kv_pool", kv_pool, torch.bfloat16, 5)
     num_pages, hkv, two, page, dim = kv_pool.shape
     if two != 2:
@@ -51,12 +79,28 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, kv_pool: torch.Tensor,
     ntok = k.shape[0]
     if k.shape != (ntok, hkv, dim) or v.shape != k.shape or slot_mapping.shape[0] != ntok:
         raise ValueError("kv_append: k/v must be [ntok, Hkv, D] with one slot per token")
-    _capi.call("sc_kv_append", ptr(k), ptr(v), ptr(kv_pool), ptr(slot_mapping), ntok, hkv, dim,
-               page, num_pages, stream_of(kv_pool))
+    name = "sc_kv_append_q8" if kv_pool.dtype == torch.uint8 else "sc_kv_append"
+    _capi.call(name, ptr(k), ptr(v), ptr(kv_pool), ptr(slot_mapping), ntok, hkv, dim, page,
+               num_pages, stream_of(kv_pool))
+
+
+def kv_gather_q8(kv_pool: torch.Tensor, slot_mapping: torch.Tensor) -> tuple:
+    """An 8-bit pool's tokens at slot_mapping in plain order: codes [ntok, Hkv, 2, D]
+    uint8 (K, V) and scale_bias [ntok, Hkv, 2, D/64, 2] bf16 (zeros for slots < 0)."""
+    num_pages, hkv, page, dim = _q8_dims(kv_pool)
+    require_cuda("slot_mapping", slot_mapping, torch.int64, 1, align=8)
+    ntok = slot_mapping.shape[0]
+    codes = torch.empty((ntok, hkv, 2, dim), dtype=torch.uint8, device=kv_pool.device)
+    sb = torch.empty((ntok, hkv, 2, dim // 64, 2), dtype=torch.bfloat16, device=kv_pool.device)
+    _capi.call("sc_kv_gather_q8", ptr(kv_pool), ptr(slot_mapping), ntok, hkv, dim, page,
+               num_pages, ptr(codes), ptr(sb), stream_of(kv_pool))
+    return codes, sb
 
 
 def kv_gather(kv_pool: torch.Tensor, slot_mapping: torch.Tensor) -> tuple:
     """Logical k, v [ntok, Hkv, D] stored at slot_mapping (zeros for negative slots)."""
+    if kv_pool.dtype == torch.uint8:
+        raise TypeError("kv_gather reads bf16 pools; use kv_gather_q8 for 8-bit pools")
     num_pages, hkv, page, dim = _pool_dims(kv_pool)
     require_cuda("slot_mapping", slot_mapping, torch.int64, 1, align=8)
     ntok = slot_mapping.shape[0]
@@ -74,8 +118,9 @@ def kv_copy_pages(kv_pool: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -
     require_cuda("dst", dst, torch.int32, 1, align=4)
     if src.shape != dst.shape:
         raise ValueError("kv_copy_pages: src and dst must match")
-    _capi.call("sc_kv_copy_pages", ptr(kv_pool), ptr(src), ptr(dst), src.shape[0], hkv, dim,
-               page, num_pages, stream_of(kv_pool))
+    name = "sc_kv_copy_pages_q8" if kv_pool.dtype == torch.uint8 else "sc_kv_copy_pages"
+    _capi.call(name, ptr(kv_pool), ptr(src), ptr(dst), src.shape[0], hkv, dim, page, num_pages,
+               stream_of(kv_pool))
 
 
 _SM_COUNT: dict = {}
@@ -171,9 +216,11 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
         if workspace is None or not workspace.fits(B, hq, dim, nsplit):
             workspace = AttentionWorkspace(B, hq, dim, nsplit, device=q.device)
         part_out, part_lse = workspace.views(B, nsplit)
-    _capi.call("sc_paged_decode_attention", ptr(q), ptr(kv_pool), num_pages, ptr(block_table),
-               ptr(ctx_len), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
-               ptr(part_out), ptr(part_lse), ptr(out), ptr(lse_out), stream_of(q))
+    name = ("sc_paged_decode_attention_q8" if kv_pool.dtype == torch.uint8
+            else "sc_paged_decode_attention")
+    _capi.call(name, ptr(q), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len), B, hq, hkv,
+               dim, page, max_pages, pps, nsplit, float(scale), ptr(part_out), ptr(part_lse),
+               ptr(out), ptr(lse_out), stream_of(q))
     return out
 
 
@@ -204,6 +251,8 @@ def paged_decode_attention_packed(q: torch.Tensor, kv_pool: torch.Tensor,
                                   workspace: AttentionWorkspace | None = None) -> torch.Tensor:
     """Like paged_decode_attention, but returns fp32 packed [B * Hq, D + 1]: each row's
     normalised output and, at index D, its natural-log lse (a device's partial)."""
+    if kv_pool.dtype == torch.uint8:
+        raise TypeError("paged_decode_attention_packed takes bf16 pools")
     num_pages, hkv, page, dim = _pool_dims(kv_pool)
     require_cuda("q", q, torch.bfloat16, 3)
     require_cuda("block_table", block_table, torch.int32, 2, align=4)
