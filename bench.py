@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-config1", action="store_true",
-                    help="skip the config-1 chunked-prefill and GDN-front measurements")
+                    help="skip the config-1 chunked-prefill, GDN-front and 8-bit KV measurements")
     ap.add_argument("--front-only", action="store_true",
                     help="only time one GDN layer run from its projections (fused glue) "
                          "against the plain state update, with --batch rows; prints a JSON "
@@ -393,10 +393,11 @@ def run_ours(args, world, rank, local):
     peaks = measured_peaks()
     hbm = peaks["hbm_gbs"]
 
-    prefill_c1 = front = None
+    prefill_c1 = front = kv8 = None
     if not args.no_config1 and rank == 0:
         prefill_c1 = config1_prefill(device)
         front = gdn_front_layer(device)
+        kv8 = kv8_attention_layer(wl, device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -459,6 +460,8 @@ def run_ours(args, world, rank, local):
         line["config1_prefill"] = prefill_c1
     if front is not None:
         line["gdn_front"] = front
+    if kv8 is not None:
+        line["kv8_attention"] = kv8
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -551,6 +554,65 @@ def gdn_front_layer(device, batch: int = 256, rounds: int = 5) -> dict:
                     "launch (2-CTA clusters); split = the same in three launches (front + tap "
                     "rows, update, gated norm); plain = the state update alone on "
                     "pre-made q/k/v/g/beta. GB/s use the fused bytes for both forms"}
+
+
+def kv8_attention_layer(wl, device, rounds: int = 5) -> dict:
+    """One attention layer of the step just measured (append + split-K attention
+    over the same block tables and context lengths) on 8-bit pages beside bf16
+    pages. Algorithmic bytes per launch as step_bytes, with a cached token
+    costing 2 * Hkv * D code bytes plus 8 * Hkv * D / 64 of bf16 scale and bias."""
+    import torch
+
+    from shellsmith_b200 import paged
+
+    eng, cfg = wl.engine, wl.cfg
+    layer = cfg.attention_layers[0]
+    q, k, v = wl.inputs[layer]
+    out = wl.outputs[layer]
+    D = cfg.head_dim
+    pool8 = paged.new_pool_q8(cfg.num_pages, cfg.kv_heads, D, device)
+    pool8.random_(0, 256)
+    pool8[:, :, 32 * D:].view(torch.bfloat16).fill_(0.01)   # scales and biases
+    stream = torch.cuda.current_stream(device)
+
+    def run(pool):
+        paged.kv_append(k, v, pool, eng.slot_map)
+        paged.paged_decode_attention(q, pool, eng.table, eng.ctx_len, eng.scale,
+                                     max_pages_in_batch=eng.max_pages_in_batch,
+                                     pages_per_split=cfg.pages_per_split,
+                                     total_pages=eng.total_pages, workspace=eng.workspace,
+                                     out=out)
+
+    ms = {}
+    for name, pool in (("bf16", eng.kv[eng.attn_index[layer]]), ("8bit", pool8)):
+        run(pool)
+        run(pool)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(rounds):
+            run(pool)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms[name] = e0.elapsed_time(e1) / rounds
+    del pool8
+    active = np.flatnonzero(eng.blocks.active)
+    lengths = eng.blocks.lengths[active].astype(np.float64)
+    n = len(lengths)
+    rows = {"bf16": cfg.kv_heads * D * 4, "8bit": cfg.kv_heads * (2 * D + 8 * D / 64)}
+    extra = n * cfg.q_heads * D * 4 + float(np.ceil(lengths / cfg.page_size).sum()) * 4
+    nbytes = {key: float(lengths.sum()) * r + n * r + extra for key, r in rows.items()}
+    peaks = measured_peaks()
+    gbs = {key: nbytes[key] / (ms[key] / 1e3) / 1e9 for key in ms}
+    return {"workload": f"one config-3 attention layer, {n} sequences, mean ctx "
+                        f"{lengths.mean():.0f}, Hq{cfg.q_heads}/Hkv{cfg.kv_heads} D{D}",
+            "bf16_ms": round(ms["bf16"], 4), "kv8_ms": round(ms["8bit"], 4),
+            "speedup": round(ms["bf16"] / ms["8bit"], 3),
+            "bf16_gbs": round(gbs["bf16"], 1), "kv8_gbs": round(gbs["8bit"], 1),
+            "kv8_frac": round(gbs["8bit"] / peaks["hbm_gbs"], 4),
+            "kv8_bytes_per_launch": round(nbytes["8bit"]), "launches": rounds,
+            "note": "8-bit pages hold random codes with bf16 scale/bias 0.01; timing does not "
+                    "depend on the values"}
 
 
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:

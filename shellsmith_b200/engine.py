@@ -48,6 +48,7 @@ class HybridConfig:
     snapshot_rows: int = 0               # extra GDN state rows for prefix snapshots
     gdn_taps: bool = False               # keep conv tap rings (layers run with their glue)
     gdn_glue_fused: bool = False         # one-launch cluster kernel instead of the 3-kernel step
+    kv_precision: str = "bf16"           # "8bit": quantised pages (paged.new_pool_q8)
 
     def is_attention(self, layer: int) -> bool:
         return layer % self.attention_every == self.attention_every - 1
@@ -69,9 +70,15 @@ class HybridConfig:
         return (len(self.gdn_layers) * self.max_seqs * self.gdn_value_heads * self.value_dim
                 * self.key_dim * elem)
 
+    def kv_token_bytes(self) -> float:
+        """Bytes one cached token holds per attention layer (K and V of every kv head)."""
+        if self.kv_precision == "8bit":   # codes + bf16 scale and bias per group of 64
+            return self.kv_heads * (2 * self.head_dim + 8 * self.head_dim / 64)
+        return self.kv_heads * self.head_dim * 2 * 2
+
     def kv_bytes(self) -> int:
-        return (len(self.attention_layers) * self.num_pages * self.kv_heads * 2 * self.page_size
-                * self.head_dim * 2)
+        return int(len(self.attention_layers) * self.num_pages * self.page_size
+                   * self.kv_token_bytes())
 
 
 class HybridCacheEngine:
@@ -93,8 +100,15 @@ class HybridCacheEngine:
         self.taps = (torch.zeros((n_gdn, self.state.shape[1], gdn_layer.RING, channels),
                                  dtype=torch.bfloat16, device=dev) if cfg.gdn_taps else None)
         self._glue_ws = None
-        self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads, 2, cfg.page_size,
-                               cfg.head_dim), dtype=torch.bfloat16, device=dev)
+        if cfg.kv_precision not in ("bf16", "8bit"):
+            raise ValueError("Unsupported inference cache precision.")
+        if cfg.kv_precision == "8bit":
+            self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads,
+                                   paged.Q8_BYTES_PER_DIM * cfg.head_dim), dtype=torch.uint8,
+                                  device=dev)
+        else:
+            self.kv = torch.empty((n_attn, cfg.num_pages, cfg.kv_heads, 2, cfg.page_size,
+                                   cfg.head_dim), dtype=torch.bfloat16, device=dev)
         self.blocks = BlockManager(cfg.num_pages, cfg.page_size, cfg.max_seqs,
                                    cfg.max_pages_per_seq, seed=seed)
         # Pinned host mirrors, copied to the device once per step.
@@ -210,7 +224,7 @@ class HybridCacheEngine:
         """Bytes a cache of `tokens` tokens holds: K/V of every attention layer plus the
         GDN state of every GDN layer (what a prefix snapshot is charged)."""
         c = self.cfg
-        kv = tokens * c.kv_heads * c.head_dim * 2 * 2 * len(c.attention_layers)
+        kv = tokens * c.kv_token_bytes() * len(c.attention_layers)
         elem = torch.finfo(c.state_dtype).bits // 8
         st = c.gdn_value_heads * c.value_dim * c.key_dim * elem * len(c.gdn_layers)
         if self.taps is not None:
@@ -364,7 +378,7 @@ class HybridCacheEngine:
             2 * c.gdn_value_heads * c.value_dim * c.key_dim * (torch.finfo(c.state_dtype).bits // 8)
             + (2 * c.gdn_key_heads * c.key_dim + 2 * c.gdn_value_heads * c.value_dim) * 2
             + 2 * c.gdn_value_heads * 4)
-        row = c.kv_heads * c.head_dim * 2 * 2          # K + V bytes of one token
+        row = c.kv_token_bytes()                        # K + V bytes of one token
         pages = np.ceil(lengths / c.page_size)
         attn_layer = (float(lengths.sum()) * row + n * row + n * c.q_heads * c.head_dim * 2 * 2
                       + float(pages.sum()) * 4)
