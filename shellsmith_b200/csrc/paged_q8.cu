@@ -497,7 +497,14 @@ __global__ void __launch_bounds__(NW * 32)
   }
 }
 
-constexpr int kQ8Warps = 4, kQ8Stages = 3;
+// Launch shape: warps per CTA and shared-memory stages (one page block each) per warp.
+#ifndef SC_Q8_WARPS
+#define SC_Q8_WARPS 4
+#endif
+#ifndef SC_Q8_STAGES
+#define SC_Q8_STAGES 2  // 70 KiB CTAs, three per SM: 90% of measured HBM on config 3
+#endif
+constexpr int kQ8Warps = SC_Q8_WARPS, kQ8Stages = SC_Q8_STAGES;
 
 template <int D>
 int launch_q8(const uint16_t* q, const uint8_t* pool, const int32_t* block_table,
