@@ -75,6 +75,10 @@ def parse():
                     help="only time one GDN layer run from its projections (fused glue) "
                          "against the plain state update, with --batch rows; prints a JSON "
                          "object (a profiling entry, not a bench line)")
+    ap.add_argument("--kv8-only", action="store_true",
+                    help="only time one attention layer on 8-bit pages beside bf16 pages for "
+                         "--batch sequences of U[--min-len, --max-len] tokens; prints a JSON "
+                         "object (a profiling entry, not a bench line)")
     ap.add_argument("--config", type=int, choices=(3, 4), default=3,
                     help="3: ragged batch decode step (default); 4: one long sequence with its "
                          "KV pages split across the GPUs")
@@ -615,6 +619,76 @@ def kv8_attention_layer(wl, device, rounds: int = 5) -> dict:
                     "depend on the values"}
 
 
+def kv8_layer_standalone(args, device, rounds: int = 10) -> dict:
+    """One config-3 attention layer (append + split-K attention + combine) over
+    --batch sequences of U[--min-len, --max-len] tokens, on 8-bit and on bf16
+    pages (random contents; timing does not depend on the values)."""
+    import torch
+
+    from shellsmith_b200 import paged
+
+    rng = np.random.default_rng(SEED)
+    B, Hq, Hkv, D, P = args.batch, 16, 2, 256, paged.PAGE_SIZE
+    lengths = rng.integers(args.min_len, args.max_len + 1, size=B)
+    need = np.ceil(lengths / P).astype(np.int64)
+    num_pages, width = int(need.sum()) + 16, int(need.max())
+    perm = rng.permutation(num_pages)
+    table = np.zeros((B, width), np.int32)
+    cursor = 0
+    for b, n in enumerate(need):
+        table[b, :n] = perm[cursor:cursor + n]
+        cursor += n
+    slots = (table[np.arange(B), (lengths - 1) // P].astype(np.int64) * P + (lengths - 1) % P)
+    bt = torch.from_numpy(table).to(device)
+    ctx = torch.from_numpy(lengths.astype(np.int32)).to(device)
+    slot_t = torch.from_numpy(slots).to(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(SEED)
+    q = torch.randn((B, Hq, D), generator=gen, device=device).to(torch.bfloat16)
+    kn = torch.randn((B, Hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    total = int(need.sum())
+    ws = paged.AttentionWorkspace(B, Hq, D, paged.split_plan(width, 16)[1], device=device)
+    stream = torch.cuda.current_stream(device)
+    ms, nbytes = {}, {}
+    for name in ("bf16", "8bit"):
+        if name == "8bit":
+            pool = paged.new_pool_q8(num_pages, Hkv, D, device)
+            pool.random_(0, 256)
+            pool[:, :, 32 * D:].view(torch.bfloat16).fill_(0.01)
+            row = Hkv * (2 * D + 8 * D / 64)
+        else:
+            pool = paged.new_pool(num_pages, Hkv, D, device=device)
+            pool.view(torch.int16).random_(0, 16000)  # finite bf16 values below 1
+            row = Hkv * D * 4
+
+        def run():
+            paged.kv_append(kn, kn, pool, slot_t)
+            paged.paged_decode_attention(q, pool, bt, ctx, 1.0 / 16, max_pages_in_batch=width,
+                                         total_pages=total, workspace=ws, out=out)
+
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(rounds):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms[name] = e0.elapsed_time(e1) / rounds
+        nbytes[name] = float(lengths.sum()) * row + B * row + B * Hq * D * 4 + total * 4
+        del pool
+    peaks = measured_peaks()
+    return {"workload": f"attention layer, {B} sequences U[{args.min_len},{args.max_len}] "
+                        f"(mean {lengths.mean():.0f}), Hq16/Hkv2 D256",
+            "bf16_ms": round(ms["bf16"], 4), "kv8_ms": round(ms["8bit"], 4),
+            "bf16_gbs": round(nbytes["bf16"] / ms["bf16"] / 1e6, 1),
+            "kv8_gbs": round(nbytes["8bit"] / ms["8bit"] / 1e6, 1),
+            "kv8_frac": round(nbytes["8bit"] / ms["8bit"] / 1e6 / peaks["hbm_gbs"], 4),
+            "kv8_bytes_per_launch": round(nbytes["8bit"]), "launches": rounds + 3}
+
+
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:
     """Config 1: chunked GDN prefill, B=8, T=4096, 16 key / 32 value heads, 128 x 128,
     fp32 state, on the tensor cores. Algorithmic FLOPs and bytes of the reference
@@ -912,6 +986,11 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.kv8_only:
+            import torch
+
+            print(json.dumps(kv8_layer_standalone(args, torch.device("cuda", local))),
+                  flush=True)
         elif args.front_only:
             import torch
 
