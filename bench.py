@@ -75,6 +75,9 @@ def parse():
                     help="only time one GDN layer run from its projections (fused glue) "
                          "against the plain state update, with --batch rows; prints a JSON "
                          "object (a profiling entry, not a bench line)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only time the config-1 chunked prefill; prints a JSON "
+                         "object (a profiling entry, not a bench line)")
     ap.add_argument("--kv8-only", action="store_true",
                     help="only time one attention layer on 8-bit pages beside bf16 pages for "
                          "--batch sequences of U[--min-len, --max-len] tokens; prints a JSON "
@@ -986,6 +989,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.prefill_only:
+            import torch
+
+            print(json.dumps(config1_prefill(torch.device("cuda", local))), flush=True)
         elif args.kv8_only:
             import torch
 
