@@ -273,23 +273,30 @@ class HybridCacheEngine:
         paged.kv_append(k, v, self.kv[self.attn_index[layer]],
                         torch.from_numpy(slots).to(self.device, non_blocking=True))
 
-    def begin_step(self) -> int:
-        """Append one token to every active sequence and stage the step's tables.
+    def begin_step(self, rows=None) -> int:
+        """Append one token to every active sequence (or to the listed slots only) and
+        stage the step's tables. Rows outside the step are skipped by every kernel
+        (state slot -1, slot mapping -1, context length 0).
 
-        Returns the number of active rows (tokens this step decodes).
+        Returns the number of rows this step decodes.
         """
         self._staged.synchronize()  # the previous step's copies have read the staging
         blocks = self.blocks
-        active = np.flatnonzero(blocks.active)
+        active = (np.flatnonzero(blocks.active) if rows is None
+                  else np.asarray(sorted(int(r) for r in rows), np.int64))
+        if rows is not None and not blocks.active[active].all():
+            raise ValueError("begin_step: a listed slot holds no sequence")
         slot_map = np.full(self.cfg.max_seqs, -1, np.int64)
         slot_map[active] = blocks.append_token(active)
         self._h_slot_map.numpy()[:] = slot_map
-        self._h_ctx.numpy()[:] = blocks.lengths.astype(np.int32)
+        ctx = np.zeros(self.cfg.max_seqs, np.int32)
+        ctx[active] = blocks.lengths[active]
+        self._h_ctx.numpy()[:] = ctx
         state_slot = np.full(self.cfg.max_seqs, -1, np.int32)
         state_slot[active] = active
         self._h_state_slot.numpy()[:] = state_slot
         self._h_position.numpy()[:] = np.maximum(blocks.lengths - 1, 0).astype(np.int32)
-        self.max_pages_in_batch = max(1, int(blocks.pages_for(blocks.lengths.max())))
+        self.max_pages_in_batch = max(1, int(blocks.pages_for(ctx.max())))
         self.total_pages = int(np.ceil(blocks.lengths[active] / self.cfg.page_size).sum())
         self.table.copy_(self._h_table, non_blocking=True)
         self.ctx_len.copy_(self._h_ctx, non_blocking=True)

@@ -41,6 +41,8 @@ import math
 import time
 from typing import Any
 
+import numpy as np
+
 from .prefix_cache import PrefixCache
 from .scheduler import DecodeRequest
 
@@ -70,7 +72,7 @@ def _policy_bytes(engine: Any, body: dict) -> int:
 
 def _fresh_cache(engine: Any, precision: str):
     cache = engine.lm.make_cache()
-    if precision == "8bit":
+    if precision == "8bit" and isinstance(cache, list):  # a paged cache's precision is its pool's
         cache = [item.to_quantized(bits=8, group_size=64) if hasattr(item, "to_quantized")
                  else item for item in cache]
     return cache
@@ -143,6 +145,61 @@ def release_request(engine: Any, request: DecodeRequest) -> None:
         request.lease.__exit__(None, None, None)
     finally:
         engine.reserved.pop((RESERVATION, request.request_id), None)
+
+
+def prefill_request(engine: Any, request: DecodeRequest) -> None:
+    """Advance at most engine.prefill_tokens prompt tokens (inference.py:124-163).
+
+    The request's cache is a PagedSequence: a fresh one takes its slot (and the
+    pages of the whole prompt) on its first chunk; a prefix-cache fork continues
+    from its cached offset. The last chunk sets the logits and, unless the body
+    opts out, stores the prompt's snapshot in the prefix cache.
+    """
+    body = request.body
+    prompt = body["prompt_token_ids"]
+    start = request.offset
+    stop = min(len(prompt), start + engine.prefill_tokens)
+    seq = request.cache
+    if seq.slot is None:
+        seq.slot = seq.engine.admit(request.request_id, len(prompt))
+    logits = engine.resident.prefill(seq, prompt[start:stop], start)
+    request.offset = stop
+    if stop < len(prompt):
+        return
+    request.logits = logits
+    if body.get("use_prefix_cache", True):
+        engine.prefixes.put(engine.prefix_identity, body["policy"],
+                            body.get("cache_precision", "bf16"), prompt, request.cache,
+                            request.logits)
+    request.prefill_seconds = time.monotonic() - request.started
+    request.decode_started = time.monotonic()
+
+
+def advance_requests(engine: Any, requests: list) -> None:
+    """One decode token for every listed request (inference.py:166-173)."""
+    engine.resident.decode_rows(engine, requests)
+    for request in requests:
+        request.batch_size = max(request.batch_size, len(requests))
+
+
+def sample_requests(engine: Any, requests: list) -> None:
+    """One token per request from its logits (inference.py:176-218): a forced target
+    when the body has one, else a categorical draw from a generator seeded with the
+    request's RNG key (the reference splits an MLX key; the draws differ, the
+    bookkeeping does not)."""
+    import torch
+
+    for request in requests:
+        lp = torch.log_softmax(request.logits.float(), dim=-1)[0]
+        forced = request.body.get("target_token_ids")
+        if forced:
+            token = int(forced[len(request.tokens)])
+        else:
+            key = [int(x) for x in np.asarray(request.rng).ravel()]
+            gen = torch.Generator(device="cpu").manual_seed(
+                (key[0] << 32 | key[-1]) + len(request.tokens))
+            token = int(torch.multinomial(lp.exp().cpu(), 1, generator=gen))
+        finish_sample(request, token, float(lp[token]))
 
 
 def finish_sample(request: DecodeRequest, token: int, logprob: float) -> None:
