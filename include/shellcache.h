@@ -251,7 +251,8 @@ int sc_kv_copy_pages_q8(uint8_t* kv_pool, const int32_t* src, const int32_t* dst
 /* sc_paged_decode_attention over an 8-bit pool (same split plan, partials and
  * combine); kv_pool 16-byte aligned. */
 int sc_paged_decode_attention_q8(const sc_bf16* q, const uint8_t* kv_pool, int64_t num_pages,
-                                 const int32_t* block_table, const int32_t* ctx_len, int B,
+                                 const int32_t* block_table, const int32_t* ctx_len,
+                                 const int32_t* seq_order, int B,
                                  int Hq, int Hkv, int D, int P, int max_pages,
                                  int pages_per_split, int num_splits, float scale,
                                  float* part_out, float* part_lse, sc_bf16* out, float* lse_out,
@@ -272,6 +273,9 @@ int sc_paged_decode_attention_q8(const sc_bf16* q, const uint8_t* kv_pool, int64
  * block_table  [B, max_pages] int32 (row stride max_pages); an entry outside
  *              [0, num_pages) sets the device status word (DEV_BAD_INDEX)
  * ctx_len      [B] int32, tokens to attend (includes the appended token)
+ * seq_order    [B] int32 or NULL: a permutation of 0..B-1, the order in which
+ *              the sequences' CTAs launch (longest first keeps the last wave
+ *              short on ragged batches); NULL launches in row order
  * pages_per_split  pages one CTA reduces; the sequence is cut into
  *                  ceil(ceil(ctx_len / P) / pages_per_split) splits
  * num_splits   grid bound: >= the largest split count in the batch
@@ -286,7 +290,8 @@ int sc_paged_decode_attention_q8(const sc_bf16* q, const uint8_t* kv_pool, int64
  * ------------------------------------------------------------------------ */
 int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
                               int64_t num_pages, const int32_t* block_table,
-                              const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
+                              const int32_t* ctx_len, const int32_t* seq_order, int B,
+                              int Hq, int Hkv, int D,
                               int P, int max_pages, int pages_per_split,
                               int num_splits, float scale,
                               float* part_out, float* part_lse, sc_bf16* out,

@@ -39,13 +39,13 @@ SIGNATURES = {
     "sc_kv_append_q8": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_gather_q8": [_P, _P, _I, _I, _I, _I, _I64, _P, _P, _P],
     "sc_kv_copy_pages_q8": [_P, _P, _P, _I, _I, _I, _I, _I64, _P],
-    "sc_paged_decode_attention_q8": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
-                                     _P, _P, _P, _P, _P],
+    "sc_paged_decode_attention_q8": [_P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
+                                     _F, _P, _P, _P, _P, _P],
     "sc_kv_append": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_gather": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],
     "sc_kv_copy_pages": [_P, _P, _P, _I, _I, _I, _I, _I64, _P],
-    "sc_paged_decode_attention": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
-                                  _P, _P, _P, _P, _P],
+    "sc_paged_decode_attention": [_P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
+                                  _F, _P, _P, _P, _P, _P],
     "sc_attention_combine": [_P, _P, _I, _I, _I, _P, _P, _P],
     "sc_paged_decode_attention_packed": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                          _F, _P, _P, _P, _P],

@@ -45,7 +45,8 @@ template <int D, int NW, int NSTAGE>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kv_pool,
                         const int32_t* __restrict__ block_table,
-                        const int32_t* __restrict__ ctx_len, int Hq, int Hkv, int G, int HG,
+                        const int32_t* __restrict__ ctx_len,
+                        const int32_t* __restrict__ seq_order, int Hq, int Hkv, int G, int HG,
                         int max_pages, int pages_per_split, int num_splits, float scale_log2,
                         float* __restrict__ part_out, float* __restrict__ part_lse,
                         uint16_t* __restrict__ out, float* __restrict__ lse_out,
@@ -62,7 +63,12 @@ __global__ void __launch_bounds__(NW * 32)
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / HG;
   const int hg = blockIdx.y - kvh * HG;
-  const int b = blockIdx.z;
+  // Sequences in launch order (longest first shortens the tail of ragged batches).
+  const int b = seq_order != nullptr ? seq_order[blockIdx.z] : (int)blockIdx.z;
+  if (b < 0 || b >= (int)gridDim.z) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
+    return;
+  }
   const int L = ctx_len[b];
   const int npages = (L + kPage - 1) / kPage;
   const int p_begin = split * pages_per_split;
@@ -477,7 +483,8 @@ constexpr int kStages = SC_ATTN_STAGES;
 
 template <int D>
 int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* block_table,
-                  const int32_t* ctx_len, int B, int Hq, int Hkv, int max_pages,
+                  const int32_t* ctx_len, const int32_t* seq_order, int B, int Hq, int Hkv,
+                  int max_pages,
                   int pages_per_split, int num_splits, float scale, float* part_out,
                   float* part_lse, uint16_t* out, float* lse_out, float* packed,
                   long long num_pages, cudaStream_t s) {
@@ -500,7 +507,8 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
   const int HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(num_splits, Hkv * HG, B);
-  kernel<<<grid, NW * 32, smem, s>>>(q, kv_pool, block_table, ctx_len, Hq, Hkv, G, HG, max_pages,
+  kernel<<<grid, NW * 32, smem, s>>>(q, kv_pool, block_table, ctx_len, seq_order, Hq, Hkv, G, HG,
+                                     max_pages,
                                      pages_per_split, num_splits, scale_log2, part_out, part_lse,
                                      out, lse_out, packed, num_pages, device_status_word());
   if (int rc = check_launch("sc_paged_decode_attention")) return rc;
@@ -518,7 +526,8 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
 namespace sc {
 namespace {
 int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int64_t num_pages,
-                 const int32_t* block_table, const int32_t* ctx_len, int B, int Hq, int Hkv,
+                 const int32_t* block_table, const int32_t* ctx_len, const int32_t* seq_order,
+                 int B, int Hq, int Hkv,
                  int D, int P, int max_pages, int pages_per_split, int num_splits, float scale,
                  float* part_out, float* part_lse, sc_bf16* out, float* lse_out, float* packed,
                  void* stream) {
@@ -539,15 +548,18 @@ int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (D) {
     case 64:
-      return launch_decode<64>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+      return launch_decode<64>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
+                                 max_pages,
                                    pages_per_split, num_splits, scale, part_out, part_lse, out,
                                    lse_out, packed, num_pages, s);
     case 128:
-      return launch_decode<128>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+      return launch_decode<128>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
+                                 max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
                                     lse_out, packed, num_pages, s);
     case 256:
-      return launch_decode<256>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+      return launch_decode<256>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
+                                 max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
                                     lse_out, packed, num_pages, s);
     default:
@@ -559,14 +571,16 @@ int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int
 
 extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_pool,
                                          int64_t num_pages, const int32_t* block_table,
-                                         const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
+                                         const int32_t* ctx_len, const int32_t* seq_order, int B,
+                                         int Hq, int Hkv, int D,
                                          int P, int max_pages, int pages_per_split,
                                          int num_splits, float scale,
                                          float* part_out, float* part_lse, sc_bf16* out,
                                          float* lse_out, void* stream) {
   SC_REQUIRE(out != nullptr, SC_ERR_INVALID, "sc_paged_decode_attention: null pointer");
   return sc::decode_entry("sc_paged_decode_attention", q, kv_pool, num_pages, block_table,
-                          ctx_len, B, Hq, Hkv, D, P, max_pages, pages_per_split, num_splits,
+                          ctx_len, seq_order, B, Hq, Hkv, D, P, max_pages, pages_per_split,
+                          num_splits,
                           scale, part_out, part_lse, out, lse_out, nullptr, stream);
 }
 
@@ -579,7 +593,8 @@ extern "C" int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16*
                                                 void* stream) {
   SC_REQUIRE(packed != nullptr, SC_ERR_INVALID, "sc_paged_decode_attention_packed: null pointer");
   return sc::decode_entry("sc_paged_decode_attention_packed", q, kv_pool, num_pages,
-                          block_table, ctx_len, B, Hq, Hkv, D, P, max_pages, pages_per_split,
+                          block_table, ctx_len, nullptr, B, Hq, Hkv, D, P, max_pages,
+                          pages_per_split,
                           num_splits, scale, part_out, part_lse, nullptr, nullptr, packed,
                           stream);
 }
@@ -674,7 +689,8 @@ extern "C" int sc_paged_decode_attention_noalloc(const sc_bf16* q, const sc_bf16
   if (scratch == nullptr) return SC_ERR_CUDA;
   float* part_out = num_splits > 1 ? scratch : nullptr;
   float* part_lse = num_splits > 1 ? scratch + rows * D : nullptr;
-  return sc_paged_decode_attention(q, kv_pool, num_pages, block_table, ctx_len, B, Hq, Hkv, D, P,
+  return sc_paged_decode_attention(q, kv_pool, num_pages, block_table, ctx_len, nullptr, B, Hq,
+                                   Hkv, D, P,
                                    max_pages, pages_per_split, num_splits, scale, part_out,
                                    part_lse, out, lse_out, stream);
 }

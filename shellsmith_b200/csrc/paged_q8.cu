@@ -218,7 +218,8 @@ template <int D, int NW, int NSTAGE>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_q8_kernel(const uint16_t* __restrict__ q, const uint8_t* __restrict__ pool,
                            const int32_t* __restrict__ block_table,
-                           const int32_t* __restrict__ ctx_len, int Hq, int Hkv, int G, int HG,
+                           const int32_t* __restrict__ ctx_len,
+                           const int32_t* __restrict__ seq_order, int Hq, int Hkv, int G, int HG,
                            int max_pages, int pages_per_split, int num_splits, float scale_log2,
                            float* __restrict__ part_out, float* __restrict__ part_lse,
                            uint16_t* __restrict__ out, float* __restrict__ lse_out,
@@ -233,7 +234,11 @@ __global__ void __launch_bounds__(NW * 32)
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / HG;
   const int hg = blockIdx.y - kvh * HG;
-  const int b = blockIdx.z;
+  const int b = seq_order != nullptr ? seq_order[blockIdx.z] : (int)blockIdx.z;
+  if (b < 0 || b >= (int)gridDim.z) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
+    return;
+  }
   const int L = ctx_len[b];
   const int npages = (L + kPage - 1) / kPage;
   const int p_begin = split * pages_per_split;
@@ -508,7 +513,7 @@ constexpr int kQ8Warps = SC_Q8_WARPS, kQ8Stages = SC_Q8_STAGES;
 
 template <int D>
 int launch_q8(const uint16_t* q, const uint8_t* pool, const int32_t* block_table,
-              const int32_t* ctx_len, int B, int Hq, int Hkv, int max_pages, int pages_per_split,
+              const int32_t* ctx_len, const int32_t* seq_order, int B, int Hq, int Hkv, int max_pages, int pages_per_split,
               int num_splits, float scale, float* part_out, float* part_lse, uint16_t* out,
               float* lse_out, long long num_pages, cudaStream_t s) {
   using S = Q8<D>;
@@ -531,7 +536,8 @@ int launch_q8(const uint16_t* q, const uint8_t* pool, const int32_t* block_table
   const int G = Hq / Hkv;
   const int HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
   dim3 grid(num_splits, Hkv * HG, B);
-  kernel<<<grid, NW * 32, smem, s>>>(q, pool, block_table, ctx_len, Hq, Hkv, G, HG, max_pages,
+  kernel<<<grid, NW * 32, smem, s>>>(q, pool, block_table, ctx_len, seq_order, Hq, Hkv, G, HG,
+                                     max_pages,
                                      pages_per_split, num_splits, scale * 1.4426950408889634f,
                                      part_out, part_lse, out, lse_out, num_pages,
                                      device_status_word());
@@ -640,8 +646,9 @@ extern "C" int sc_kv_copy_pages_q8(uint8_t* kv_pool, const int32_t* src, const i
 
 extern "C" int sc_paged_decode_attention_q8(const sc_bf16* q, const uint8_t* kv_pool,
                                             int64_t num_pages, const int32_t* block_table,
-                                            const int32_t* ctx_len, int B, int Hq, int Hkv,
-                                            int D, int P, int max_pages, int pages_per_split,
+                                            const int32_t* ctx_len, const int32_t* seq_order,
+                                            int B, int Hq, int Hkv, int D, int P, int max_pages,
+                                            int pages_per_split,
                                             int num_splits, float scale, float* part_out,
                                             float* part_lse, sc_bf16* out, float* lse_out,
                                             void* stream) {
@@ -664,9 +671,10 @@ extern "C" int sc_paged_decode_attention_q8(const sc_bf16* q, const uint8_t* kv_
   if (B == 0) return SC_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (D == 128)
-    return launch_q8<128>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages,
+    return launch_q8<128>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv, max_pages,
                           pages_per_split, num_splits, scale, part_out, part_lse, out, lse_out,
                           num_pages, s);
-  return launch_q8<256>(q, kv_pool, block_table, ctx_len, B, Hq, Hkv, max_pages, pages_per_split,
-                        num_splits, scale, part_out, part_lse, out, lse_out, num_pages, s);
+  return launch_q8<256>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv, max_pages,
+                        pages_per_split, num_splits, scale, part_out, part_lse, out, lse_out,
+                        num_pages, s);
 }

@@ -119,11 +119,13 @@ class HybridCacheEngine:
         self._h_slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, pin_memory=True)
         self._h_state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, pin_memory=True)
         self._h_position = torch.zeros(cfg.max_seqs, dtype=torch.int32, pin_memory=True)
+        self._h_order = torch.arange(cfg.max_seqs, dtype=torch.int32).pin_memory()
         self.table = torch.zeros_like(self._h_table, device=dev)
         self.ctx_len = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
         self.slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, device=dev)
         self.state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, device=dev)
         self.position = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
+        self.seq_order = torch.arange(cfg.max_seqs, dtype=torch.int32, device=dev)
         self._staged = torch.cuda.Event()
         self._staged.record()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
@@ -292,6 +294,7 @@ class HybridCacheEngine:
         ctx = np.zeros(self.cfg.max_seqs, np.int32)
         ctx[active] = blocks.lengths[active]
         self._h_ctx.numpy()[:] = ctx
+        self._h_order.numpy()[:] = np.argsort(-ctx, kind="stable")  # attention: longest first
         state_slot = np.full(self.cfg.max_seqs, -1, np.int32)
         state_slot[active] = active
         self._h_state_slot.numpy()[:] = state_slot
@@ -303,6 +306,7 @@ class HybridCacheEngine:
         self.slot_map.copy_(self._h_slot_map, non_blocking=True)
         self.state_slot.copy_(self._h_state_slot, non_blocking=True)
         self.position.copy_(self._h_position, non_blocking=True)
+        self.seq_order.copy_(self._h_order, non_blocking=True)
         self._staged.record()
         return len(active)
 
@@ -362,7 +366,8 @@ class HybridCacheEngine:
                                      max_pages_in_batch=self.max_pages_in_batch,
                                      pages_per_split=self.cfg.pages_per_split,
                                      total_pages=self.total_pages,
-                                     workspace=self.workspace, out=out)
+                                     workspace=self.workspace, out=out,
+                                     seq_order=self.seq_order)
 
     def decode_step(self, inputs: dict, outputs: dict) -> None:
         """Run every layer's cache work for the staged token of each active row.

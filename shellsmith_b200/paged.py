@@ -186,8 +186,12 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
                            total_pages: int | None = None,
                            workspace: AttentionWorkspace | None = None,
                            out: torch.Tensor | None = None,
-                           lse_out: torch.Tensor | None = None) -> torch.Tensor:
+                           lse_out: torch.Tensor | None = None,
+                           seq_order: torch.Tensor | None = None) -> torch.Tensor:
     """Decode attention of q [B, Hq, D] over each sequence's ctx_len[b] cached tokens.
+
+    seq_order [B] int32 (a permutation) launches the sequences' CTAs in that
+    order; longest first shortens the last wave of a ragged batch.
 
     block_table [B, max_pages] int32 lists each sequence's pages in token
     order. max_pages_in_batch (host-known) sizes the grid; when omitted the
@@ -211,6 +215,10 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     require_cuda("out", out, torch.bfloat16, 3)
     if lse_out is not None:
         require_cuda("lse_out", lse_out, torch.float32, 1, align=4)
+    if seq_order is not None:
+        require_cuda("seq_order", seq_order, torch.int32, 1, align=4)
+        if seq_order.shape[0] != B:
+            raise ValueError("paged_decode_attention: seq_order needs one entry per sequence")
     part_out = part_lse = None
     if nsplit > 1:
         if workspace is None or not workspace.fits(B, hq, dim, nsplit):
@@ -218,9 +226,9 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
         part_out, part_lse = workspace.views(B, nsplit)
     name = ("sc_paged_decode_attention_q8" if kv_pool.dtype == torch.uint8
             else "sc_paged_decode_attention")
-    _capi.call(name, ptr(q), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len), B, hq, hkv,
-               dim, page, max_pages, pps, nsplit, float(scale), ptr(part_out), ptr(part_lse),
-               ptr(out), ptr(lse_out), stream_of(q))
+    _capi.call(name, ptr(q), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len),
+               ptr(seq_order), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
+               ptr(part_out), ptr(part_lse), ptr(out), ptr(lse_out), stream_of(q))
     return out
 
 

@@ -53,6 +53,6 @@ def test_version_and_error_text_without_gpu(library):
                                  128, 1, None)
     assert code == 1
     assert "null pointer" in _capi.last_error()
-    code = library.sc_paged_decode_attention(1, 1, 10, 1, 1, 1, 16, 2, 256, 8, 4, 64, 1, 0.1,
-                                             None, None, 1, None, None)
+    code = library.sc_paged_decode_attention(1, 1, 10, 1, 1, None, 1, 16, 2, 256, 8, 4, 64, 1,
+                                             0.1, None, None, 1, None, None)
     assert code == 2 and "page size" in _capi.last_error()

@@ -171,3 +171,26 @@ def test_bad_page_index_sets_device_status(cuda):
     with pytest.raises(_capi.DeviceFault):
         _capi.check_device()
     assert _capi.device_status() == 0
+
+
+def test_launch_order_changes_nothing_but_the_schedule(cuda):
+    """Any permutation as seq_order gives bit-identical outputs; an entry outside
+    0..B-1 is reported through the device status word."""
+    from shellsmith_b200 import _capi
+
+    rng = np.random.default_rng(21)
+    lengths = [3000, 17, 512, 1, 0, 700, 64, 1300]
+    pool, q, table = _build_case(rng, lengths, 16, 2, 256, 400, cuda)
+    bt = torch.from_numpy(table).to(cuda)
+    ctx = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    base = paged.paged_decode_attention(q, pool, bt, ctx, 0.0625, pages_per_split=8)
+    for order in (np.argsort(-np.array(lengths), kind="stable"), rng.permutation(len(lengths))):
+        got = paged.paged_decode_attention(q, pool, bt, ctx, 0.0625, pages_per_split=8,
+                                           seq_order=torch.from_numpy(order.astype(np.int32))
+                                           .to(cuda))
+        assert torch.equal(got, base)
+    _capi.device_status()
+    bad = torch.tensor([0, 1, 2, 3, 4, 5, 6, 99], dtype=torch.int32, device=cuda)
+    paged.paged_decode_attention(q, pool, bt, ctx, 0.0625, pages_per_split=8, seq_order=bad)
+    with pytest.raises(_capi.DeviceFault):
+        _capi.check_device()

@@ -52,7 +52,7 @@ def _regular(pool, q, table, ctx, width, pps, nsplit):
     out = torch.empty((B, hq, D), dtype=torch.bfloat16, device=q.device)
     lse = torch.empty((B * hq,), dtype=torch.float32, device=q.device)
     _capi.call("sc_paged_decode_attention", ptr(q), ptr(pool), pool.shape[0], ptr(table),
-               ptr(ctx), B, hq, pool.shape[1], D, pool.shape[3], width, pps, nsplit, 1.0 / 16,
+               ptr(ctx), None, B, hq, pool.shape[1], D, pool.shape[3], width, pps, nsplit, 1.0 / 16,
                ptr(part_out), ptr(part_lse), ptr(out), ptr(lse), stream_of(q))
     return out, lse
 
