@@ -179,6 +179,9 @@ constexpr int kBulkChunkBytes = kBulkRows * 128 * 4;
 #endif
 constexpr int kBulkChunksPerCta = SC_GDN_BULK_CHUNKS;
 
+// NCH chunks of 32 rows per CTA: kBulkChunksPerCta for batches that fill the
+// GPU, 1 (twice the CTAs) when a batch is too small to.
+template <int NCH>
 __global__ void __launch_bounds__(128)
     gdn_decode_bulk_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
                            const uint16_t* __restrict__ v, const float* __restrict__ g,
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(128)
                            const int32_t* __restrict__ state_slot, uint16_t* __restrict__ out,
                            int Hk, int Hv, int dv, int num_slots, unsigned int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int nchunks = kBulkChunksPerCta;
+  constexpr int nchunks = NCH;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nchunks * kBulkChunkBytes);
   const int chunk0 = blockIdx.y * nchunks;  // first 32-row chunk of this CTA
   const int bh = blockIdx.x;
@@ -323,19 +326,27 @@ int gdn_bulk_launch(const char* name, const uint16_t* q, const uint16_t* k, cons
                     const float* g, const float* beta, float* state, const int32_t* slot,
                     uint16_t* out, int B, int Hk, int Hv, int dv, int num_slots, cudaStream_t s,
                     bool programmatic) {
-  const int smem = kBulkChunksPerCta * (kBulkChunkBytes + 8) + 8;
   static int configured[64] = {};
+  static int sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(gdn_decode_bulk_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (dev < 0 || dev >= 64) return set_error(SC_ERR_CUDA, "%s: device %d", name, dev);
+  if (!configured[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(gdn_decode_bulk_kernel<kBulkChunksPerCta>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kBulkChunksPerCta * (kBulkChunkBytes + 8) + 8);
+    if (err == cudaSuccess)
+      err = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     if (err != cudaSuccess)
-      return set_error(SC_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(err));
+      return set_error(SC_ERR_CUDA, "%s: setup: %s", name, cudaGetErrorString(err));
     configured[dev] = 1;
   }
+  // Fewer CTAs than two per SM: one 16 KiB chunk per CTA instead (more loads in flight).
+  const bool small = (long long)B * Hv * (dv / (kBulkRows * kBulkChunksPerCta)) < 2LL * sms[dev];
+  const int nch = small ? 1 : kBulkChunksPerCta;
+  const int smem = nch * (kBulkChunkBytes + 8) + 8;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(B * Hv, dv / (kBulkRows * kBulkChunksPerCta));
+  cfg.gridDim = dim3(B * Hv, dv / (kBulkRows * nch));
   cfg.blockDim = dim3(128);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -344,8 +355,12 @@ int gdn_bulk_launch(const char* name, const uint16_t* q, const uint16_t* k, cons
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = programmatic ? 1 : 0;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, gdn_decode_bulk_kernel, q, k, v, g, beta, state, slot,
-                                       out, Hk, Hv, dv, num_slots, device_status_word());
+  cudaError_t err =
+      small ? cudaLaunchKernelEx(&cfg, gdn_decode_bulk_kernel<1>, q, k, v, g, beta, state, slot,
+                                 out, Hk, Hv, dv, num_slots, device_status_word())
+            : cudaLaunchKernelEx(&cfg, gdn_decode_bulk_kernel<kBulkChunksPerCta>, q, k, v, g,
+                                 beta, state, slot, out, Hk, Hv, dv, num_slots,
+                                 device_status_word());
   if (err != cudaSuccess)
     return set_error(SC_ERR_CUDA, "%s: launch: %s", name, cudaGetErrorString(err));
   return check_launch(name);

@@ -421,9 +421,24 @@ __global__ void __launch_bounds__(kCombineThreads)
     wsum = wsum * rescale + block_sum(part, red);
     M = Mn;
     float a = acc * rescale;
-    if (d < D)
-      for (int s = warp; s < n; s += kCombineThreads / 32)
-        a = fmaf(w[s], o[(size_t)(s0 + s) * o_part + d], a);
+    if (d < D) {
+      // Four parts in flight per warp: the loads do not wait on the sum chain.
+      constexpr int kStride = kCombineThreads / 32;
+      float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int s = warp;
+      for (; s + 3 * kStride < n; s += 4 * kStride) {
+        const float v0 = o[(size_t)(s0 + s) * o_part + d];
+        const float v1 = o[(size_t)(s0 + s + kStride) * o_part + d];
+        const float v2 = o[(size_t)(s0 + s + 2 * kStride) * o_part + d];
+        const float v3 = o[(size_t)(s0 + s + 3 * kStride) * o_part + d];
+        a = fmaf(w[s], v0, a);
+        a1 = fmaf(w[s + kStride], v1, a1);
+        a2 = fmaf(w[s + 2 * kStride], v2, a2);
+        a3 = fmaf(w[s + 3 * kStride], v3, a3);
+      }
+      for (; s < n; s += kStride) a = fmaf(w[s], o[(size_t)(s0 + s) * o_part + d], a);
+      a += (a1 + a2) + a3;
+    }
     acc = a;
     __syncthreads();
   }

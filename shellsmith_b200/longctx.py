@@ -84,6 +84,7 @@ class ShardedSequence:
                                     device=device)
         self.out = torch.empty((q_heads, head_dim), dtype=torch.bfloat16, device=device)
         self.workspace = None
+        self.pages_per_split = None
 
     def begin_token(self) -> None:
         """Stage the next decode token: the tail rank appends it after its last token.
@@ -115,14 +116,18 @@ class ShardedSequence:
         pool = self.kv[layer]
         paged.kv_append(k_new, v_new, pool, self.slot)
         # The grid covers the whole local capacity (fixed, so the step can be
-        # captured); CTAs past the context return at once.
+        # captured); CTAs past the context return at once. One sequence makes
+        # equal CTAs, so the split is sized for exactly one wave on every SM
+        # (the batch rule's two waves only add CTA overhead and partials here).
         if self.workspace is None:
-            _, nsplit = paged.split_plan(self.capacity, None, self.capacity * self.groups(),
-                                         paged.sm_count(q.device))
+            sms = paged.sm_count(q.device)
+            self.pages_per_split = max(1, -(-self.capacity * self.groups() // sms))
+            _, nsplit = paged.split_plan(self.capacity, self.pages_per_split)
             self.workspace = paged.AttentionWorkspace(1, self.q_heads, self.head_dim,
                                                       max(1, nsplit), device=q.device)
         paged.paged_decode_attention_packed(q, pool, self.table, self.ctx, scale,
                                             packed=self.packed, max_pages_in_batch=self.capacity,
+                                            pages_per_split=self.pages_per_split,
                                             total_pages=self.capacity, workspace=self.workspace)
         if all_gather is None:
             import torch.distributed as dist
