@@ -82,6 +82,9 @@ def parse():
                     help="only time one attention layer on 8-bit pages beside bf16 pages for "
                          "--batch sequences of U[--min-len, --max-len] tokens; prints a JSON "
                          "object (a profiling entry, not a bench line)")
+    ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+                    help="config 4, N > 1: exchange the attention partials by NVLink peer "
+                         "stores with epoch flags (p2p) or by an NCCL all-gather")
     ap.add_argument("--config", type=int, choices=(3, 4), default=3,
                     help="3: ragged batch decode step (default); 4: one long sequence with its "
                          "KV pages split across the GPUs")
@@ -832,7 +835,8 @@ def cpu_baseline(args, wl):
 def run_config4(args, world, rank, local):
     """Config 4: one sequence of --ctx4 tokens; its KV pages are split evenly across the
     ranks (contiguous ranges), the GDN state (32 heads) is updated on every rank, and each
-    attention layer all-gathers the per-rank (out, lse) partials over NCCL."""
+    attention layer sends the per-rank (out, lse) partial to every rank: NVLink peer
+    stores with epoch flags (--exchange p2p, default) or an NCCL all-gather (nccl)."""
     import torch
     import torch.distributed as dist
 
@@ -847,6 +851,9 @@ def run_config4(args, world, rank, local):
     hq, hkv, d = 16, 2, 256
     shard = ShardedSequence(args.ctx4, rank, world, attention_layers=n_attn, kv_heads=hkv,
                             head_dim=d, q_heads=hq, headroom_pages=8, device=device)
+    use_p2p = world > 1 and args.exchange == "p2p"
+    if use_p2p:
+        shard.enable_peer_exchange()
     gen = torch.Generator(device=device)
     gen.manual_seed(4)
     block = torch.randn(1 << 26, generator=gen, device=device).to(torch.bfloat16)
@@ -904,9 +911,21 @@ def run_config4(args, world, rank, local):
     torch.cuda.synchronize()
     local_ms = e0.elapsed_time(e1)
     ms = max_over_ranks(local_ms, world)
-    # The exchange alone: the all-gather of one layer's packed partial.
+    # The exchange alone: one layer's packed partial to every rank.
     ag_ms = None
-    if world > 1:
+    if use_p2p:
+        for i in range(5):
+            shard.peer.put_and_wait(shard.packed, shard.epoch, 1 << 20 | i, i & 1)
+        torch.cuda.synchronize()
+        barrier(world)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for i in range(50):
+            shard.peer.put_and_wait(shard.packed, shard.epoch, (1 << 20) + 8 + i, i & 1)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ag_ms = max_over_ranks(a0.elapsed_time(a1) / 50, world)
+    elif world > 1:
         for _ in range(5):
             dist.all_gather_into_tensor(shard.gathered, shard.packed)
         torch.cuda.synchronize()
@@ -919,6 +938,8 @@ def run_config4(args, world, rank, local):
         ag_ms = max_over_ranks(a0.elapsed_time(a1) / 50, world)
     _capi.check_device()
     del graph  # release the graph (it holds NCCL work) before the process group goes
+    barrier(world)
+    shard.close()
     bytes_rank = n_attn * (shard.local_tokens * hkv * d * 2 * 2) + 36 * 4210944
     bytes_all = sum_over_ranks(float(bytes_rank), world)
     if rank != 0:
@@ -933,11 +954,14 @@ def run_config4(args, world, rank, local):
         "dtype": "bf16 kv / fp32 gdn state", "data": "synthetic",
         "config": {"workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN "
                                f"replicated + 12 attention with KV pages split over {world} GPU)",
-                   "parallelism": f"KV-page sharding x{world}, NCCL all-gather of (out, lse)"},
+                   "parallelism": f"KV-page sharding x{world}, "
+                                  + ("NVLink peer stores of (out, lse) with epoch flags"
+                                     if use_p2p else "NCCL all-gather of (out, lse)")},
         "hbm": {"bytes_per_step_all_ranks": bytes_all,
                 "gbs_per_gpu": round(bytes_all / world / per_step / 1e9, 1),
                 "frac_per_gpu": round(bytes_all / world / per_step / 1e9 / peaks["hbm_gbs"], 4)},
-        "all_gather_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
+        "exchange_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
+        "exchange": ("p2p" if use_p2p else "nccl") if world > 1 else None,
         "all_gather_bytes_per_rank": hq * (d + 1) * 4,
     }
     print(json.dumps(line), flush=True)

@@ -317,6 +317,25 @@ int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16* kv_pool,
 int sc_attention_combine_packed(const float* gathered, int nparts, int rows, int D,
                                 sc_bf16* out, float* lse_out, void* stream);
 
+/* --------------------------------------------------------------------------
+ * (e) Peer exchange of the packed partials over NVLink (replaces the NCCL
+ * all-gather of step 3 of the KV-sharded sequence; no reference counterpart).
+ *
+ * sc_exchange_put: one CTA per rank p copies `bytes` (a multiple of 16) from
+ * src to peer_dst[p] (this rank's slot in rank p's receive buffer, mapped
+ * with CUDA IPC), then release-stores *epoch_base + epoch_add into
+ * *peer_flag[p] (rank p's flag for this rank). peer_dst and peer_flag are
+ * device arrays of `world` device addresses.
+ * sc_exchange_wait: waits (bounded; a timeout sets the device status word)
+ * until flags[r] >= *epoch_base + epoch_add for every rank r < world. Kernels
+ * after it on the stream see every rank's block. Plain stores and loads over
+ * NVLink only (no multicast). */
+int sc_exchange_put(const void* src, long long bytes, void* const* peer_dst,
+                    unsigned int* const* peer_flag, const unsigned int* epoch_base,
+                    unsigned int epoch_add, int world, void* stream);
+int sc_exchange_wait(const unsigned int* flags, int world, const unsigned int* epoch_base,
+                     unsigned int epoch_add, void* stream);
+
 /* Split-K decode attention that allocates nothing and takes no scratch.
  *
  * No counterpart in the reference: it exists for callers of this library

@@ -11,7 +11,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libshellcache.so"
 SOURCES = ("status.cu", "gdn_decode.cu", "gdn_front.cu", "gdn_chunk.cu", "paged_kv.cu",
-           "paged_attention.cu", "paged_q8.cu")
+           "paged_attention.cu", "paged_q8.cu", "exchange.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

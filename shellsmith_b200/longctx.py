@@ -7,15 +7,19 @@ layer and decode token:
   1. the rank that owns the tail page appends the new token's K/V;
   2. every rank computes its split-K partial over its own pages: normalised
      fp32 output and lse, packed [Hq, D + 1] (sc_paged_decode_attention_packed);
-  3. the ranks all-gather the packed partials (NCCL over NVLink; Hq (D + 1) 4
-     bytes = 16.4 KB per rank at Hq 16, D 256) -- the one exchange of the path;
+  3. the ranks exchange the packed partials (Hq (D + 1) 4 bytes = 16.4 KB per
+     rank at Hq 16, D 256) -- the one exchange of the path: either each rank
+     stores its block straight into every peer's receive buffer over NVLink and
+     raises an epoch flag there (PeerExchange: sc_exchange_put / sc_exchange_wait
+     over CUDA IPC mappings), or an NCCL all-gather;
   4. every rank merges the gathered parts into the same bf16 output
      (sc_attention_combine_packed).
 The GDN layers' state (32 heads x 128 x 128 fp32, 2 MiB) is small and is
 updated identically on every rank.
 
 `PageRanges` is the host-only partition (tested on CPU with gloo ranks);
-`ShardedSequence` owns the device pools of one rank.
+`ShardedSequence` owns the device pools of one rank; `PeerExchange` owns the
+NVLink receive buffers.
 """
 
 from __future__ import annotations
@@ -24,7 +28,8 @@ import math
 
 import torch
 
-from . import paged
+from . import _capi, paged
+from ._torch import ptr, stream_of
 
 
 class PageRanges:
@@ -46,6 +51,92 @@ class PageRanges:
             if self.starts[r] <= page < self.starts[r + 1]:
                 return r
         return self.world - 1  # pages past the split belong to the tail rank
+
+
+def _cudart():
+    from cuda.bindings import runtime as cudart
+
+    return cudart
+
+
+def _check(result, what):
+    err = result[0]
+    if int(err) != 0:
+        raise RuntimeError(f"{what} failed: {err}")
+    return result[1] if len(result) > 1 else None
+
+
+class PeerExchange:
+    """NVLink receive buffers for the packed partials of `world` ranks.
+
+    Each rank allocates [2 parities][world][rows][D + 1] fp32 plus [world] uint32
+    epoch flags in one cudaMalloc block, shares it with CUDA IPC, and maps every
+    peer's block, so its put kernel stores straight into the peers' memory. The
+    process group only carries the IPC handles once (all_gather_object)."""
+
+    def __init__(self, rows: int, width: int, rank: int, world: int, group=None,
+                 device="cuda"):
+        import torch.distributed as dist
+
+        cudart = _cudart()
+        self.rows, self.width, self.rank, self.world = rows, width, rank, world
+        self.block = rows * width * 4                                # one rank's partial
+        if self.block % 16:
+            raise ValueError("PeerExchange: rows * (D + 1) * 4 must be a multiple of 16")
+        self.flags_off = 2 * world * self.block
+        nbytes = self.flags_off + ((world * 4 + 255) // 256) * 256
+        dev = torch.device(device)
+        self.device = dev
+        with torch.cuda.device(dev):
+            self.base = int(_check(cudart.cudaMalloc(nbytes), "cudaMalloc"))
+            _check(cudart.cudaMemset(self.base, 0, nbytes), "cudaMemset")
+            handle = _check(cudart.cudaIpcGetMemHandle(self.base), "cudaIpcGetMemHandle")
+        raw = bytes(handle.reserved)
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, raw, group=group)
+        else:
+            handles = [raw]
+        self.peer_bases, self._opened = [], []
+        with torch.cuda.device(dev):
+            for r, h in enumerate(handles):
+                if r == rank:
+                    self.peer_bases.append(self.base)
+                    continue
+                mh = cudart.cudaIpcMemHandle_t()
+                mh.reserved = h
+                p = int(_check(cudart.cudaIpcOpenMemHandle(
+                    mh, cudart.cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+                self.peer_bases.append(p)
+                self._opened.append(p)
+        # Per parity: where this rank's block goes on each peer, and each peer's flag for it.
+        self.dst = [torch.tensor([b + (par * world + rank) * self.block for b in self.peer_bases],
+                                 dtype=torch.int64, device=dev) for par in (0, 1)]
+        self.flag_ptrs = torch.tensor([b + self.flags_off + 4 * rank for b in self.peer_bases],
+                                      dtype=torch.int64, device=dev)
+
+    def gathered(self, parity: int) -> int:
+        """Device address of this rank's received [world][rows][D + 1] blocks."""
+        return self.base + parity * self.world * self.block
+
+    def put_and_wait(self, packed: torch.Tensor, epoch: torch.Tensor, epoch_add: int,
+                     parity: int) -> None:
+        stream = stream_of(packed)
+        _capi.call("sc_exchange_put", ptr(packed), self.block, ptr(self.dst[parity]),
+                   ptr(self.flag_ptrs), ptr(epoch), epoch_add, self.world, stream)
+        _capi.call("sc_exchange_wait", self.base + self.flags_off, self.world, ptr(epoch),
+                   epoch_add, stream)
+
+    def close(self) -> None:
+        cudart = _cudart()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                cudart.cudaIpcCloseMemHandle(p)
+            self._opened = []
+            if self.base:
+                cudart.cudaFree(self.base)
+                self.base = 0
 
 
 class ShardedSequence:
@@ -85,6 +176,10 @@ class ShardedSequence:
         self.out = torch.empty((q_heads, head_dim), dtype=torch.bfloat16, device=device)
         self.workspace = None
         self.pages_per_split = None
+        self.peer = None      # PeerExchange, when enable_peer_exchange() was called
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self._h_epoch = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.tokens_done = 0
 
     def begin_token(self) -> None:
         """Stage the next decode token: the tail rank appends it after its last token.
@@ -101,10 +196,31 @@ class ShardedSequence:
         else:
             self._h_slot[0] = -1
         self._h_ctx[0] = self.local_tokens
+        # Exchange epochs: attention layer l of this token raises flags to base + l + 1.
+        # The kernels add and compare modulo 2^32, so the base wraps like a u32
+        # (stored in an int32 tensor as its two's-complement image).
+        e = (self.tokens_done * self.kv.shape[0]) & 0xFFFFFFFF
+        self._h_epoch[0] = e - (1 << 32) if e >= 1 << 31 else e
+        self.tokens_done += 1
         self.slot.copy_(self._h_slot, non_blocking=True)
         self.ctx.copy_(self._h_ctx, non_blocking=True)
+        self.epoch.copy_(self._h_epoch, non_blocking=True)
         self._staged = torch.cuda.Event()
         self._staged.record()
+
+    def enable_peer_exchange(self, group=None) -> None:
+        """Exchange the packed partials by NVLink stores instead of NCCL (collective:
+        every rank calls it)."""
+        if self.kv.shape[0] % 2:
+            raise ValueError("peer exchange alternates receive buffers per attention layer: "
+                             "it needs an even number of attention layers")
+        self.peer = PeerExchange(self.q_heads, self.head_dim + 1, self.rank, self.world,
+                                 group=group, device=self.kv.device)
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def groups(self) -> int:
         hkv = self.kv.shape[2]
@@ -129,6 +245,12 @@ class ShardedSequence:
                                             packed=self.packed, max_pages_in_batch=self.capacity,
                                             pages_per_split=self.pages_per_split,
                                             total_pages=self.capacity, workspace=self.workspace)
+        if self.peer is not None:
+            parity = (layer + 1) & 1   # the parity of this call's epoch (even layer count)
+            self.peer.put_and_wait(self.packed, self.epoch, layer + 1, parity)
+            _capi.call("sc_attention_combine_packed", self.peer.gathered(parity), self.world,
+                       self.q_heads, self.head_dim, ptr(self.out), None, stream_of(self.out))
+            return self.out
         if all_gather is None:
             import torch.distributed as dist
 

@@ -3,8 +3,10 @@
 Single-GPU: W ranks are emulated as W ShardedSequence objects on one device
 (each with its own pool); their packed partials are stacked as the all-gather
 would and merged with sc_attention_combine_packed. Two GPUs (when present):
-two processes, NCCL all-gather. Both are checked against the CPU oracle on
-the whole sequence, rtol 2e-2 / atol 2e-3.
+two processes, NCCL all-gather, and the NVLink peer exchange (put + epoch
+flags) over two layers and two tokens, which must give bit-identical outputs
+to the NCCL path. All are checked against the CPU oracle on the whole
+sequence, rtol 2e-2 / atol 2e-3.
 """
 
 import math
@@ -135,3 +137,110 @@ def test_two_gpus_nccl_all_gather():
                                         v.float().numpy(), 1 / 16)
         for r in range(2):
             np.testing.assert_allclose(result[r], want, rtol=RTOL, atol=ATOL)
+
+
+def _p2p_worker(rank, world, port, tokens, result):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    dev = f"cuda:{rank}"
+    try:
+        q, k, v = _sequence(tokens + 1)
+        shards = {}
+        for mode in ("nccl", "p2p"):
+            s = ShardedSequence(tokens, rank, world, attention_layers=2, kv_heads=HKV,
+                                head_dim=D, q_heads=HQ, device=dev)
+            lo = s.first_page * paged.PAGE_SIZE
+            if s.local_tokens:
+                slots = torch.arange(s.local_tokens, dtype=torch.int64, device=dev)
+                for layer in range(2):
+                    paged.kv_append(k[lo:lo + s.local_tokens].to(dev),
+                                    v[lo:lo + s.local_tokens].to(dev), s.kv[layer], slots)
+            if mode == "p2p":
+                s.enable_peer_exchange()
+            shards[mode] = s
+        outs = {"nccl": [], "p2p": []}
+        for step in range(2):
+            t = tokens + step
+            for mode, s in shards.items():
+                s.begin_token()
+                for layer in range(2):
+                    out = s.attention(layer, q.to(dev), k[t:t + 1].to(dev), v[t:t + 1].to(dev),
+                                      1 / 16)
+                    outs[mode].append(out.float().cpu().numpy())
+        torch.cuda.synchronize()
+        from shellsmith_b200 import _capi
+
+        _capi.check_device()
+        result[rank] = outs
+        shards["p2p"].close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpus_peer_exchange_matches_nccl():
+    import torch.multiprocessing as mp
+
+    tokens = 10000
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        result = manager.dict()
+        procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, tokens, result))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+        q, k, v = _sequence(tokens + 1)
+        for r in range(2):
+            outs = result[r]
+            for i, (a, b) in enumerate(zip(outs["nccl"], outs["p2p"])):
+                assert np.array_equal(a, b), (r, i)
+            for step in range(2):
+                n = tokens + 1 + step
+                want, _ = oatt.decode_attention(q[0].float().numpy(), k[:n].float().numpy(),
+                                                v[:n].float().numpy(), 1 / 16)
+                for layer in range(2):
+                    np.testing.assert_allclose(outs["p2p"][2 * step + layer], want, rtol=RTOL,
+                                               atol=ATOL)
+
+
+def test_peer_exchange_single_rank_matches_local_path(cuda):
+    """World 1: the put/flag/wait kernels run against this GPU's own buffer."""
+    tokens = 3000
+    q, k, v = _sequence(tokens + 1)
+    shards = []
+    for use_peer in (False, True):
+        s = ShardedSequence(tokens, 0, 1, attention_layers=2, kv_heads=HKV, head_dim=D,
+                            q_heads=HQ)
+        for layer in range(2):
+            _fill(s, k, v, layer)
+        if use_peer:
+            s.enable_peer_exchange()
+        shards.append(s)
+
+    def gather(dst, src):
+        dst[0].copy_(src)
+
+    for step in range(2):
+        t = tokens + step
+        for s in shards:
+            s.begin_token()
+        for layer in range(2):
+            a = shards[0].attention(layer, q.cuda(), k[t:t + 1].cuda(), v[t:t + 1].cuda(), 1 / 16,
+                                    all_gather=gather).clone()
+            b = shards[1].attention(layer, q.cuda(), k[t:t + 1].cuda(), v[t:t + 1].cuda(), 1 / 16)
+            torch.cuda.synchronize()
+            assert torch.equal(a, b)
+    from shellsmith_b200 import _capi
+
+    _capi.check_device()
+    shards[1].close()
