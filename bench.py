@@ -82,9 +82,11 @@ def parse():
                     help="only time one attention layer on 8-bit pages beside bf16 pages for "
                          "--batch sequences of U[--min-len, --max-len] tokens; prints a JSON "
                          "object (a profiling entry, not a bench line)")
-    ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+    ap.add_argument("--exchange", choices=("fused", "p2p", "nccl"), default="p2p",
                     help="config 4, N > 1: exchange the attention partials by NVLink peer "
-                         "stores with epoch flags (p2p) or by an NCCL all-gather")
+                         "stores with epoch flags, issued by the attention merge itself "
+                         "(fused) or by a separate put/wait kernel pair (p2p), or by an "
+                         "NCCL all-gather (nccl)")
     ap.add_argument("--config", type=int, choices=(3, 4), default=3,
                     help="3: ragged batch decode step (default); 4: one long sequence with its "
                          "KV pages split across the GPUs")
@@ -851,9 +853,9 @@ def run_config4(args, world, rank, local):
     hq, hkv, d = 16, 2, 256
     shard = ShardedSequence(args.ctx4, rank, world, attention_layers=n_attn, kv_heads=hkv,
                             head_dim=d, q_heads=hq, headroom_pages=8, device=device)
-    use_p2p = world > 1 and args.exchange == "p2p"
+    use_p2p = world > 1 and args.exchange != "nccl"
     if use_p2p:
-        shard.enable_peer_exchange()
+        shard.enable_peer_exchange(fused=args.exchange == "fused")
     gen = torch.Generator(device=device)
     gen.manual_seed(4)
     block = torch.randn(1 << 26, generator=gen, device=device).to(torch.bfloat16)
@@ -869,10 +871,6 @@ def run_config4(args, world, rank, local):
                 torch.randn((1, hkv, d), generator=gen, device=device).to(torch.bfloat16),
                 torch.randn((1, hkv, d), generator=gen, device=device).to(torch.bfloat16))
                for _ in range(n_attn)]
-    gather = None
-    if world == 1:
-        def gather(dst, src):
-            dst[0].copy_(src)
     stream = torch.cuda.current_stream(device)
 
     def layers():
@@ -880,7 +878,7 @@ def run_config4(args, world, rank, local):
         for layer in range(L):
             if layer % 4 == 3:
                 q, k, v = attn_in[a_i]
-                shard.attention(a_i, q, k, v, 1 / 16, all_gather=gather)
+                shard.attention(a_i, q, k, v, 1 / 16)
                 a_i += 1
             else:
                 numerics.gdn_decode(*gdn_in[g_i], state[g_i], out=gdn_out)
@@ -955,13 +953,18 @@ def run_config4(args, world, rank, local):
         "config": {"workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN "
                                f"replicated + 12 attention with KV pages split over {world} GPU)",
                    "parallelism": f"KV-page sharding x{world}, "
-                                  + ("NVLink peer stores of (out, lse) with epoch flags"
-                                     if use_p2p else "NCCL all-gather of (out, lse)")},
+                                  + {"fused": "attention merge stores (out, lse) into the "
+                                              "peers over NVLink, epoch flags",
+                                     "p2p": "put/wait kernels store (out, lse) into the peers "
+                                            "over NVLink, epoch flags",
+                                     "nccl": "NCCL all-gather of (out, lse)"}[args.exchange]},
         "hbm": {"bytes_per_step_all_ranks": bytes_all,
                 "gbs_per_gpu": round(bytes_all / world / per_step / 1e9, 1),
                 "frac_per_gpu": round(bytes_all / world / per_step / 1e9 / peaks["hbm_gbs"], 4)},
+        # One layer's partial to every rank, timed alone: the put/wait kernel pair
+        # (fused and p2p) or the all-gather (nccl).
         "exchange_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
-        "exchange": ("p2p" if use_p2p else "nccl") if world > 1 else None,
+        "exchange": args.exchange if world > 1 else None,
         "all_gather_bytes_per_rank": hq * (d + 1) * 4,
     }
     print(json.dumps(line), flush=True)

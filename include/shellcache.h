@@ -336,6 +336,31 @@ int sc_exchange_put(const void* src, long long bytes, void* const* peer_dst,
 int sc_exchange_wait(const unsigned int* flags, int world, const unsigned int* epoch_base,
                      unsigned int epoch_add, void* stream);
 
+/* The same exchange folded into the attention kernels (two launches fewer per
+ * layer):
+ * sc_paged_decode_attention_exchange: sc_paged_decode_attention_packed whose
+ * split merge stores the packed rows [B * Hq][D + 1] straight into
+ * peer_dst[p] for every rank p (float* device addresses) and, once every row
+ * is out, release-stores *epoch_base + epoch_add into *peer_flag[p].
+ * `counter` is a device word that is zero before the first call (the kernel
+ * leaves it zero). Needs num_splits > 1.
+ * sc_attention_combine_exchange: sc_attention_combine_packed that first waits
+ * (bounded, as sc_exchange_wait) for flags[r] to reach the epoch for every
+ * r < nparts; after a timeout it writes nothing and sets the status word. */
+int sc_paged_decode_attention_exchange(const sc_bf16* q, const sc_bf16* kv_pool,
+                                       int64_t num_pages, const int32_t* block_table,
+                                       const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
+                                       int P, int max_pages, int pages_per_split,
+                                       int num_splits, float scale, float* part_out,
+                                       float* part_lse, float* const* peer_dst,
+                                       unsigned int* const* peer_flag, unsigned int* counter,
+                                       const unsigned int* epoch_base, unsigned int epoch_add,
+                                       int world, void* stream);
+int sc_attention_combine_exchange(const float* gathered, const unsigned int* flags,
+                                  const unsigned int* epoch_base, unsigned int epoch_add,
+                                  int nparts, int rows, int D, sc_bf16* out, float* lse_out,
+                                  void* stream);
+
 /* Split-K decode attention that allocates nothing and takes no scratch.
  *
  * No counterpart in the reference: it exists for callers of this library

@@ -8,6 +8,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <utility>
 
 #include "../../include/shellcache.h"
 
@@ -35,6 +36,37 @@ unsigned int* device_status_word();
 
 __device__ __forceinline__ void flag_device(unsigned int* status, unsigned int bits) {
   if (status != nullptr) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------- dependent launch
+// Kernels of one decode step are launched as programmatic dependents of the
+// kernel before them (launch_pdl): the next grid is scheduled while the
+// current one runs, which hides the per-launch gap of a step made of many
+// small kernels. A kernel launched that way calls pdl_wait() before it touches
+// memory at all (every earlier kernel's writes are visible after it, and no
+// earlier kernel still reads what it writes), then pdl_trigger(): the next
+// grid launches once every CTA of this one has triggered or exited, so its
+// CTAs only take resources this grid no longer needs. Both are no-ops in an
+// ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- bf16 helpers

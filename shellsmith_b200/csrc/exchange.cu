@@ -17,20 +17,10 @@
 // one layer ahead (its next put waits on this GPU's previous put through its
 // own wait), so it never overwrites a block this GPU has not merged.
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace sc {
 namespace {
-
-constexpr uint32_t kSpinLimit = 1u << 24;  // ~seconds with the back-off below
-
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // grid = world CTAs: CTA p copies `bytes` (a multiple of 16) from src to
 // peer_dst[p], then sets *peer_flag[p] = epoch.
@@ -38,6 +28,8 @@ __global__ void __launch_bounds__(256)
     exchange_put_kernel(const uint4* __restrict__ src, int chunks, uint4* const* peer_dst,
                         unsigned int* const* peer_flag, const unsigned int* epoch_base,
                         unsigned int epoch_add) {
+  pdl_wait();
+  pdl_trigger();
   const int p = blockIdx.x;
   uint4* dst = peer_dst[p];
   for (int i = threadIdx.x; i < chunks; i += blockDim.x) dst[i] = src[i];
@@ -48,23 +40,14 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// One thread waits until flags[r] >= epoch for every r < world (wrap-safe
-// comparison); on timeout it flags the device status word.
+// One thread waits until flags[r] has reached the epoch for every r < world.
 __global__ void exchange_wait_kernel(const unsigned int* flags, int world,
                                      const unsigned int* epoch_base, unsigned int epoch_add,
                                      unsigned int* status) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x != 0) return;
-  const unsigned int want = *epoch_base + epoch_add;
-  for (int r = 0; r < world; ++r) {
-    uint32_t i = 0;
-    while ((int)(ld_acquire_sys(flags + r) - want) < 0) {
-      if (++i >= kSpinLimit) {
-        flag_device(status, DEV_WAIT_TIMEOUT);
-        return;
-      }
-      if (i > 64) __nanosleep(64);
-    }
-  }
+  wait_epochs(flags, world, *epoch_base + epoch_add, status);
 }
 
 }  // namespace
@@ -83,9 +66,9 @@ extern "C" int sc_exchange_put(const void* src, long long bytes, void* const* pe
              bytes);
   SC_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0, SC_ERR_INVALID,
              "%s: src must be 16-byte aligned", name);
-  exchange_put_kernel<<<world, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(src), (int)(bytes / 16),
-      reinterpret_cast<uint4* const*>(peer_dst), peer_flag, epoch_base, epoch_add);
+  launch_pdl(exchange_put_kernel, dim3(world), dim3(256), 0, static_cast<cudaStream_t>(stream),
+             static_cast<const uint4*>(src), (int)(bytes / 16),
+             reinterpret_cast<uint4* const*>(peer_dst), peer_flag, epoch_base, epoch_add);
   return check_launch(name);
 }
 
@@ -96,7 +79,7 @@ extern "C" int sc_exchange_wait(const unsigned int* flags, int world,
   const char* name = "sc_exchange_wait";
   SC_REQUIRE(flags && epoch_base, SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE(world > 0 && world <= 1024, SC_ERR_INVALID, "%s: world=%d", name, world);
-  exchange_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      flags, world, epoch_base, epoch_add, device_status_word());
+  launch_pdl(exchange_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+             flags, world, epoch_base, epoch_add, device_status_word());
   return check_launch(name);
 }

@@ -187,9 +187,13 @@ __global__ void __launch_bounds__(128)
                            const uint16_t* __restrict__ v, const float* __restrict__ g,
                            const float* __restrict__ beta, float* __restrict__ state,
                            const int32_t* __restrict__ state_slot, uint16_t* __restrict__ out,
-                           int Hk, int Hv, int dv, int num_slots, unsigned int* status) {
+                           int Hk, int Hv, int dv, int num_slots, int wait_first,
+                           unsigned int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int nchunks = NCH;
+  // A dependent launch whose predecessor may write the state (or anything
+  // else this kernel reads) waits before touching memory at all.
+  if (wait_first) pdl_wait();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nchunks * kBulkChunkBytes);
   const int chunk0 = blockIdx.y * nchunks;  // first 32-row chunk of this CTA
   const int bh = blockIdx.x;
@@ -223,7 +227,8 @@ __global__ void __launch_bounds__(128)
   // Launched as a programmatic dependent of the kernel that makes q/k/v/g/beta,
   // the state loads above overlap that kernel; its outputs are read only after
   // this wait (a no-op in an ordinary launch).
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_wait();
+  pdl_trigger();
   const float4 kf = load_bf16x4(k + ((size_t)b * Hk + kh) * 128 + 4 * lane);
   const float4 qf = load_bf16x4(q + ((size_t)b * Hk + kh) * 128 + 4 * lane);
   const float decay = g[bh], bt = beta[bh];
@@ -293,7 +298,7 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
   if constexpr (std::is_same<ST, float>::value) {
     if (gdn_bulk_supported(dk, dv))
       return gdn_bulk_launch(name, q, k, v, g, beta, state, slot, out, B, Hk, Hv, dv, num_slots,
-                             s, false);
+                             s, BulkLaunch::kDependent);
   }
   dim3 block(kWarps * 32);
 #define SC_GDN_CASE(DK_)                                                                     \
@@ -325,7 +330,7 @@ bool gdn_bulk_supported(int dk, int dv) {
 int gdn_bulk_launch(const char* name, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                     const float* g, const float* beta, float* state, const int32_t* slot,
                     uint16_t* out, int B, int Hk, int Hv, int dv, int num_slots, cudaStream_t s,
-                    bool programmatic) {
+                    BulkLaunch mode) {
   static int configured[64] = {};
   static int sms[64] = {};
   int dev = 0;
@@ -354,12 +359,13 @@ int gdn_bulk_launch(const char* name, const uint16_t* q, const uint16_t* k, cons
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = programmatic ? 1 : 0;
+  cfg.numAttrs = mode == BulkLaunch::kOrdinary ? 0 : 1;
+  const int wait_first = mode == BulkLaunch::kDependent ? 1 : 0;
   cudaError_t err =
       small ? cudaLaunchKernelEx(&cfg, gdn_decode_bulk_kernel<1>, q, k, v, g, beta, state, slot,
-                                 out, Hk, Hv, dv, num_slots, device_status_word())
+                                 out, Hk, Hv, dv, num_slots, wait_first, device_status_word())
             : cudaLaunchKernelEx(&cfg, gdn_decode_bulk_kernel<kBulkChunksPerCta>, q, k, v, g,
-                                 beta, state, slot, out, Hk, Hv, dv, num_slots,
+                                 beta, state, slot, out, Hk, Hv, dv, num_slots, wait_first,
                                  device_status_word());
   if (err != cudaSuccess)
     return set_error(SC_ERR_CUDA, "%s: launch: %s", name, cudaGetErrorString(err));

@@ -26,6 +26,7 @@
 
 #include "attention_internal.cuh"
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace sc {
 namespace {
@@ -55,6 +56,8 @@ __global__ void __launch_bounds__(NW * 32)
   using S = AttnShape<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NW * NSTAGE * S::STAGE_BYTES);
+  pdl_wait();
+  pdl_trigger();
 
   // After any bounded wait has given up on this device, later CTAs stop at
   // once instead of each waiting out its own limit.
@@ -311,14 +314,26 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
+// With kWait the CTA first waits (one thread, bounded) until every part's
+// producer has published `wait`'s epoch; if that wait gives up it writes nothing.
+template <bool kWait>
 __global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const float* __restrict__ po, const float* __restrict__ pl, size_t o_row,
                    size_t o_part, size_t l_row, size_t l_part,
                    const int32_t* __restrict__ ctx_len, int Hq, int nparts, int pages_per_split,
                    int D, uint16_t* __restrict__ out, float* __restrict__ lse_out,
-                   float* __restrict__ packed) {
+                   float* __restrict__ packed, PeerWait wait) {
   __shared__ float w[kCombineWindow];
   __shared__ float red[kCombineThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  if constexpr (kWait) {
+    __shared__ int ready;
+    if (threadIdx.x == 0)
+      ready = wait_epochs(wait.flags, wait.world, *wait.epoch_base + wait.epoch_add, wait.status);
+    __syncthreads();
+    if (!ready) return;
+  }
   const int row = blockIdx.x;
   int ns = nparts;
   if (ctx_len != nullptr) {
@@ -384,15 +399,22 @@ __global__ void __launch_bounds__(kCombineThreads)
 // splits, or many devices): one CTA per (row, 32-dim tile), lane = dim, and
 // the four warps take every fourth part, so each part's 128-byte slice is one
 // coalesced load and the row's work spreads over D / 32 CTAs.
+// With kPut the merged row is stored, packed, into every rank's receive slot
+// for this rank (`put.dst`, over NVLink) instead of `packed`; the CTA that
+// arrives last on `put.counter` resets it and publishes the epoch in every
+// rank's flag for this rank (system-scope release).
+template <bool kPut>
 __global__ void __launch_bounds__(kCombineThreads)
     combine_tiled_kernel(const float* __restrict__ po, const float* __restrict__ pl,
                          size_t o_row, size_t o_part, size_t l_row, size_t l_part,
                          const int32_t* __restrict__ ctx_len, int Hq, int nparts,
                          int pages_per_split, int D, uint16_t* __restrict__ out,
-                         float* __restrict__ lse_out, float* __restrict__ packed) {
+                         float* __restrict__ lse_out, float* __restrict__ packed, PeerPut put) {
   __shared__ float w[kCombineWindow];
   __shared__ float red[kCombineThreads / 32];
   __shared__ float part_acc[kCombineThreads / 32][32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int d = blockIdx.y * 32 + lane;
@@ -450,16 +472,37 @@ __global__ void __launch_bounds__(kCombineThreads)
     for (int k = 0; k < kCombineThreads / 32; ++k) total += part_acc[k][lane];
     const bool empty = M == -CUDART_INF_F;
     const float val = empty ? 0.f : total / wsum;
-    if (packed != nullptr)
-      packed[(size_t)row * (D + 1) + d] = val;
-    else
-      out[(size_t)row * D + d] = f_to_bf16(val);
-    if (blockIdx.y == 0 && lane == 0) {
-      const float l = empty ? -CUDART_INF_F : M + logf(wsum);
+    const float l = empty ? -CUDART_INF_F : M + logf(wsum);
+    if constexpr (kPut) {
+      for (int p = 0; p < put.world; ++p) {
+        float* dst = put.dst[p] + (size_t)row * (D + 1);
+        dst[d] = val;
+        if (blockIdx.y == 0 && lane == 0) dst[D] = l;
+      }
+    } else {
       if (packed != nullptr)
-        packed[(size_t)row * (D + 1) + D] = l;
-      else if (lse_out != nullptr)
-        lse_out[row] = l;
+        packed[(size_t)row * (D + 1) + d] = val;
+      else
+        out[(size_t)row * D + d] = f_to_bf16(val);
+      if (blockIdx.y == 0 && lane == 0) {
+        if (packed != nullptr)
+          packed[(size_t)row * (D + 1) + D] = l;
+        else if (lse_out != nullptr)
+          lse_out[row] = l;
+      }
+    }
+  }
+  if constexpr (kPut) {
+    __syncthreads();  // this CTA's stores precede thread 0's fence below
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const unsigned int total = gridDim.x * gridDim.y;
+      if (atomicAdd(put.counter, 1u) == total - 1) {
+        *put.counter = 0;  // ready for the next launch (stream order)
+        __threadfence_system();
+        const unsigned int epoch = *put.epoch_base + put.epoch_add;
+        for (int p = 0; p < put.world; ++p) st_release_sys(put.flag[p], epoch);
+      }
     }
   }
 }
@@ -474,13 +517,13 @@ void launch_combine(const float* po, const float* pl, size_t o_row, size_t o_par
                     float* packed, cudaStream_t s) {
   if (nparts >= 16) {
     dim3 grid(rows, (D + 31) / 32);
-    combine_tiled_kernel<<<grid, kCombineThreads, 0, s>>>(po, pl, o_row, o_part, l_row, l_part,
-                                                          ctx_len, Hq, nparts, pages_per_split,
-                                                          D, out, lse_out, packed);
+    launch_pdl(combine_tiled_kernel<false>, grid, dim3(kCombineThreads), 0, s, po, pl, o_row,
+               o_part, l_row, l_part, ctx_len, Hq, nparts, pages_per_split, D, out, lse_out,
+               packed, PeerPut{});
   } else {
-    combine_kernel<<<rows, kCombineThreads, 0, s>>>(po, pl, o_row, o_part, l_row, l_part,
-                                                    ctx_len, Hq, nparts, pages_per_split, D, out,
-                                                    lse_out, packed);
+    launch_pdl(combine_kernel<false>, dim3(rows), dim3(kCombineThreads), 0, s, po, pl, o_row,
+               o_part, l_row, l_part, ctx_len, Hq, nparts, pages_per_split, D, out, lse_out,
+               packed, PeerWait{});
   }
 }
 
@@ -502,7 +545,7 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
                   int max_pages,
                   int pages_per_split, int num_splits, float scale, float* part_out,
                   float* part_lse, uint16_t* out, float* lse_out, float* packed,
-                  long long num_pages, cudaStream_t s) {
+                  long long num_pages, const PeerPut* put, cudaStream_t s) {
   using S = AttnShape<D>;
   constexpr int NW = kWarpsPerCta, NST = kStages;
   const size_t smem = (size_t)NW * NST * S::STAGE_BYTES + NW * NST * sizeof(uint64_t);
@@ -522,11 +565,22 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
   const int HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(num_splits, Hkv * HG, B);
-  kernel<<<grid, NW * 32, smem, s>>>(q, kv_pool, block_table, ctx_len, seq_order, Hq, Hkv, G, HG,
-                                     max_pages,
-                                     pages_per_split, num_splits, scale_log2, part_out, part_lse,
-                                     out, lse_out, packed, num_pages, device_status_word());
+  cudaError_t err = launch_pdl(kernel, grid, dim3(NW * 32), smem, s, q, kv_pool, block_table,
+                               ctx_len, seq_order, Hq, Hkv, G, HG, max_pages, pages_per_split,
+                               num_splits, scale_log2, part_out, part_lse, out, lse_out, packed,
+                               num_pages, device_status_word());
+  if (err != cudaSuccess)
+    return set_error(SC_ERR_CUDA, "sc_paged_decode_attention: launch: %s",
+                     cudaGetErrorString(err));
   if (int rc = check_launch("sc_paged_decode_attention")) return rc;
+  if (put != nullptr) {  // the entry guarantees num_splits > 1
+    dim3 cgrid(B * Hq, (D + 31) / 32);
+    launch_pdl(combine_tiled_kernel<true>, cgrid, dim3(kCombineThreads), 0, s,
+               (const float*)part_out, (const float*)part_lse, (size_t)num_splits * D, (size_t)D,
+               (size_t)num_splits, (size_t)1, ctx_len, Hq, num_splits, pages_per_split, D,
+               (uint16_t*)nullptr, (float*)nullptr, (float*)nullptr, *put);
+    return check_launch("sc_paged_decode_attention_exchange(combine)");
+  }
   if (num_splits > 1) {
     launch_combine(part_out, part_lse, (size_t)num_splits * D, D, num_splits, 1, ctx_len, Hq,
                    num_splits, pages_per_split, D, B * Hq, out, lse_out, packed, s);
@@ -545,8 +599,8 @@ int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int
                  int B, int Hq, int Hkv,
                  int D, int P, int max_pages, int pages_per_split, int num_splits, float scale,
                  float* part_out, float* part_lse, sc_bf16* out, float* lse_out, float* packed,
-                 void* stream) {
-  SC_REQUIRE(q && kv_pool && block_table && ctx_len && (out || packed), SC_ERR_INVALID,
+                 const PeerPut* put, void* stream) {
+  SC_REQUIRE(q && kv_pool && block_table && ctx_len && (out || packed || put), SC_ERR_INVALID,
              "%s: null pointer", name);
   SC_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, SC_ERR_INVALID,
              "%s: bad heads Hq=%d Hkv=%d", name, Hq, Hkv);
@@ -566,17 +620,17 @@ int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int
       return launch_decode<64>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
                                  max_pages,
                                    pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                   lse_out, packed, num_pages, s);
+                                   lse_out, packed, num_pages, put, s);
     case 128:
       return launch_decode<128>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
                                  max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                    lse_out, packed, num_pages, s);
+                                    lse_out, packed, num_pages, put, s);
     case 256:
       return launch_decode<256>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
                                  max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                    lse_out, packed, num_pages, s);
+                                    lse_out, packed, num_pages, put, s);
     default:
       return set_error(SC_ERR_UNSUPPORTED, "%s: D=%d not in {64,128,256}", name, D);
   }
@@ -596,7 +650,7 @@ extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_poo
   return sc::decode_entry("sc_paged_decode_attention", q, kv_pool, num_pages, block_table,
                           ctx_len, seq_order, B, Hq, Hkv, D, P, max_pages, pages_per_split,
                           num_splits,
-                          scale, part_out, part_lse, out, lse_out, nullptr, stream);
+                          scale, part_out, part_lse, out, lse_out, nullptr, nullptr, stream);
 }
 
 extern "C" int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16* kv_pool,
@@ -611,7 +665,7 @@ extern "C" int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16*
                           block_table, ctx_len, nullptr, B, Hq, Hkv, D, P, max_pages,
                           pages_per_split,
                           num_splits, scale, part_out, part_lse, nullptr, nullptr, packed,
-                          stream);
+                          nullptr, stream);
 }
 
 extern "C" int sc_attention_combine_packed(const float* gathered, int nparts, int rows, int D,
@@ -625,6 +679,56 @@ extern "C" int sc_attention_combine_packed(const float* gathered, int nparts, in
   sc::launch_combine(gathered, gathered + D, stride, (size_t)rows * stride, stride,
                      (size_t)rows * stride, nullptr, 1, nparts, 1, D, rows, out, lse_out, nullptr,
                      static_cast<cudaStream_t>(stream));
+  return sc::check_launch(name);
+}
+
+extern "C" int sc_paged_decode_attention_exchange(
+    const sc_bf16* q, const sc_bf16* kv_pool, int64_t num_pages, const int32_t* block_table,
+    const int32_t* ctx_len, int B, int Hq, int Hkv, int D, int P, int max_pages,
+    int pages_per_split, int num_splits, float scale, float* part_out, float* part_lse,
+    float* const* peer_dst, unsigned int* const* peer_flag, unsigned int* counter,
+    const unsigned int* epoch_base, unsigned int epoch_add, int world, void* stream) {
+  const char* name = "sc_paged_decode_attention_exchange";
+  SC_REQUIRE(peer_dst && peer_flag && counter && epoch_base, SC_ERR_INVALID, "%s: null pointer",
+             name);
+  SC_REQUIRE(world > 0 && world <= 1024, SC_ERR_INVALID, "%s: world=%d", name, world);
+  SC_REQUIRE(num_splits > 1 && B > 0, SC_ERR_INVALID,
+             "%s: needs num_splits > 1 (got %d) and B > 0 (got %d)", name, num_splits, B);
+  SC_REQUIRE((long long)B * Hq <= 65535, SC_ERR_INVALID, "%s: B*Hq=%lld rows", name,
+             (long long)B * Hq);
+  sc::PeerPut put;
+  put.dst = peer_dst;
+  put.flag = peer_flag;
+  put.counter = counter;
+  put.epoch_base = epoch_base;
+  put.epoch_add = epoch_add;
+  put.world = world;
+  return sc::decode_entry(name, q, kv_pool, num_pages, block_table, ctx_len, nullptr, B, Hq, Hkv,
+                          D, P, max_pages, pages_per_split, num_splits, scale, part_out, part_lse,
+                          nullptr, nullptr, nullptr, &put, stream);
+}
+
+extern "C" int sc_attention_combine_exchange(const float* gathered, const unsigned int* flags,
+                                             const unsigned int* epoch_base,
+                                             unsigned int epoch_add, int nparts, int rows, int D,
+                                             sc_bf16* out, float* lse_out, void* stream) {
+  const char* name = "sc_attention_combine_exchange";
+  SC_REQUIRE(gathered && flags && epoch_base && out, SC_ERR_INVALID, "%s: null pointer", name);
+  SC_REQUIRE(rows >= 0 && nparts > 0 && nparts <= 1024 && D > 0 && D <= 512, SC_ERR_INVALID,
+             "%s: rows=%d nparts=%d D=%d (D <= 512)", name, rows, nparts, D);
+  if (rows == 0) return SC_OK;
+  const size_t stride = (size_t)D + 1;
+  sc::PeerWait wait;
+  wait.flags = flags;
+  wait.epoch_base = epoch_base;
+  wait.epoch_add = epoch_add;
+  wait.world = nparts;
+  wait.status = sc::device_status_word();
+  sc::launch_pdl(sc::combine_kernel<true>, dim3(rows), dim3(sc::kCombineThreads), 0,
+                 static_cast<cudaStream_t>(stream), gathered, (const float*)(gathered + D),
+                 stride, (size_t)rows * stride, stride, (size_t)rows * stride,
+                 (const int32_t*)nullptr, 1, nparts, 1, D, reinterpret_cast<uint16_t*>(out),
+                 lse_out, (float*)nullptr, wait);
   return sc::check_launch(name);
 }
 

@@ -25,6 +25,8 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k, const uint4* __res
                                  uint16_t* __restrict__ pool, const int64_t* __restrict__ slots,
                                  long long total, int Hkv, int D, int P, int64_t num_pages,
                                  unsigned int* status) {
+  pdl_wait();
+  pdl_trigger();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int chunks = D / 8;
@@ -112,9 +114,13 @@ extern "C" int sc_kv_append(const sc_bf16* k, const sc_bf16* v, sc_bf16* kv_pool
   const long long total = (long long)ntok * Hkv * 2 * (D / 8);
   const int threads = 256;
   const long long blocks = (total + threads - 1) / threads;
-  sc::kv_append_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(k), reinterpret_cast<const uint4*>(v), kv_pool, slot_mapping,
+  cudaError_t err = sc::launch_pdl(
+      sc::kv_append_kernel, dim3((unsigned)blocks), dim3(threads), 0,
+      static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(k),
+      reinterpret_cast<const uint4*>(v), reinterpret_cast<uint16_t*>(kv_pool), slot_mapping,
       total, Hkv, D, P, num_pages, sc::device_status_word());
+  if (err != cudaSuccess)
+    return sc::set_error(SC_ERR_CUDA, "%s: launch: %s", name, cudaGetErrorString(err));
   return sc::check_launch(name);
 }
 

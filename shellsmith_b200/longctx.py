@@ -114,6 +114,8 @@ class PeerExchange:
                                  dtype=torch.int64, device=dev) for par in (0, 1)]
         self.flag_ptrs = torch.tensor([b + self.flags_off + 4 * rank for b in self.peer_bases],
                                       dtype=torch.int64, device=dev)
+        # Arrival counter of the fused attention merge (the kernel leaves it zero).
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def gathered(self, parity: int) -> int:
         """Device address of this rank's received [world][rows][D + 1] blocks."""
@@ -126,6 +128,29 @@ class PeerExchange:
                    ptr(self.flag_ptrs), ptr(epoch), epoch_add, self.world, stream)
         _capi.call("sc_exchange_wait", self.base + self.flags_off, self.world, ptr(epoch),
                    epoch_add, stream)
+
+    def attention_put(self, q: torch.Tensor, pool: torch.Tensor, table: torch.Tensor,
+                      ctx: torch.Tensor, scale: float, *, max_pages: int,
+                      pages_per_split: int, num_splits: int, workspace, epoch: torch.Tensor,
+                      epoch_add: int, parity: int) -> None:
+        """Split-K attention of this rank's pages whose merge stores the packed rows
+        into every rank's slot for this rank and then raises the epoch flags (one
+        kernel pair; sc_paged_decode_attention_exchange)."""
+        B, hq, d = q.shape
+        num_pages, hkv, page, _ = paged._pool_dims(pool)
+        part_out, part_lse = workspace.views(B, num_splits)
+        _capi.call("sc_paged_decode_attention_exchange", ptr(q), ptr(pool), num_pages,
+                   ptr(table), ptr(ctx), B, hq, hkv, d, page, max_pages, pages_per_split,
+                   num_splits, float(scale), ptr(part_out), ptr(part_lse),
+                   ptr(self.dst[parity]), ptr(self.flag_ptrs), ptr(self.counter), ptr(epoch),
+                   epoch_add, self.world, stream_of(q))
+
+    def merge(self, out: torch.Tensor, epoch: torch.Tensor, epoch_add: int, parity: int) -> None:
+        """Wait (bounded) for every rank's epoch, then merge the received parts into
+        out [rows, D] bf16 (sc_attention_combine_exchange)."""
+        _capi.call("sc_attention_combine_exchange", self.gathered(parity),
+                   self.base + self.flags_off, ptr(epoch), epoch_add, self.world, self.rows,
+                   self.width - 1, ptr(out), None, stream_of(out))
 
     def close(self) -> None:
         cudart = _cudart()
@@ -177,6 +202,7 @@ class ShardedSequence:
         self.workspace = None
         self.pages_per_split = None
         self.peer = None      # PeerExchange, when enable_peer_exchange() was called
+        self.peer_fused = False
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self._h_epoch = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.tokens_done = 0
@@ -208,14 +234,18 @@ class ShardedSequence:
         self._staged = torch.cuda.Event()
         self._staged.record()
 
-    def enable_peer_exchange(self, group=None) -> None:
+    def enable_peer_exchange(self, group=None, fused: bool = False) -> None:
         """Exchange the packed partials by NVLink stores instead of NCCL (collective:
-        every rank calls it)."""
+        every rank calls it). By default a put and a wait kernel carry the packed block
+        (one fence per destination). fused: the split merge itself stores into the peers
+        and the final merge waits for them (two launches fewer per layer, but every
+        merge CTA fences at system scope; measured slower at 2 GPUs)."""
         if self.kv.shape[0] % 2:
             raise ValueError("peer exchange alternates receive buffers per attention layer: "
                              "it needs an even number of attention layers")
         self.peer = PeerExchange(self.q_heads, self.head_dim + 1, self.rank, self.world,
                                  group=group, device=self.kv.device)
+        self.peer_fused = fused
 
     def close(self) -> None:
         if self.peer is not None:
@@ -238,9 +268,25 @@ class ShardedSequence:
         if self.workspace is None:
             sms = paged.sm_count(q.device)
             self.pages_per_split = max(1, -(-self.capacity * self.groups() // sms))
-            _, nsplit = paged.split_plan(self.capacity, self.pages_per_split)
+            _, self.num_splits = paged.split_plan(self.capacity, self.pages_per_split)
             self.workspace = paged.AttentionWorkspace(1, self.q_heads, self.head_dim,
-                                                      max(1, nsplit), device=q.device)
+                                                      max(1, self.num_splits), device=q.device)
+        if self.world == 1 and all_gather is None:
+            # One rank holds every page: the split merge writes the final rows.
+            paged.paged_decode_attention(q, pool, self.table, self.ctx, scale,
+                                         max_pages_in_batch=self.capacity,
+                                         pages_per_split=self.pages_per_split,
+                                         total_pages=self.capacity, workspace=self.workspace,
+                                         out=self.out.view(1, self.q_heads, self.head_dim))
+            return self.out
+        if self.peer is not None and self.peer_fused and self.num_splits > 1:
+            parity = (layer + 1) & 1   # the parity of this call's epoch (even layer count)
+            self.peer.attention_put(q, pool, self.table, self.ctx, scale,
+                                    max_pages=self.capacity, pages_per_split=self.pages_per_split,
+                                    num_splits=self.num_splits, workspace=self.workspace,
+                                    epoch=self.epoch, epoch_add=layer + 1, parity=parity)
+            self.peer.merge(self.out, self.epoch, layer + 1, parity)
+            return self.out
         paged.paged_decode_attention_packed(q, pool, self.table, self.ctx, scale,
                                             packed=self.packed, max_pages_in_batch=self.capacity,
                                             pages_per_split=self.pages_per_split,

@@ -150,7 +150,7 @@ def _p2p_worker(rank, world, port, tokens, result):
     try:
         q, k, v = _sequence(tokens + 1)
         shards = {}
-        for mode in ("nccl", "p2p"):
+        for mode in ("nccl", "p2p", "fused"):
             s = ShardedSequence(tokens, rank, world, attention_layers=2, kv_heads=HKV,
                                 head_dim=D, q_heads=HQ, device=dev)
             lo = s.first_page * paged.PAGE_SIZE
@@ -159,10 +159,10 @@ def _p2p_worker(rank, world, port, tokens, result):
                 for layer in range(2):
                     paged.kv_append(k[lo:lo + s.local_tokens].to(dev),
                                     v[lo:lo + s.local_tokens].to(dev), s.kv[layer], slots)
-            if mode == "p2p":
-                s.enable_peer_exchange()
+            if mode != "nccl":
+                s.enable_peer_exchange(fused=mode == "fused")
             shards[mode] = s
-        outs = {"nccl": [], "p2p": []}
+        outs = {"nccl": [], "p2p": [], "fused": []}
         for step in range(2):
             t = tokens + step
             for mode, s in shards.items():
@@ -176,7 +176,9 @@ def _p2p_worker(rank, world, port, tokens, result):
 
         _capi.check_device()
         result[rank] = outs
+        dist.barrier()
         shards["p2p"].close()
+        shards["fused"].close()
     finally:
         dist.destroy_process_group()
 
@@ -202,8 +204,9 @@ def test_two_gpus_peer_exchange_matches_nccl():
         q, k, v = _sequence(tokens + 1)
         for r in range(2):
             outs = result[r]
-            for i, (a, b) in enumerate(zip(outs["nccl"], outs["p2p"])):
-                assert np.array_equal(a, b), (r, i)
+            for mode in ("p2p", "fused"):
+                for i, (a, b) in enumerate(zip(outs["nccl"], outs[mode])):
+                    assert np.array_equal(a, b), (r, mode, i)
             for step in range(2):
                 n = tokens + 1 + step
                 want, _ = oatt.decode_attention(q[0].float().numpy(), k[:n].float().numpy(),
@@ -213,8 +216,10 @@ def test_two_gpus_peer_exchange_matches_nccl():
                                                atol=ATOL)
 
 
-def test_peer_exchange_single_rank_matches_local_path(cuda):
-    """World 1: the put/flag/wait kernels run against this GPU's own buffer."""
+@pytest.mark.parametrize("fused", [False, True])
+def test_peer_exchange_single_rank_matches_local_path(cuda, fused):
+    """World 1: the put/flag/wait kernels (separate, or folded into the attention merge
+    and the final merge) run against this GPU's own buffer."""
     tokens = 3000
     q, k, v = _sequence(tokens + 1)
     shards = []
@@ -224,7 +229,7 @@ def test_peer_exchange_single_rank_matches_local_path(cuda):
         for layer in range(2):
             _fill(s, k, v, layer)
         if use_peer:
-            s.enable_peer_exchange()
+            s.enable_peer_exchange(fused=fused)
         shards.append(s)
 
     def gather(dst, src):
@@ -244,3 +249,34 @@ def test_peer_exchange_single_rank_matches_local_path(cuda):
 
     _capi.check_device()
     shards[1].close()
+
+
+def test_single_rank_direct_path_matches_packed_path(cuda):
+    """World 1 without an all-gather: the split merge writes the final rows, equal bit for
+    bit to the packed partial merged as one part."""
+    tokens = 3000
+    q, k, v = _sequence(tokens + 1)
+    shards = []
+    for _ in range(2):
+        s = ShardedSequence(tokens, 0, 1, attention_layers=2, kv_heads=HKV, head_dim=D,
+                            q_heads=HQ)
+        for layer in range(2):
+            _fill(s, k, v, layer)
+        shards.append(s)
+
+    def gather(dst, src):
+        dst[0].copy_(src)
+
+    for step in range(2):
+        t = tokens + step
+        for s in shards:
+            s.begin_token()
+        for layer in range(2):
+            a = shards[0].attention(layer, q.cuda(), k[t:t + 1].cuda(), v[t:t + 1].cuda(), 1 / 16,
+                                    all_gather=gather).clone()
+            b = shards[1].attention(layer, q.cuda(), k[t:t + 1].cuda(), v[t:t + 1].cuda(), 1 / 16)
+            torch.cuda.synchronize()
+            assert torch.equal(a, b)
+    from shellsmith_b200 import _capi
+
+    _capi.check_device()
