@@ -185,6 +185,50 @@ __device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D(16x8 f32) += A(16x8 tf32, row) * B(8x8 tf32, col). Fragments (g = lane / 4,
+// t = lane % 4): a0 (g, t), a1 (g + 8, t), a2 (g, t + 4), a3 (g + 8, t + 4);
+// b0 (k = t, n = g), b1 (k = t + 4, n = g); d0/d1 (g, 2t / 2t + 1), d2/d3 (g + 8, ...).
+__device__ __forceinline__ void mma_tf32_1688(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// x = big + small, both tf32 (round to nearest): big*big + big*small + small*big
+// carries a product to about fp32 accuracy on the tf32 tensor path.
+__device__ __forceinline__ void split_tf32(float x, uint32_t& big, uint32_t& small) {
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(big) : "f"(x));
+  const float rest = x - __uint_as_float(big);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(small) : "f"(rest));
+}
+
+// acc (a 16x8 fp32 tile in the mma_tf32_1688 D layout) += A[16][K] * B[K][8], both
+// fp32 in shared memory (row strides lda, ldb), as three tf32 products per k-step.
+template <int K>
+__device__ __forceinline__ void warp_gemm_tf32x3(float* acc, const float* A, int lda,
+                                                 const float* B, int ldb, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  // Three accumulators, so the dependent MMA chain is K / 8 long, not 3K / 8.
+  float c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    uint32_t ab[4], as[4], bb[2], bs[2];
+    split_tf32(A[g * lda + k0 + t], ab[0], as[0]);
+    split_tf32(A[(g + 8) * lda + k0 + t], ab[1], as[1]);
+    split_tf32(A[g * lda + k0 + t + 4], ab[2], as[2]);
+    split_tf32(A[(g + 8) * lda + k0 + t + 4], ab[3], as[3]);
+    split_tf32(B[(k0 + t) * ldb + g], bb[0], bs[0]);
+    split_tf32(B[(k0 + t + 4) * ldb + g], bb[1], bs[1]);
+    mma_tf32_1688(c1, as, bb);
+    mma_tf32_1688(c2, ab, bs);
+    mma_tf32_1688(acc, ab, bb);
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) acc[e] += c1[e] + c2[e];
+}
+
 // Transposes one 8x8 b16 matrix held in the ldmatrix fragment layout.
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;

@@ -21,7 +21,9 @@
 //   G34 W^T [X;Y]^T (+= 0 | decay P2^T) -> U^T | O^T    M128 N128 K64
 //   GS  (U^T r) K  (+= decay_63 S)                      M128 N128 K64
 // Q/K/V chunk tiles arrive by TMA (128-byte swizzle, no multicast); the
-// unit-lower inverse runs column-per-thread in fp32. Operands that feed the
+// unit-lower inverse solves its 8 x 8 diagonal blocks column-per-thread in fp32
+// and builds the off-diagonal blocks from them (warp mma.sync tf32 tiles, each
+// product as three tf32 products, fp32-accurate). Operands that feed the
 // fp32 state (S, W, X, Y, U) are split into bf16 hi + lo and multiplied as
 // hi*hi + hi*lo + lo*hi, which keeps the state within ~1e-5 of fp32 math.
 #include <cudaTypedefs.h>
@@ -53,10 +55,12 @@ constexpr uint32_t OFF_SMALL = 212992;  // lg, beta, decay, r [64] floats; barri
 constexpr uint32_t OFF_MH = OFF_SH;            // m hi [128 rows (0-63 used)][128 B]
 constexpr uint32_t OFF_ML = OFF_SH + 16384;    // m lo
 constexpr uint32_t OFF_AMAT = OFF_SH + 32768;  // A (strict lower) fp32 [64][68], then X
-constexpr uint32_t OFF_TBUF = OFF_SH + 50176;  // inverse scratch fp32 [32][32]
+constexpr uint32_t OFF_TBUF = OFF_SH + 50176;  // inverse scratch fp32 [32][kTStride]
 constexpr uint32_t OFF_XTH = OFF_WH;           // X^T rows hi [64 rows][128 B]
 constexpr uint32_t OFF_XTL = OFF_WL;           // lo
 constexpr int kAStride = 68;                   // fp32 row stride of A (conflict-free float4 rows)
+constexpr int kTStride = 40;                   // fp32 row stride of the inverse scratch
+static_assert(OFF_TBUF + 32 * kTStride * 4 <= OFF_XYH, "inverse scratch overlaps [X;Y]");
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + 5 * 64 * 4 + 64 + 1024;  // + 1024 alignment slack
 
 // TMEM columns (512 allocated).
@@ -291,13 +295,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // R_tj = 2^(lg_t - lg_j). When the chunk's decay spans < 2^-100, write it
       // as 2^(lg_t - lg_0) * 2^(lg_0 - lg_j): both factors stay in range and the
       // per-element exponentials become one multiply.
-      const bool factor = s_lg[0] - s_lg[63] < 100.f;
-      const float at = exp2f(lgt - s_lg[0]);
       float rr[32];
+      if (s_lg[0] - s_lg[63] < 100.f) {  // uniform over the CTA
+        const float at = exp2f(lgt - s_lg[0]);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float lgj = s_lg[32 * hf + e];
-        rr[e] = factor ? at * s_inv[32 * hf + e] : exp2f(lgt - lgj);
+        for (int e = 0; e < 32; ++e) rr[e] = at * s_inv[32 * hf + e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) rr[e] = exp2f(lgt - s_lg[32 * hf + e]);
       }
       if (quarter < 2) {
         const float bt = s_beta[t];
@@ -323,90 +328,98 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
 
-    // ---- (4) X = (I + A)^-1 in place, by 16 x 16 blocks.
-    // L0: warp w < 4 inverts diagonal block w; lane c < 16 owns column c.
-    if (warp < 4) {
-      const int c16 = lane_id & 15;
-      const float* Ab = Xf + (16 * warp) * kAStride + 16 * warp;
+    // ---- (4) X = (I + A)^-1 in place: 8 x 8 diagonal blocks by substitution,
+    //          then the off-diagonal blocks level by level (8, 16, 32 wide).
+    // L0: warp w inverts diagonal block w (rows and columns 8w + [0, 8)); lane
+    //     c < 8 owns column c.
+    {
+      const int c8 = lane_id & 7;
+      const float* Ab = Xf + (8 * warp) * kAStride + 8 * warp;
       // Right-looking substitution: once x[k] is final it updates every later
       // row, so the loads of column k do not wait on the x chain.
-      float x[16];
+      float x[8];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) x[r] = (r == c16) ? 1.f : 0.f;
+      for (int r = 0; r < 8; ++r) x[r] = (r == c8) ? 1.f : 0.f;
 #pragma unroll
-      for (int k = 0; k < 15; ++k) {
-        float col[16];
+      for (int k = 0; k < 7; ++k) {
+        float col[8];
 #pragma unroll
-        for (int r = k + 1; r < 16; ++r) col[r] = Ab[r * kAStride + k];
+        for (int r = k + 1; r < 8; ++r) col[r] = Ab[r * kAStride + k];
 #pragma unroll
-        for (int r = k + 1; r < 16; ++r) x[r] = fmaf(-col[r], x[k], x[r]);
+        for (int r = k + 1; r < 8; ++r) x[r] = fmaf(-col[r], x[k], x[r]);
       }
       __syncwarp();
-      if (lane_id < 16) {
-        float* Xb = Xf + (16 * warp) * kAStride + 16 * warp + c16;
+      if (lane_id < 8) {
+        float* Xb = Xf + (8 * warp) * kAStride + 8 * warp + c8;
 #pragma unroll
-        for (int r = 0; r < 16; ++r) Xb[r * kAStride] = x[r];
+        for (int r = 0; r < 8; ++r) Xb[r * kAStride] = x[r];
       }
     }
     __syncthreads();
-    // L1: X[2p+1][2p] = -D_{2p+1}^-1 (A[2p+1][2p] D_{2p}^-1), p = 0, 1.
+    // L0b: in each 16 x 16 diagonal block b, X[lower 8][upper 8] =
+    //      -D_hi (A[lower 8][upper 8] D_lo); one output per thread.
     {
-      const int p = tid >> 7, r = (tid >> 3) & 15, c0 = (tid & 7) * 2;
-      const float* Arow = Xf + (16 * (2 * p + 1) + r) * kAStride + 16 * (2 * p);
-      const float* Xd = Xf + (16 * (2 * p)) * kAStride + 16 * (2 * p) + c0;
-      float t0 = 0.f, t1 = 0.f;
+      const int b = tid >> 6, r = (tid >> 3) & 7, cc = tid & 7;
+      const int lo = 16 * b, hi = 16 * b + 8;
+      const float* Arow = Xf + (hi + r) * kAStride + lo;
+      float tsum = 0.f;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float a = Arow[k];
-        t0 = fmaf(a, Xd[k * kAStride], t0);
-        t1 = fmaf(a, Xd[k * kAStride + 1], t1);
-      }
-      Tbuf[p * 256 + r * 16 + c0] = t0;
-      Tbuf[p * 256 + r * 16 + c0 + 1] = t1;
+      for (int k = 0; k < 8; ++k) tsum = fmaf(Arow[k], Xf[(lo + k) * kAStride + lo + cc], tsum);
+      Tbuf[b * 64 + r * 8 + cc] = tsum;
       __syncthreads();
-      const float* Drow = Xf + (16 * (2 * p + 1) + r) * kAStride + 16 * (2 * p + 1);
-      float x0 = 0.f, x1 = 0.f;
+      const float* Drow = Xf + (hi + r) * kAStride + hi;
+      float xs = 0.f;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float d = Drow[k];
-        x0 = fmaf(d, Tbuf[p * 256 + k * 16 + c0], x0);
-        x1 = fmaf(d, Tbuf[p * 256 + k * 16 + c0 + 1], x1);
-      }
-      float* Xo = Xf + (16 * (2 * p + 1) + r) * kAStride + 16 * (2 * p) + c0;
-      Xo[0] = -x0;
-      Xo[1] = -x1;
+      for (int k = 0; k < 8; ++k) xs = fmaf(Drow[k], Tbuf[b * 64 + k * 8 + cc], xs);
+      Xf[(hi + r) * kAStride + lo + cc] = -xs;
     }
     __syncthreads();
-    // L2: X[32:64][0:32] = -X[32:64][32:64] (A[32:64][0:32] X[0:32][0:32]).
+    // The off-diagonal blocks are products of the blocks already inverted, run
+    // as warp tensor-core tiles (three tf32 products each, fp32-accurate): a
+    // 16 x 8 output tile per warp, the intermediate in Tbuf (row stride kTStride).
+    // L1: X[2p+1][2p] = -D_{2p+1} (A[2p+1][2p] D_{2p}), p = 0, 1; warp w < 4 owns
+    //     p = w / 2 and columns 8 (w % 2) + [0, 8).
     {
-      const int r = tid >> 3, c0 = (tid & 7) * 4;
-      const float* Arow = Xf + (32 + r) * kAStride;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float a = Arow[k];
-        const float4 xk = *reinterpret_cast<const float4*>(Xf + k * kAStride + c0);
-        acc.x = fmaf(a, xk.x, acc.x);
-        acc.y = fmaf(a, xk.y, acc.y);
-        acc.z = fmaf(a, xk.z, acc.z);
-        acc.w = fmaf(a, xk.w, acc.w);
+      const int g = lane_id >> 2, t4 = lane_id & 3;
+      const int p = warp >> 1, n0 = 8 * (warp & 1);
+      const int r1 = 16 * (2 * p + 1), c1 = 16 * (2 * p);
+      float* T = Tbuf + p * 16 * kTStride + n0;
+      if (warp < 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        warp_gemm_tf32x3<16>(acc, Xf + r1 * kAStride + c1, kAStride,
+                             Xf + c1 * kAStride + c1 + n0, kAStride, lane_id);
+        *reinterpret_cast<float2*>(T + g * kTStride + 2 * t4) = make_float2(acc[0], acc[1]);
+        *reinterpret_cast<float2*>(T + (g + 8) * kTStride + 2 * t4) = make_float2(acc[2], acc[3]);
       }
-      *reinterpret_cast<float4*>(Tbuf + r * 32 + c0) = acc;
       __syncthreads();
-      const float* Drow = Xf + (32 + r) * kAStride + 32;
-      float4 xo = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float d = Drow[k];
-        const float4 tk = *reinterpret_cast<const float4*>(Tbuf + k * 32 + c0);
-        xo.x = fmaf(d, tk.x, xo.x);
-        xo.y = fmaf(d, tk.y, xo.y);
-        xo.z = fmaf(d, tk.z, xo.z);
-        xo.w = fmaf(d, tk.w, xo.w);
+      if (warp < 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        warp_gemm_tf32x3<16>(acc, Xf + r1 * kAStride + r1, kAStride, T, kTStride, lane_id);
+        float* Xo = Xf + r1 * kAStride + c1 + n0;
+        *reinterpret_cast<float2*>(Xo + g * kAStride + 2 * t4) = make_float2(-acc[0], -acc[1]);
+        *reinterpret_cast<float2*>(Xo + (g + 8) * kAStride + 2 * t4) =
+            make_float2(-acc[2], -acc[3]);
       }
-      __syncthreads();  // every thread has read A[32:64][0:32] and X before it is overwritten
-      *reinterpret_cast<float4*>(Xf + (32 + r) * kAStride + c0) =
-          make_float4(-xo.x, -xo.y, -xo.z, -xo.w);
+    }
+    __syncthreads();
+    // L2: X[32:64][0:32] = -X[32:64][32:64] (A[32:64][0:32] X[0:32][0:32]); warp w
+    //     owns rows 32 + 16 (w / 4) + [0, 16), columns 8 (w % 4) + [0, 8).
+    {
+      const int g = lane_id >> 2, t4 = lane_id & 3;
+      const int r0 = 32 + 16 * (warp >> 2), n0 = 8 * (warp & 3);
+      float* T = Tbuf + (r0 - 32) * kTStride + n0;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      warp_gemm_tf32x3<32>(acc, Xf + r0 * kAStride, kAStride, Xf + n0, kAStride, lane_id);
+      *reinterpret_cast<float2*>(T + g * kTStride + 2 * t4) = make_float2(acc[0], acc[1]);
+      *reinterpret_cast<float2*>(T + (g + 8) * kTStride + 2 * t4) = make_float2(acc[2], acc[3]);
+      __syncthreads();  // T complete; every warp is done reading A[32:64][0:32]
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      warp_gemm_tf32x3<32>(acc, Xf + r0 * kAStride + 32, kAStride, Tbuf + n0, kTStride,
+                           lane_id);
+      float* Xo = Xf + r0 * kAStride + n0;
+      *reinterpret_cast<float2*>(Xo + g * kAStride + 2 * t4) = make_float2(-acc[0], -acc[1]);
+      *reinterpret_cast<float2*>(Xo + (g + 8) * kAStride + 2 * t4) =
+          make_float2(-acc[2], -acc[3]);
     }
     __syncthreads();
     // X -> bf16 hi/lo: X^T rows (B of the Y GEMM) and X rows (rows 0-63 of [X;Y]).
