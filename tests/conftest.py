@@ -13,6 +13,15 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
+@pytest.fixture(autouse=True)
+def _seeded_torch():
+    """Every test draws its torch tensors (host and device) from the same seed, so a
+    run reproduces the last one whatever the order or selection of tests."""
+    import torch
+
+    torch.manual_seed(0)
+
+
 @pytest.fixture(scope="session")
 def cuda():
     import torch

@@ -16,7 +16,10 @@ from shellsmith_b200 import paged
 
 pytestmark = pytest.mark.gpu
 
-RTOL, ATOL = 2e-2, 2e-3
+# The kernel feeds the probabilities to the P.V product in bf16 (relative rounding
+# 2^-9), so an output's error has a standard deviation near 2^-9 / sqrt(3) * ||p||_2:
+# up to ~5e-4 for the short contexts below (||p||_2 ~ 0.5). ATOL is ~6 of those.
+RTOL, ATOL = 2e-2, 3e-3
 
 
 def _bits(t: torch.Tensor) -> np.ndarray:
