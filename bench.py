@@ -405,9 +405,11 @@ def run_ours(args, world, rank, local):
     peaks = measured_peaks()
     hbm = peaks["hbm_gbs"]
 
-    prefill_c1 = front = kv8 = None
+    prefill_c1 = front = kv8 = decode_c0 = attention_c2 = None
     if not args.no_config1 and rank == 0:
         prefill_c1 = config1_prefill(device)
+        decode_c0 = config0_decode(device)
+        attention_c2 = config2_attention(device)
         front = gdn_front_layer(device)
         kv8 = kv8_attention_layer(wl, device)
 
@@ -470,6 +472,8 @@ def run_ours(args, world, rank, local):
         line["e2e"] = e2e
     if prefill_c1 is not None:
         line["config1_prefill"] = prefill_c1
+        line["config0_decode"] = decode_c0
+        line["config2_attention"] = attention_c2
     if front is not None:
         line["gdn_front"] = front
     if kv8 is not None:
@@ -695,6 +699,139 @@ def kv8_layer_standalone(args, device, rounds: int = 10) -> dict:
             "kv8_gbs": round(nbytes["8bit"] / ms["8bit"] / 1e6, 1),
             "kv8_frac": round(nbytes["8bit"] / ms["8bit"] / 1e6 / peaks["hbm_gbs"], 4),
             "kv8_bytes_per_launch": round(nbytes["8bit"]), "launches": rounds + 3}
+
+
+def config0_decode(device, steps: int = 256, rounds: int = 5) -> dict:
+    """Config 0: GDN one-token decode, B=4 sequences, 8 heads, 128 x 128 fp32 state, 256
+    steps from a zero state (each step reads the state the previous one wrote). The 2 MiB
+    state stays in L2, so the step is bound by launch and dependency latency; tokens/s =
+    B x steps / time. Inputs of all steps are made before the timed region. Timed twice:
+    256 calls from Python (each call's host work included) and the same 256 launches
+    replayed as one CUDA graph (the device-side chain)."""
+    import torch
+
+    from shellsmith_b200 import numerics
+    from shellsmith_b200.workloads import gdn_token_inputs_device
+
+    B, H, d = 4, 8, 128
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    inputs = [gdn_token_inputs_device(gen, B, H, H, d, d, device=device) for _ in range(steps)]
+    state = torch.zeros((B, H, d, d), dtype=torch.float32, device=device)
+    out = torch.empty((B, H, d), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def run():
+        for q, k, v, g, beta in inputs:
+            numerics.gdn_decode(q, k, v, g, beta, state, out=out)
+
+    def timed(fn):
+        times = []
+        for _ in range(rounds):
+            state.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            times.append((e0, e1))
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in times)
+
+    run()
+    ms_calls = timed(run)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    torch.cuda.synchronize()
+    ms = timed(graph.replay)
+    del graph
+    return {"workload": "config0 GDN decode B=4 H=8 128x128 fp32 state, 256 dependent steps",
+            "ms_per_256_steps": round(ms, 3), "us_per_step": round(ms * 1e3 / steps, 2),
+            "tokens_per_s": round(B * steps / (ms / 1e3), 1),
+            "python_calls": {"us_per_step": round(ms_calls * 1e3 / steps, 2),
+                             "tokens_per_s": round(B * steps / (ms_calls / 1e3), 1)},
+            "note": "graph replay of the 256 launches; state (2 MiB) L2-resident: "
+                    "latency-bound, HBM fraction not meaningful",
+            "launches": steps}
+
+
+def config2_attention(device, steps: int = 20, warmup: int = 3) -> dict:
+    """Config 2: paged KV append + split-K decode attention, bf16. 64 sequences with
+    contexts U[1k, 32k], 16 query / 2 KV heads, D 256, pages of 16 tokens handed out from a
+    random permutation of a 150k-page pool. Each step appends one token per sequence and
+    attends over the grown context. Slots, lengths and the launch order (longest first) of
+    every step are made before the timed region; 2.2 GB per step, well above L2."""
+    import torch
+
+    from shellsmith_b200 import paged
+
+    B, hq, hkv, D, P, NP = 64, 16, 2, 256, 16, 150_000
+    total = warmup + steps
+    rng = np.random.default_rng(2)
+    lengths = rng.integers(1024, 32 * 1024 + 1, size=B)
+    need = -(-(lengths + total) // P)
+    perm = rng.permutation(NP).astype(np.int32)
+    table = np.zeros((B, int(need.max())), np.int32)
+    cursor = 0
+    for b in range(B):
+        table[b, :need[b]] = perm[cursor:cursor + need[b]]
+        cursor += need[b]
+    pos = lengths[None, :] + np.arange(total)[:, None]            # [step, B] new token index
+    slots = table[np.arange(B)[None, :], pos // P].astype(np.int64) * P + pos % P
+    ctx = (pos + 1).astype(np.int32)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2)
+    pool = torch.empty((NP, hkv, 2, P, D), dtype=torch.bfloat16, device=device)
+    flat, block = pool.view(-1), 1 << 26
+    for start in range(0, flat.numel(), block):
+        part = flat[start:start + block]
+        part.copy_(torch.randn(part.shape, generator=gen, device=device))
+    table_d = torch.from_numpy(table).to(device)
+    slots_d = torch.from_numpy(slots).to(device)
+    ctx_d = torch.from_numpy(ctx).to(device)
+    order = torch.from_numpy(np.argsort(-lengths, kind="stable").astype(np.int32)).to(device)
+    q = torch.randn((B, hq, D), generator=gen, device=device).to(torch.bfloat16)
+    kn = torch.randn((B, hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    vn = torch.randn((B, hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((B, hq, D), dtype=torch.bfloat16, device=device)
+    max_pages = int(-(-ctx.max() // P))
+    total_pages = int((-(-ctx[-1] // P)).sum())
+    groups = hkv * ((hq // hkv + 7) // 8)
+    pps, nsplit = paged.split_plan(max_pages, None, total_pages * groups, paged.sm_count(device))
+    ws = paged.AttentionWorkspace(B, hq, D, nsplit, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(s):
+        paged.kv_append(kn, vn, pool, slots_d[s])
+        paged.paged_decode_attention(q, pool, table_d, ctx_d[s], 1 / 16,
+                                     max_pages_in_batch=max_pages, pages_per_split=pps,
+                                     workspace=ws, out=out, seq_order=order)
+
+    for s in range(warmup):
+        step(s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for s in range(warmup, total):
+        step(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    from shellsmith_b200 import _capi
+
+    _capi.check_device()
+    ms = e0.elapsed_time(e1) / steps
+    c = ctx[warmup:].astype(np.float64)
+    nbytes = (c.sum() * hkv * D * 2 * 2 + steps * B * hkv * D * 2 * 2
+              + steps * B * hq * D * 2 * 2 + np.ceil(c / P).sum() * 4) / steps
+    gbs = nbytes / (ms / 1e3) / 1e9
+    peak = measured_peaks()["hbm_gbs"]
+    del pool
+    return {"workload": "config2 paged append + split-K decode attention, 64 seqs ctx U[1k,32k], "
+                        "16/2 heads D256, 150k-page pool (random permutation)",
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(B / (ms / 1e3), 1),
+            "bytes_per_step": int(nbytes), "gbs": round(gbs, 1),
+            "hbm_frac": round(gbs / peak, 4), "pages_per_split": pps, "num_splits": nsplit,
+            "launches_per_step": 3}
 
 
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:

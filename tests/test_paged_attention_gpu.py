@@ -197,3 +197,48 @@ def test_launch_order_changes_nothing_but_the_schedule(cuda):
     paged.paged_decode_attention(q, pool, bt, ctx, 0.0625, pages_per_split=8, seq_order=bad)
     with pytest.raises(_capi.DeviceFault):
         _capi.check_device()
+
+
+def test_config2_scale_sample_matches_oracle(cuda):
+    """Config 2's shapes at full size: 64 sequences with contexts U[1k, 32k] whose pages
+    come from a random permutation of a 150k-page pool (4.9 GB). One append + attention
+    step with the default split plan and longest-first launch order: every appended token
+    reads back bit for bit, and three sequences (shortest, longest, one more) match the
+    oracle."""
+    rng = np.random.default_rng(20)
+    B, hq, hkv, D, P, NP = 64, 16, 2, 256, paged.PAGE_SIZE, 150_000
+    lengths = rng.integers(1024, 32 * 1024 + 1, size=B)
+    need = -(-(lengths + 1) // P)
+    perm = rng.permutation(NP).astype(np.int32)
+    table = np.zeros((B, int(need.max())), np.int32)
+    cursor = 0
+    for b in range(B):
+        table[b, :need[b]] = perm[cursor:cursor + need[b]]
+        cursor += need[b]
+    pool = torch.empty((NP, hkv, 2, P, D), dtype=torch.bfloat16, device=cuda)
+    flat = pool.view(-1)
+    for start in range(0, flat.numel(), 1 << 26):
+        part = flat[start:start + (1 << 26)]
+        part.copy_(torch.randn(part.shape, device=cuda))
+    slots = torch.from_numpy(table[np.arange(B), lengths // P].astype(np.int64) * P
+                             + lengths % P).to(cuda)
+    ctx = lengths + 1
+    q = torch.randn((B, hq, D), device=cuda).to(torch.bfloat16)
+    kn = torch.randn((B, hkv, D), device=cuda).to(torch.bfloat16)
+    vn = torch.randn((B, hkv, D), device=cuda).to(torch.bfloat16)
+    order = torch.from_numpy(np.argsort(-ctx, kind="stable").astype(np.int32)).to(cuda)
+    scale = 1.0 / math.sqrt(D)
+    paged.kv_append(kn, vn, pool, slots)
+    out = paged.paged_decode_attention(q, pool, torch.from_numpy(table).to(cuda),
+                                       torch.from_numpy(ctx.astype(np.int32)).to(cuda), scale,
+                                       total_pages=int(need.sum()), seq_order=order)
+    kg, vg = paged.kv_gather(pool, slots)
+    assert torch.equal(kg, kn) and torch.equal(vg, vn)
+    for b in (int(np.argmin(lengths)), int(np.argmax(lengths)), 7):
+        pages = torch.from_numpy(table[b, :need[b]].astype(np.int64)).to(cuda)
+        sub = pool[pages].float().cpu().numpy()
+        k, v = oatt.pool_read_pages(sub, np.arange(need[b]), int(ctx[b]), hkv, P, D)
+        want, _ = oatt.decode_attention(q[b].float().cpu().numpy(), k, v, scale)
+        np.testing.assert_allclose(out[b].float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    del pool
+    torch.cuda.empty_cache()
