@@ -1038,7 +1038,8 @@ def run_config4(args, world, rank, local):
                 shard.attention(a_i, q, k, v, 1 / 16)
                 a_i += 1
             else:
-                numerics.gdn_decode(*gdn_in[g_i], state[g_i], out=gdn_out)
+                # Each layer has its own state: the update may stream it in early.
+                numerics.gdn_decode(*gdn_in[g_i], state[g_i], out=gdn_out, chained=True)
                 g_i += 1
 
     for _ in range(args.warmup):

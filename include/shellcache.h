@@ -94,6 +94,17 @@ int sc_gdn_decode_bf16(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
                        const int32_t* state_slot, sc_bf16* out, int B, int Hk,
                        int Hv, int dk, int dv, int num_slots, void* stream);
 
+/* sc_gdn_decode for a chain of layers (no reference counterpart: the same
+ * math). The caller promises that the kernel queued just before it on the
+ * stream writes neither the state rows this call reads nor state_slot (e.g.
+ * it is another layer's update, or an attention layer): the state then
+ * streams in while that kernel still runs. Consecutive calls on the SAME
+ * state rows must use sc_gdn_decode. */
+int sc_gdn_decode_chained(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
+                          const float* g, const float* beta, float* state,
+                          const int32_t* state_slot, sc_bf16* out, int B, int Hk,
+                          int Hv, int dk, int dv, int num_slots, void* stream);
+
 /* GDN chunked prefill (chunk 64) on tcgen05 tensor cores, state IN PLACE.
  *
  * Replaces studio_compute/numerics/ops.py:151-215 `gated_delta_chunked`

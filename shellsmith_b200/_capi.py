@@ -23,6 +23,7 @@ SIGNATURES = {
     "sc_last_error": [ctypes.c_char_p, _I],
     "sc_device_status": [ctypes.POINTER(ctypes.c_uint), _P],
     "sc_gdn_decode": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "sc_gdn_decode_chained": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "sc_gdn_decode_bf16": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "sc_gdn_chunk_prefill": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
                              _I, _P],

@@ -285,7 +285,7 @@ template <typename ST>
 int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       const float* g, const float* beta, ST* state, const int32_t* slot,
                       uint16_t* out, int B, int Hk, int Hv, int dk, int dv, int num_slots,
-                      void* stream) {
+                      void* stream, BulkLaunch mode = BulkLaunch::kDependent) {
   SC_REQUIRE(q && k && v && g && beta && state && out, SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE(B >= 0 && Hk > 0 && Hv > 0 && dv > 0, SC_ERR_INVALID,
              "%s: bad sizes B=%d Hk=%d Hv=%d dv=%d", name, B, Hk, Hv, dv);
@@ -298,7 +298,7 @@ int launch_gdn_decode(const char* name, const uint16_t* q, const uint16_t* k, co
   if constexpr (std::is_same<ST, float>::value) {
     if (gdn_bulk_supported(dk, dv))
       return gdn_bulk_launch(name, q, k, v, g, beta, state, slot, out, B, Hk, Hv, dv, num_slots,
-                             s, BulkLaunch::kDependent);
+                             s, mode);
   }
   dim3 block(kWarps * 32);
 #define SC_GDN_CASE(DK_)                                                                     \
@@ -380,6 +380,15 @@ extern "C" int sc_gdn_decode(const sc_bf16* q, const sc_bf16* k, const sc_bf16* 
                              void* stream) {
   return sc::launch_gdn_decode<float>("sc_gdn_decode", q, k, v, g, beta, state, state_slot, out, B,
                                       Hk, Hv, dk, dv, num_slots, stream);
+}
+
+extern "C" int sc_gdn_decode_chained(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
+                                     const float* g, const float* beta, float* state,
+                                     const int32_t* state_slot, sc_bf16* out, int B, int Hk,
+                                     int Hv, int dk, int dv, int num_slots, void* stream) {
+  return sc::launch_gdn_decode<float>("sc_gdn_decode_chained", q, k, v, g, beta, state,
+                                      state_slot, out, B, Hk, Hv, dk, dv, num_slots, stream,
+                                      sc::BulkLaunch::kStateAhead);
 }
 
 extern "C" int sc_gdn_decode_bf16(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,

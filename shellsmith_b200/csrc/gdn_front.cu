@@ -621,7 +621,7 @@ extern "C" int sc_gdn_decode_glue(const sc_bf16* qkv, const sc_bf16* z, const sc
       B, Hk, Hv, num_slots, device_status_word());
   if (int rc = check_launch(name)) return rc;
   if (int rc = gdn_bulk_launch(name, q, k, v, g, beta, state, state_slot, y, B, Hk, Hv, 128,
-                               num_slots, s, BulkLaunch::kAfterFront))
+                               num_slots, s, BulkLaunch::kStateAhead))
     return rc;
   const long long rows = (long long)B * Hv;
   gated_rmsnorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(y, z, norm_w, eps, out, rows,

@@ -24,12 +24,14 @@ from ._torch import ptr, require_cuda, stream_of
 
 def gdn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                beta: torch.Tensor, state: torch.Tensor, state_slot: torch.Tensor | None = None,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, chained: bool = False) -> torch.Tensor:
     """One-token GDN update of rows b (state row state_slot[b]), in place.
 
     q, k [B, Hk, dk] bf16; v [B, Hv, dv] bf16; g (decay), beta [B, Hv] fp32;
     state [slots, Hv, dv, dk] fp32 or bf16; state_slot [B] int32 or None
-    (identity). Returns out [B, Hv, dv] bf16.
+    (identity). Returns out [B, Hv, dv] bf16. chained (fp32 state): the work
+    queued just before this call does not write these state rows (another
+    layer's update, an attention layer), so the state may stream in early.
     """
     B, Hk, dk = q.shape
     Hv, dv = v.shape[1], v.shape[2]
@@ -52,7 +54,7 @@ def gdn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tenso
     require_cuda("out", out, torch.bfloat16, 3, align=2)
     if state.dtype == torch.float32:
         require_cuda("state", state, torch.float32, 4)
-        name = "sc_gdn_decode"
+        name = "sc_gdn_decode_chained" if chained else "sc_gdn_decode"
     elif state.dtype == torch.bfloat16:
         require_cuda("state", state, torch.bfloat16, 4, align=8)
         name = "sc_gdn_decode_bf16"

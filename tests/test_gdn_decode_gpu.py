@@ -135,3 +135,34 @@ def test_out_of_range_state_slot_is_flagged_not_read(cuda):
     with pytest.raises(_capi.DeviceFault):
         _capi.check_device()
     assert torch.count_nonzero(state[1]) == 0
+
+
+def test_chained_layers_equal_plain_updates(cuda):
+    """sc_gdn_decode_chained over a stack of layers (each its own state, as a model's
+    GDN layers) equals the plain entry bit for bit, queued back to back with no host
+    sync, for the one-chunk-per-CTA (B = 1) and bulk (B = 16) launch shapes."""
+    from shellsmith_b200.workloads import gdn_token_inputs_device
+
+    for B in (1, 16):
+        gen = torch.Generator(device=cuda)
+        gen.manual_seed(B)
+        layers, Hk, Hv, d = 6, 16, 32, 128
+        inputs = [gdn_token_inputs_device(gen, B, Hk, Hv, d, d, device=cuda)
+                  for _ in range(layers)]
+        start = torch.randn((layers, B, Hv, d, d), generator=gen, device=cuda) * 0.1
+        results = []
+        for chained in (False, True):
+            state = start.clone()
+            outs = []
+            for step in range(3):
+                for layer in range(layers):
+                    outs.append(numerics.gdn_decode(*inputs[layer], state[layer],
+                                                    chained=chained))
+            torch.cuda.synchronize()
+            results.append((state, outs))
+        (s0, o0), (s1, o1) = results
+        assert torch.equal(s0, s1)
+        assert all(torch.equal(a, b) for a, b in zip(o0, o1))
+    from shellsmith_b200 import _capi
+
+    _capi.check_device()
