@@ -60,6 +60,7 @@ constexpr uint32_t OFF_XTH = OFF_WH;           // X^T rows hi [64 rows][128 B]
 constexpr uint32_t OFF_XTL = OFF_WL;           // lo
 constexpr int kAStride = 68;                   // fp32 row stride of A (conflict-free float4 rows)
 constexpr int kTStride = 40;                   // fp32 row stride of the inverse scratch
+constexpr int kMaxRankedSeqs = 4096;           // longer varlen batches keep their order
 static_assert(OFF_TBUF + 32 * kTStride * 4 <= OFF_XYH, "inverse scratch overlaps [X;Y]");
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + 5 * 64 * 4 + 64 + 1024;  // + 1024 alignment slack
 
@@ -123,9 +124,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* Tbuf = reinterpret_cast<float*>(sm + OFF_TBUF);
 
   const int bh = blockIdx.x;
-  const int b = bh / Hv;
+  int b = bh / Hv;
   const int h = bh - b * Hv;
   const int kh = h / (Hv / Hk);
+  // Varlen batches run longest sequence first: when the grid is more than one
+  // wave, the CTAs left for the second wave belong to the shortest sequences.
+  // Block row b takes the sequence of rank b (length descending, index
+  // ascending), ranked here from cu_seqlens staged in the state-operand region,
+  // which the chunk loop first writes long after.
+  if (cu_seqlens != nullptr && (int)(gridDim.x / Hv) <= kMaxRankedSeqs) {
+    const int nseq = (int)(gridDim.x / Hv);
+    int* s_cu = reinterpret_cast<int*>(sm + OFF_SH);
+    for (int i = threadIdx.x; i <= nseq; i += blockDim.x) s_cu[i] = cu_seqlens[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nseq; i += blockDim.x) {
+      const int li = s_cu[i + 1] - s_cu[i];
+      int rank = 0;
+      for (int j = 0; j < nseq; ++j) {
+        const int lj = s_cu[j + 1] - s_cu[j];
+        rank += (lj > li || (lj == li && j < i)) ? 1 : 0;
+      }
+      if (rank == b) s_cu[nseq + 1] = i;
+    }
+    __syncthreads();
+    b = s_cu[nseq + 1];
+  }
   const int start = cu_seqlens != nullptr ? cu_seqlens[b] : b * T_fixed;
   const int len = cu_seqlens != nullptr ? cu_seqlens[b + 1] - start : T_fixed;
   const int slot = state_slot != nullptr ? state_slot[b] : b;
