@@ -198,10 +198,24 @@ def sum_over_ranks(value: float, world: int) -> float:
 
 
 # ------------------------------------------------------------------ workload
+def balanced_share(args, rank: int, world: int) -> np.ndarray:
+    """This rank's running sequences when the batch is sharded over `world` GPUs: every
+    rank draws the same global set of batch x world contexts and the sequences are dealt
+    longest first in snake order (0..N-1, N-1..0, ...), so each GPU holds `batch`
+    sequences with nearly equal resident K/V bytes."""
+    glob = np.random.default_rng(SEED).integers(args.min_len, args.max_len + 1,
+                                                size=args.batch * world)
+    order = np.argsort(-glob, kind="stable")
+    pos = np.arange(order.size)
+    turn, seat = pos // world, pos % world
+    owner = np.where(turn % 2 == 0, seat, world - 1 - seat)
+    return glob[order[owner == rank]]
+
+
 class Workload:
     """Engine, caches, per-layer inputs and the churn process of one rank."""
 
-    def __init__(self, args, rank: int, device):
+    def __init__(self, args, rank: int, device, world: int = 1):
         import torch
 
         from shellsmith_b200.engine import HybridCacheEngine, HybridConfig
@@ -234,6 +248,8 @@ class Workload:
         # Running sequences: admitted with their current context (already
         # prefilled); each decode step appends one token.
         lengths = self.rng.integers(args.min_len, args.max_len + 1, size=args.batch)
+        if world > 1:
+            lengths = balanced_share(args, rank, world)
         self.next_id = 0
         for length in lengths:
             self.engine.blocks.admit(self._new_id(), int(length) - 1)
@@ -321,7 +337,7 @@ def run_ours(args, world, rank, local):
     _build.build()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    wl = Workload(args, rank, device)
+    wl = Workload(args, rank, device, world)
     eng = wl.engine
     cfg = wl.cfg
     stream = torch.cuda.current_stream(device)
