@@ -67,17 +67,6 @@ __device__ __forceinline__ float conv_silu(const uint16_t* __restrict__ w, int c
   return silu_bf(bfr(y));
 }
 
-// The same with the weight row in shared memory.
-__device__ __forceinline__ float conv_silu_smem(const uint16_t* w, int c, float h0, float h1,
-                                                float h2, float x) {
-  const uint2 wv = *reinterpret_cast<const uint2*>(w + (size_t)c * 4);
-  float y = bf16_lo(wv.x) * h0;
-  y = fmaf(bf16_hi(wv.x), h1, y);
-  y = fmaf(bf16_lo(wv.y), h2, y);
-  y = fmaf(bf16_hi(wv.y), x, y);
-  return silu_bf(bfr(y));
-}
-
 // g and beta of one (token, head) from the logits, each op rounded like the reference.
 __device__ __forceinline__ void make_gates(float a, float b, float a_log, float dt_bias,
                                            float& g, float& beta) {
@@ -314,9 +303,12 @@ __global__ void __launch_bounds__(128)
                              float* __restrict__ g_out, float* __restrict__ beta_out, int nseq,
                              int total, int Hk, int Hv, int num_slots, unsigned int* status) {
   __shared__ float red[4][TILE];
-  // A state update launched as this kernel's programmatic dependent may start
-  // streaming its state now; it reads this kernel's outputs only after they land.
-  asm volatile("griddepcontrol.launch_dependents;");
+  // Launched as a dependent of the kernel before it: nothing is touched before
+  // that kernel has completed. A state update launched as this kernel's own
+  // dependent may start streaming its state now; it reads this kernel's
+  // outputs only after they land.
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int blk = blockIdx.y;
   const int c = blk * kHead + tid;
@@ -423,6 +415,8 @@ __global__ void gdn_taps_store_kernel(const uint16_t* __restrict__ qkv, uint16_t
 __global__ void gated_rmsnorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ z,
                                      const uint16_t* __restrict__ w, float eps,
                                      uint16_t* __restrict__ out, long long rows, int width) {
+  pdl_wait();
+  pdl_trigger();
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -524,14 +518,14 @@ extern "C" int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cu_seqlens == nullptr) {
     dim3 grid((total_tokens + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
-    gdn_prefill_front_kernel<kTokTileDecode><<<grid, 128, 0, s>>>(
-        qkv, a, b, conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g,
-        beta, nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
+    launch_pdl(gdn_prefill_front_kernel<kTokTileDecode>, grid, dim3(128), 0, s, qkv, a, b,
+               conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g, beta,
+               nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
   } else {
     dim3 grid((total_tokens + kTokTile - 1) / kTokTile, 2 * Hk + Hv);
-    gdn_prefill_front_kernel<kTokTile><<<grid, 128, 0, s>>>(
-        qkv, a, b, conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g,
-        beta, nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
+    launch_pdl(gdn_prefill_front_kernel<kTokTile>, grid, dim3(128), 0, s, qkv, a, b, conv_w,
+               A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g, beta, nseq,
+               total_tokens, Hk, Hv, num_slots, device_status_word());
   }
   return check_launch(name);
 }
@@ -563,8 +557,8 @@ extern "C" int sc_gated_rmsnorm(const sc_bf16* y, const sc_bf16* z, const sc_bf1
              SC_ERR_INVALID, "%s: pointers must be 8-byte aligned", name);
   if (rows == 0) return SC_OK;
   const long long blocks = (rows + 7) / 8;
-  gated_rmsnorm_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      y, z, w, eps, out, rows, width);
+  launch_pdl(gated_rmsnorm_kernel, dim3((unsigned)blocks), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), y, z, w, eps, out, rows, width);
   return check_launch(name);
 }
 
@@ -616,15 +610,15 @@ extern "C" int sc_gdn_decode_glue(const sc_bf16* qkv, const sc_bf16* z, const sc
   float* beta = reinterpret_cast<float*>(w + 2 * qk + 2 * vy + gb);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid((B + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
-  gdn_prefill_front_kernel<kTokTileDecode><<<grid, 128, 0, s>>>(
-      qkv, a, b, conv_w, A_log, dt_bias, taps, nullptr, state_slot, position, q, k, v, g, beta, B,
-      B, Hk, Hv, num_slots, device_status_word());
+  launch_pdl(gdn_prefill_front_kernel<kTokTileDecode>, grid, dim3(128), 0, s, qkv, a, b, conv_w,
+             A_log, dt_bias, taps, (const int32_t*)nullptr, state_slot, position, q, k, v, g,
+             beta, B, B, Hk, Hv, num_slots, device_status_word());
   if (int rc = check_launch(name)) return rc;
   if (int rc = gdn_bulk_launch(name, q, k, v, g, beta, state, state_slot, y, B, Hk, Hv, 128,
                                num_slots, s, BulkLaunch::kStateAhead))
     return rc;
   const long long rows = (long long)B * Hv;
-  gated_rmsnorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(y, z, norm_w, eps, out, rows,
-                                                                  128);
+  launch_pdl(gated_rmsnorm_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, s,
+             (const uint16_t*)y, z, norm_w, eps, out, rows, 128);
   return check_launch(name);
 }
