@@ -389,6 +389,103 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// The front for a decode batch (row i is one token at position seq_start[i]):
+// one warp per (row, head) with four channels per lane, so every access is an
+// 8-byte vector and the q/k L2 norm is one warp sum. The arithmetic and
+// rounding points are those of gdn_prefill_front_kernel (only the order of the
+// norm's sum differs). Reads ring rows (start-3..start-1) & 3 of the row's slot
+// and stores the input into row start & 3.
+__global__ void __launch_bounds__(128)
+    gdn_decode_front_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ a_in,
+                            const uint16_t* __restrict__ b_in,
+                            const uint16_t* __restrict__ conv_w,
+                            const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                            uint16_t* __restrict__ taps, const int32_t* __restrict__ seq_slot,
+                            const int32_t* __restrict__ seq_start, uint16_t* __restrict__ q_out,
+                            uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out,
+                            float* __restrict__ g_out, float* __restrict__ beta_out, int B,
+                            int Hk, int Hv, int num_slots, unsigned int* status) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int nh = 2 * Hk + Hv;
+  const long long item = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (item >= (long long)B * nh) return;
+  const int i = (int)(item / nh), blk = (int)(item - (long long)i * nh);
+  const size_t C = (size_t)nh * kHead;
+  const int c0 = blk * kHead + 4 * lane;
+  const int slot = seq_slot != nullptr ? __ldg(seq_slot + i) : i;
+  const int start = __ldg(seq_start + i);
+  float val[4] = {0.f, 0.f, 0.f, 0.f};
+  bool active = slot >= 0;  // an inactive row: no history, outputs unused
+  if (active && (slot >= num_slots || start < 0)) {
+    if (lane == 0) flag_device(status, DEV_BAD_INDEX);
+    active = false;
+  }
+  if (active) {
+    uint16_t* ring = taps + (size_t)slot * kRing * C + c0;
+    const uint2 h0 = *reinterpret_cast<const uint2*>(ring + (size_t)((start - 3) & 3) * C);
+    const uint2 h1 = *reinterpret_cast<const uint2*>(ring + (size_t)((start - 2) & 3) * C);
+    const uint2 h2 = *reinterpret_cast<const uint2*>(ring + (size_t)((start - 1) & 3) * C);
+    const uint2 x = *reinterpret_cast<const uint2*>(qkv + (size_t)i * C + c0);
+    const float hx0[4] = {bf16_lo(h0.x), bf16_hi(h0.x), bf16_lo(h0.y), bf16_hi(h0.y)};
+    const float hx1[4] = {bf16_lo(h1.x), bf16_hi(h1.x), bf16_lo(h1.y), bf16_hi(h1.y)};
+    const float hx2[4] = {bf16_lo(h2.x), bf16_hi(h2.x), bf16_lo(h2.y), bf16_hi(h2.y)};
+    const float xx[4] = {bf16_lo(x.x), bf16_hi(x.x), bf16_lo(x.y), bf16_hi(x.y)};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) val[e] = conv_silu(conv_w, c0 + e, hx0[e], hx1[e], hx2[e], xx[e]);
+    *reinterpret_cast<uint2*>(ring + (size_t)(start & 3) * C) = x;
+  }
+  if (blk >= 2 * Hk) {  // a value head: v and this row's gates
+    const int h = blk - 2 * Hk;
+    *reinterpret_cast<uint2*>(v_out + ((size_t)i * Hv + h) * kHead + 4 * lane) =
+        make_uint2(pack_bf16x2(val[0], val[1]), pack_bf16x2(val[2], val[3]));
+    if (lane == 0) {
+      const size_t e = (size_t)i * Hv + h;
+      float g, beta;
+      make_gates(bf16_to_f(a_in[e]), bf16_to_f(b_in[e]), a_log[h], dt_bias[h], g, beta);
+      g_out[e] = g;
+      beta_out[e] = beta;
+    }
+    return;
+  }
+  const float m =
+      warp_sum(val[0] * val[0] + val[1] * val[1] + val[2] * val[2] + val[3] * val[3]) *
+      (1.f / kHead);
+  const bool is_q = blk < Hk;
+  const int head = is_q ? blk : blk - Hk;
+  const float scale = is_q ? bfr(1.f / kHead) : bfr(0.08838834764831845f);
+  const float rn = 1.f / sqrtf(m + 1e-6f);
+  float o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) o[e] = bf16_to_f(f_to_bf16(bfr(val[e] * rn) * scale));
+  *reinterpret_cast<uint2*>((is_q ? q_out : k_out) + ((size_t)i * Hk + head) * kHead + 4 * lane) =
+      make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+}
+
+// Launches the decode-batch front: the vectorised kernel when every operand it
+// reads or writes as 8-byte vectors is 8-byte aligned, else the per-channel one.
+cudaError_t launch_decode_front(const uint16_t* qkv, const uint16_t* a, const uint16_t* b,
+                                const uint16_t* conv_w, const float* a_log,
+                                const float* dt_bias, uint16_t* taps, const int32_t* seq_slot,
+                                const int32_t* seq_start, uint16_t* q, uint16_t* k, uint16_t* v,
+                                float* g, float* beta, int B, int Hk, int Hv, int num_slots,
+                                cudaStream_t s) {
+  const uintptr_t any = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(taps) |
+                        reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(conv_w);
+  if ((any & 7) == 0) {
+    const long long items = (long long)B * (2 * Hk + Hv);
+    return launch_pdl(gdn_decode_front_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), 0,
+                      s, qkv, a, b, conv_w, a_log, dt_bias, taps, seq_slot, seq_start, q, k, v,
+                      g, beta, B, Hk, Hv, num_slots, device_status_word());
+  }
+  dim3 grid((B + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
+  return launch_pdl(gdn_prefill_front_kernel<kTokTileDecode>, grid, dim3(128), 0, s, qkv, a, b,
+                    conv_w, a_log, dt_bias, taps, (const int32_t*)nullptr, seq_slot, seq_start,
+                    q, k, v, g, beta, B, B, Hk, Hv, num_slots, device_status_word());
+}
+
 // Ring rows of each prompt's last min(3, n) inputs. grid (nseq, ceil(C / 256)).
 __global__ void gdn_taps_store_kernel(const uint16_t* __restrict__ qkv, uint16_t* __restrict__ taps,
                                       const int32_t* __restrict__ cu,
@@ -517,10 +614,8 @@ extern "C" int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const 
   if (total_tokens == 0) return SC_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cu_seqlens == nullptr) {
-    dim3 grid((total_tokens + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
-    launch_pdl(gdn_prefill_front_kernel<kTokTileDecode>, grid, dim3(128), 0, s, qkv, a, b,
-               conv_w, A_log, dt_bias, taps, cu_seqlens, seq_slot, seq_start, q, k, v, g, beta,
-               nseq, total_tokens, Hk, Hv, num_slots, device_status_word());
+    launch_decode_front(qkv, a, b, conv_w, A_log, dt_bias, taps, seq_slot, seq_start, q, k, v,
+                        g, beta, total_tokens, Hk, Hv, num_slots, s);
   } else {
     dim3 grid((total_tokens + kTokTile - 1) / kTokTile, 2 * Hk + Hv);
     launch_pdl(gdn_prefill_front_kernel<kTokTile>, grid, dim3(128), 0, s, qkv, a, b, conv_w,
@@ -609,10 +704,8 @@ extern "C" int sc_gdn_decode_glue(const sc_bf16* qkv, const sc_bf16* z, const sc
   float* g = reinterpret_cast<float*>(w + 2 * qk + 2 * vy);
   float* beta = reinterpret_cast<float*>(w + 2 * qk + 2 * vy + gb);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 grid((B + kTokTileDecode - 1) / kTokTileDecode, 2 * Hk + Hv);
-  launch_pdl(gdn_prefill_front_kernel<kTokTileDecode>, grid, dim3(128), 0, s, qkv, a, b, conv_w,
-             A_log, dt_bias, taps, (const int32_t*)nullptr, state_slot, position, q, k, v, g,
-             beta, B, B, Hk, Hv, num_slots, device_status_word());
+  launch_decode_front(qkv, a, b, conv_w, A_log, dt_bias, taps, state_slot, position, q, k, v, g,
+                      beta, B, Hk, Hv, num_slots, s);
   if (int rc = check_launch(name)) return rc;
   if (int rc = gdn_bulk_launch(name, q, k, v, g, beta, state, state_slot, y, B, Hk, Hv, 128,
                                num_slots, s, BulkLaunch::kStateAhead))
