@@ -350,11 +350,12 @@ int sc_exchange_wait(const unsigned int* flags, int world, const unsigned int* e
 /* The same exchange folded into the attention kernels (two launches fewer per
  * layer):
  * sc_paged_decode_attention_exchange: sc_paged_decode_attention_packed whose
- * split merge stores the packed rows [B * Hq][D + 1] straight into
- * peer_dst[p] for every rank p (float* device addresses) and, once every row
- * is out, release-stores *epoch_base + epoch_add into *peer_flag[p].
- * `counter` is a device word that is zero before the first call (the kernel
- * leaves it zero). Needs num_splits > 1.
+ * split merge writes the packed rows [B * Hq][D + 1] into `packed` (16-byte
+ * aligned; B*Hq*(D+1)*4 a multiple of 16); the merge CTA that finishes last
+ * copies the block to peer_dst[p] for every rank p (float* device addresses)
+ * and release-stores *epoch_base + epoch_add into *peer_flag[p]. `counter` is
+ * a device word that is zero before the first call (the kernel leaves it
+ * zero). Needs num_splits > 1.
  * sc_attention_combine_exchange: sc_attention_combine_packed that first waits
  * (bounded, as sc_exchange_wait) for flags[r] to reach the epoch for every
  * r < nparts; after a timeout it writes nothing and sets the status word. */
@@ -363,7 +364,7 @@ int sc_paged_decode_attention_exchange(const sc_bf16* q, const sc_bf16* kv_pool,
                                        const int32_t* ctx_len, int B, int Hq, int Hkv, int D,
                                        int P, int max_pages, int pages_per_split,
                                        int num_splits, float scale, float* part_out,
-                                       float* part_lse, float* const* peer_dst,
+                                       float* part_lse, float* packed, float* const* peer_dst,
                                        unsigned int* const* peer_flag, unsigned int* counter,
                                        const unsigned int* epoch_base, unsigned int epoch_add,
                                        int world, void* stream);

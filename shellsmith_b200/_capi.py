@@ -39,7 +39,8 @@ SIGNATURES = {
     "sc_exchange_put": [_P, ctypes.c_longlong, _P, _P, _P, ctypes.c_uint, _I, _P],
     "sc_exchange_wait": [_P, _I, _P, ctypes.c_uint, _P],
     "sc_paged_decode_attention_exchange": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
-                                           _F, _P, _P, _P, _P, _P, _P, ctypes.c_uint, _I, _P],
+                                           _F, _P, _P, _P, _P, _P, _P, _P, ctypes.c_uint, _I,
+                                           _P],
     "sc_attention_combine_exchange": [_P, _P, _P, ctypes.c_uint, _I, _I, _I, _P, _P, _P],
     "sc_kv_q8_block_bytes": [_I],
     "sc_kv_append_q8": [_P, _P, _P, _P, _I, _I, _I, _I, _I64, _P],

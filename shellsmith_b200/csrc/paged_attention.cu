@@ -474,11 +474,8 @@ __global__ void __launch_bounds__(kCombineThreads)
     const float val = empty ? 0.f : total / wsum;
     const float l = empty ? -CUDART_INF_F : M + logf(wsum);
     if constexpr (kPut) {
-      for (int p = 0; p < put.world; ++p) {
-        float* dst = put.dst[p] + (size_t)row * (D + 1);
-        dst[d] = val;
-        if (blockIdx.y == 0 && lane == 0) dst[D] = l;
-      }
+      put.local[(size_t)row * (D + 1) + d] = val;
+      if (blockIdx.y == 0 && lane == 0) put.local[(size_t)row * (D + 1) + D] = l;
     } else {
       if (packed != nullptr)
         packed[(size_t)row * (D + 1) + d] = val;
@@ -493,11 +490,25 @@ __global__ void __launch_bounds__(kCombineThreads)
     }
   }
   if constexpr (kPut) {
-    __syncthreads();  // this CTA's stores precede thread 0's fence below
+    // The CTA that arrives last copies the whole packed block to every rank
+    // and publishes the epoch: one system-scope fence per launch.
+    __shared__ int last;
+    __syncthreads();  // this CTA's rows precede thread 0's fence and arrival
     if (threadIdx.x == 0) {
-      __threadfence_system();
-      const unsigned int total = gridDim.x * gridDim.y;
-      if (atomicAdd(put.counter, 1u) == total - 1) {
+      __threadfence();
+      last = atomicAdd(put.counter, 1u) == gridDim.x * gridDim.y - 1;
+      if (last) __threadfence();  // every other CTA's rows are visible from here
+    }
+    __syncthreads();
+    if (last) {
+      const uint4* src = reinterpret_cast<const uint4*>(put.local);
+      const int chunks = (int)(gridDim.x * (size_t)(D + 1) * 4 / 16);
+      for (int p = 0; p < put.world; ++p) {
+        uint4* dst = reinterpret_cast<uint4*>(put.dst[p]);
+        for (int i = threadIdx.x; i < chunks; i += blockDim.x) dst[i] = src[i];
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
         *put.counter = 0;  // ready for the next launch (stream order)
         __threadfence_system();
         const unsigned int epoch = *put.epoch_base + put.epoch_add;
@@ -686,17 +697,23 @@ extern "C" int sc_paged_decode_attention_exchange(
     const sc_bf16* q, const sc_bf16* kv_pool, int64_t num_pages, const int32_t* block_table,
     const int32_t* ctx_len, int B, int Hq, int Hkv, int D, int P, int max_pages,
     int pages_per_split, int num_splits, float scale, float* part_out, float* part_lse,
-    float* const* peer_dst, unsigned int* const* peer_flag, unsigned int* counter,
-    const unsigned int* epoch_base, unsigned int epoch_add, int world, void* stream) {
+    float* packed, float* const* peer_dst, unsigned int* const* peer_flag,
+    unsigned int* counter, const unsigned int* epoch_base, unsigned int epoch_add, int world,
+    void* stream) {
   const char* name = "sc_paged_decode_attention_exchange";
-  SC_REQUIRE(peer_dst && peer_flag && counter && epoch_base, SC_ERR_INVALID, "%s: null pointer",
-             name);
+  SC_REQUIRE(packed && peer_dst && peer_flag && counter && epoch_base, SC_ERR_INVALID,
+             "%s: null pointer", name);
+  SC_REQUIRE((reinterpret_cast<uintptr_t>(packed) & 15) == 0 &&
+                 ((long long)B * Hq * (D + 1) * 4) % 16 == 0,
+             SC_ERR_INVALID, "%s: packed must be 16-byte aligned and B*Hq*(D+1)*4 a multiple "
+             "of 16", name);
   SC_REQUIRE(world > 0 && world <= 1024, SC_ERR_INVALID, "%s: world=%d", name, world);
   SC_REQUIRE(num_splits > 1 && B > 0, SC_ERR_INVALID,
              "%s: needs num_splits > 1 (got %d) and B > 0 (got %d)", name, num_splits, B);
   SC_REQUIRE((long long)B * Hq <= 65535, SC_ERR_INVALID, "%s: B*Hq=%lld rows", name,
              (long long)B * Hq);
   sc::PeerPut put;
+  put.local = packed;
   put.dst = peer_dst;
   put.flag = peer_flag;
   put.counter = counter;

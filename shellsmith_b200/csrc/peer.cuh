@@ -19,10 +19,12 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
   return v;
 }
 
-// Where a merge kernel sends its rows: dst[p] is rank p's receive slot for
+// Where a merge kernel sends its rows: local is this rank's packed block
+// (16-byte aligned, a multiple of 16 bytes), dst[p] rank p's receive slot for
 // this rank, flag[p] rank p's flag for this rank; counter is a local word,
 // zero between launches.
 struct PeerPut {
+  float* local = nullptr;
   float* const* dst = nullptr;
   unsigned int* const* flag = nullptr;
   unsigned int* counter = nullptr;

@@ -131,17 +131,17 @@ class PeerExchange:
 
     def attention_put(self, q: torch.Tensor, pool: torch.Tensor, table: torch.Tensor,
                       ctx: torch.Tensor, scale: float, *, max_pages: int,
-                      pages_per_split: int, num_splits: int, workspace, epoch: torch.Tensor,
-                      epoch_add: int, parity: int) -> None:
-        """Split-K attention of this rank's pages whose merge stores the packed rows
-        into every rank's slot for this rank and then raises the epoch flags (one
-        kernel pair; sc_paged_decode_attention_exchange)."""
+                      pages_per_split: int, num_splits: int, workspace, packed: torch.Tensor,
+                      epoch: torch.Tensor, epoch_add: int, parity: int) -> None:
+        """Split-K attention of this rank's pages whose merge writes the packed rows
+        into `packed`; its last CTA copies them into every rank's slot for this rank and
+        raises the epoch flags (one kernel pair; sc_paged_decode_attention_exchange)."""
         B, hq, d = q.shape
         num_pages, hkv, page, _ = paged._pool_dims(pool)
         part_out, part_lse = workspace.views(B, num_splits)
         _capi.call("sc_paged_decode_attention_exchange", ptr(q), ptr(pool), num_pages,
                    ptr(table), ptr(ctx), B, hq, hkv, d, page, max_pages, pages_per_split,
-                   num_splits, float(scale), ptr(part_out), ptr(part_lse),
+                   num_splits, float(scale), ptr(part_out), ptr(part_lse), ptr(packed),
                    ptr(self.dst[parity]), ptr(self.flag_ptrs), ptr(self.counter), ptr(epoch),
                    epoch_add, self.world, stream_of(q))
 
@@ -236,10 +236,9 @@ class ShardedSequence:
 
     def enable_peer_exchange(self, group=None, fused: bool = False) -> None:
         """Exchange the packed partials by NVLink stores instead of NCCL (collective:
-        every rank calls it). By default a put and a wait kernel carry the packed block
-        (one fence per destination). fused: the split merge itself stores into the peers
-        and the final merge waits for them (two launches fewer per layer, but every
-        merge CTA fences at system scope; measured slower at 2 GPUs)."""
+        every rank calls it). By default a put and a wait kernel carry the packed block.
+        fused: the split merge's last CTA copies the block into the peers and the final
+        merge waits for them (two launches fewer per layer)."""
         if self.kv.shape[0] % 2:
             raise ValueError("peer exchange alternates receive buffers per attention layer: "
                              "it needs an even number of attention layers")
@@ -284,7 +283,8 @@ class ShardedSequence:
             self.peer.attention_put(q, pool, self.table, self.ctx, scale,
                                     max_pages=self.capacity, pages_per_split=self.pages_per_split,
                                     num_splits=self.num_splits, workspace=self.workspace,
-                                    epoch=self.epoch, epoch_add=layer + 1, parity=parity)
+                                    packed=self.packed, epoch=self.epoch, epoch_add=layer + 1,
+                                    parity=parity)
             self.peer.merge(self.out, self.epoch, layer + 1, parity)
             return self.out
         paged.paged_decode_attention_packed(q, pool, self.table, self.ctx, scale,
