@@ -124,3 +124,36 @@ def test_reference_signature(cuda):
     assert np.abs(s.cpu().numpy() - want_s).max() <= STATE_ATOL
     with pytest.raises(ValueError):
         numerics.gated_delta_chunked(qd, kd, vd, gd, bd, s0d, chunk=32)
+
+
+def test_config1_full_size_sampled_chains(cuda):
+    """Config 1 at full size (B = 8, T = 4096, 16 key / 32 value heads, 256 chains of 64
+    chunks, 537 MB of v): every chain runs on the GPU and six (sequence, value head)
+    chains — the first and last of the grid and four drawn at random — are checked
+    against the float64 sequential recurrence over all 4,096 tokens."""
+    from shellsmith_b200.workloads import gdn_token_inputs_device
+
+    B, T, Hk, Hv, d = 8, 4096, 16, 32, 128
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(1)
+    q, k, v, decay, beta = gdn_token_inputs_device(gen, B * T, Hk, Hv, d, d, device=cuda)
+    state = torch.zeros((B, Hv, d, d), dtype=torch.float32, device=cuda)
+    out = numerics.gdn_chunk_prefill(q, k, v, decay, beta, state, T=T)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(11)
+    picks = [(0, 0), (B - 1, Hv - 1)] + [(int(rng.integers(B)), int(rng.integers(Hv)))
+                                         for _ in range(4)]
+    group = Hv // Hk
+    for b, h in picks:
+        rows = slice(b * T, (b + 1) * T)
+        kh = h // group
+        qs = q[rows, kh].float().cpu().numpy()[None, :, None]
+        ks = k[rows, kh].float().cpu().numpy()[None, :, None]
+        vs = v[rows, h].float().cpu().numpy()[None, :, None]
+        gs = decay[rows, h].cpu().numpy()[None, :, None]
+        bs = beta[rows, h].cpu().numpy()[None, :, None]
+        y, s = ogdn.sequential(qs, ks, vs, gs, bs, np.zeros((1, 1, d, d)))
+        np.testing.assert_allclose(out[rows, h].float().cpu().numpy(), y[0, :, 0],
+                                   rtol=RTOL, atol=ATOL, err_msg=f"chain {(b, h)}")
+        err = np.abs(state[b, h].cpu().numpy() - s[0, 0]).max()
+        assert err <= STATE_ATOL, (b, h, err)
