@@ -280,3 +280,36 @@ def test_single_rank_direct_path_matches_packed_path(cuda):
     from shellsmith_b200 import _capi
 
     _capi.check_device()
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_config4_full_context(cuda, world):
+    """Config 4 at full size: one 131,072-token sequence (then one decode token) with the
+    one-wave split, on one GPU or emulated as two ranks on this GPU merged as the
+    exchange would; the whole context against the float64 oracle."""
+    tokens = 131_072
+    q, k, v = _sequence(tokens + 1, seed=40)
+    shards = [ShardedSequence(tokens, r, world, attention_layers=1, kv_heads=HKV, head_dim=D,
+                              q_heads=HQ, headroom_pages=8) for r in range(world)]
+    for s in shards:
+        _fill(s, k, v)
+        s.begin_token()
+    t = tokens
+    if world == 1:
+        out = shards[0].attention(0, q.cuda(), k[t:t + 1].cuda(), v[t:t + 1].cuda(), 1 / 16)
+    else:
+        parts = []
+        for s in shards:
+            def keep(dst, src):
+                parts.append(src.clone())
+            s.attention(0, q.cuda(), k[t:t + 1].cuda(), v[t:t + 1].cuda(), 1 / 16,
+                        all_gather=keep)
+        out, _ = paged.attention_combine_packed(torch.stack(parts))
+    torch.cuda.synchronize()
+    want, _ = oatt.decode_attention(q[0].float().numpy(), k[:t + 1].float().numpy(),
+                                    v[:t + 1].float().numpy(), 1 / 16)
+    np.testing.assert_allclose(out.float().cpu().numpy().reshape(HQ, D), want, rtol=RTOL,
+                               atol=ATOL)
+    from shellsmith_b200 import _capi
+
+    _capi.check_device()
