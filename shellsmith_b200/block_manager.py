@@ -115,16 +115,17 @@ class BlockManager:
             raise OutOfPages("pool exhausted while appending decode tokens")
         if np.any(lengths // self.page_size + needs_page > self.max_pages_per_seq):
             raise OutOfPages("a sequence outgrew max_pages_per_seq")
-        out = np.empty(len(slots), np.int64)
-        for i, (slot, length, new_page) in enumerate(zip(slots.tolist(), lengths.tolist(),
-                                                         needs_page.tolist())):
-            if new_page:
-                page = self.take_pages(1)[0]
-                self.pages[slot].append(page)
-                self.table[slot, length // self.page_size] = page
-                self.dirty_rows.add(slot)
-            out[i] = self.pages[slot][length // self.page_size] * self.page_size + (
-                length % self.page_size)
+        # Only a sequence at a page boundary changes its page list (about one row in
+        # P per step); every other row's slot is read from the table, which mirrors
+        # the page lists row for row.
+        for i in np.flatnonzero(needs_page).tolist():
+            slot, length = int(slots[i]), int(lengths[i])
+            page = self.take_pages(1)[0]
+            self.pages[slot].append(page)
+            self.table[slot, length // self.page_size] = page
+            self.dirty_rows.add(slot)
+        out = (self.table[slots, lengths // self.page_size].astype(np.int64) * self.page_size
+               + lengths % self.page_size)
         self.lengths[slots] = lengths + 1
         return out
 
