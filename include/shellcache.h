@@ -346,6 +346,12 @@ int sc_exchange_put(const void* src, long long bytes, void* const* peer_dst,
                     unsigned int epoch_add, int world, void* stream);
 int sc_exchange_wait(const unsigned int* flags, int world, const unsigned int* epoch_base,
                      unsigned int epoch_add, void* stream);
+/* sc_exchange_wait with the number of polls of one flag before it gives up
+ * (sc_exchange_wait: 2^24, seconds with its 64 ns back-off): a caller's own
+ * time-out, or a test that a wait nobody answers ends with the status bit. */
+int sc_exchange_wait_limited(const unsigned int* flags, int world,
+                             const unsigned int* epoch_base, unsigned int epoch_add,
+                             unsigned int max_polls, void* stream);
 
 /* The same exchange folded into the attention kernels (two launches fewer per
  * layer):

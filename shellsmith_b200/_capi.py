@@ -38,6 +38,7 @@ SIGNATURES = {
     "sc_gated_rmsnorm": [_P, _P, _P, _F, _P, _I64, _I, _P],
     "sc_exchange_put": [_P, ctypes.c_longlong, _P, _P, _P, ctypes.c_uint, _I, _P],
     "sc_exchange_wait": [_P, _I, _P, ctypes.c_uint, _P],
+    "sc_exchange_wait_limited": [_P, _I, _P, ctypes.c_uint, ctypes.c_uint, _P],
     "sc_paged_decode_attention_exchange": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                            _F, _P, _P, _P, _P, _P, _P, _P, ctypes.c_uint, _I,
                                            _P],

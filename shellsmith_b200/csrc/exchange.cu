@@ -43,11 +43,11 @@ __global__ void __launch_bounds__(256)
 // One thread waits until flags[r] has reached the epoch for every r < world.
 __global__ void exchange_wait_kernel(const unsigned int* flags, int world,
                                      const unsigned int* epoch_base, unsigned int epoch_add,
-                                     unsigned int* status) {
+                                     uint32_t max_polls, unsigned int* status) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x != 0) return;
-  wait_epochs(flags, world, *epoch_base + epoch_add, status);
+  wait_epochs(flags, world, *epoch_base + epoch_add, status, max_polls);
 }
 
 }  // namespace
@@ -72,14 +72,22 @@ extern "C" int sc_exchange_put(const void* src, long long bytes, void* const* pe
   return check_launch(name);
 }
 
-extern "C" int sc_exchange_wait(const unsigned int* flags, int world,
-                                const unsigned int* epoch_base, unsigned int epoch_add,
-                                void* stream) {
+extern "C" int sc_exchange_wait_limited(const unsigned int* flags, int world,
+                                        const unsigned int* epoch_base, unsigned int epoch_add,
+                                        unsigned int max_polls, void* stream) {
   using namespace sc;
   const char* name = "sc_exchange_wait";
   SC_REQUIRE(flags && epoch_base, SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE(world > 0 && world <= 1024, SC_ERR_INVALID, "%s: world=%d", name, world);
+  SC_REQUIRE(max_polls > 0, SC_ERR_INVALID, "%s: max_polls must be positive", name);
   launch_pdl(exchange_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
-             flags, world, epoch_base, epoch_add, device_status_word());
+             flags, world, epoch_base, epoch_add, (uint32_t)max_polls, device_status_word());
   return check_launch(name);
+}
+
+extern "C" int sc_exchange_wait(const unsigned int* flags, int world,
+                                const unsigned int* epoch_base, unsigned int epoch_add,
+                                void* stream) {
+  return sc_exchange_wait_limited(flags, world, epoch_base, epoch_add, sc::kPeerSpinLimit,
+                                  stream);
 }

@@ -44,16 +44,17 @@ struct PeerWait {
 };
 
 // Called by one thread: returns once flags[r] has reached `want` for every
-// r < world. After kPeerSpinLimit polls of one flag (or when an earlier wait on
-// this device already gave up) it flags DEV_WAIT_TIMEOUT and returns false.
+// r < world. After `limit` polls of one flag (or when an earlier wait on this
+// device already gave up) it flags DEV_WAIT_TIMEOUT and returns false.
 __device__ __forceinline__ bool wait_epochs(const unsigned int* flags, int world,
-                                            unsigned int want, unsigned int* status) {
+                                            unsigned int want, unsigned int* status,
+                                            uint32_t limit = kPeerSpinLimit) {
   if (status != nullptr && (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT))
     return false;
   for (int r = 0; r < world; ++r) {
     uint32_t i = 0;
     while ((int)(ld_acquire_sys(flags + r) - want) < 0) {
-      if (++i >= kPeerSpinLimit) {
+      if (++i >= limit) {
         flag_device(status, DEV_WAIT_TIMEOUT);
         return false;
       }

@@ -313,3 +313,23 @@ def test_config4_full_context(cuda, world):
     from shellsmith_b200 import _capi
 
     _capi.check_device()
+
+
+def test_exchange_wait_times_out_and_the_context_stays_usable(cuda):
+    """A wait on a flag that nothing raises gives up after its poll limit: the kernel
+    returns, the device status word carries the time-out (DeviceFault on the host), and a
+    later wait whose flag is raised completes normally."""
+    from shellsmith_b200 import _capi
+    from shellsmith_b200._torch import ptr, stream_of
+
+    _capi.check_device()
+    flags = torch.zeros(1, dtype=torch.int32, device=cuda)
+    epoch = torch.zeros(1, dtype=torch.int32, device=cuda)
+    _capi.call("sc_exchange_wait_limited", ptr(flags), 1, ptr(epoch), 7, 4096, stream_of(flags))
+    torch.cuda.synchronize()
+    with pytest.raises(_capi.DeviceFault, match="bounded wait"):
+        _capi.check_device()
+    flags.fill_(7)
+    _capi.call("sc_exchange_wait_limited", ptr(flags), 1, ptr(epoch), 7, 4096, stream_of(flags))
+    torch.cuda.synchronize()
+    _capi.check_device()
