@@ -134,22 +134,29 @@ def sm_count(device) -> int:
 
 
 def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
-               total_work: int | None = None, sms: int = 148) -> tuple:
+               total_work: int | None = None, sms: int = 148, waves: int = 2,
+               cap: int = 256, rows: int | None = None) -> tuple:
     """(pages_per_split, num_splits) for a batch whose longest sequence has that many pages.
 
-    Without an explicit size, a split is the largest power of two of pages,
-    at most 256 (4 MiB of K/V per kv head at D = 256), that still gives at
-    least two waves of CTAs (one CTA per SM) for `total_work` = sum over
-    sequences of pages x kv heads x head groups. Large splits keep the
-    partials and their combine small; the floor keeps a single long sequence
-    spread over every SM.
+    Without an explicit size, a split is the largest power of two of pages, at
+    most `cap`, whose CTAs still fill `waves` waves (one CTA per SM). The CTA
+    count is estimated as total_work / pps, plus half a split per row for the
+    rounding of each sequence when `rows` (sequences x head groups) is given;
+    total_work = sum over sequences of pages x kv heads x head groups. Large
+    splits keep the per-CTA overhead, the partials and their combine small (with
+    the sequences launched longest first the last wave stays short); enough
+    waves keep the SMs evenly loaded and a single long sequence spread over all
+    of them. bf16 pages use three waves and up to 1,024 pages (16 MiB of K/V per
+    kv head at D = 256); 8-bit pages, which carry half the bytes per page and
+    more work per byte, measured best at two waves of at most 256 pages.
     """
     if pages_per_split:
         pps = pages_per_split
     elif total_work:
-        target = max(1, total_work // (2 * sms))
+        def ctas(p):
+            return total_work / p + (rows / 2 if rows else 0)
         pps = 16
-        while pps * 2 <= min(256, target):
+        while pps * 2 <= cap and ctas(pps * 2) >= waves * sms:
             pps *= 2
     else:
         pps = 64
@@ -207,9 +214,11 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
         raise ValueError("paged_decode_attention: inconsistent shapes")
     max_pages = block_table.shape[1]
     groups = hkv * ((hq // hkv + 7) // 8)
+    q8 = kv_pool.dtype == torch.uint8
     pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
                              None if total_pages is None else total_pages * groups,
-                             sm_count(q.device))
+                             sm_count(q.device), waves=2 if q8 else 3, cap=256 if q8 else 1024,
+                             rows=None if q8 else B * groups)
     if out is None:
         out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)
     require_cuda("out", out, torch.bfloat16, 3)
