@@ -59,6 +59,15 @@ def _cudart():
     return cudart
 
 
+def epoch_base(tokens_done: int, attention_layers: int) -> int:
+    """The epoch base of a token: attention layer l of token t raises the exchange flags
+    to base + l + 1 with base = t x layers. The kernels add and compare modulo 2^32, so
+    the base wraps like a u32, returned as the int32 two's-complement image an int32
+    device word holds."""
+    e = (tokens_done * attention_layers) & 0xFFFFFFFF
+    return e - (1 << 32) if e >= 1 << 31 else e
+
+
 def _check(result, what):
     err = result[0]
     if int(err) != 0:
@@ -223,10 +232,7 @@ class ShardedSequence:
             self._h_slot[0] = -1
         self._h_ctx[0] = self.local_tokens
         # Exchange epochs: attention layer l of this token raises flags to base + l + 1.
-        # The kernels add and compare modulo 2^32, so the base wraps like a u32
-        # (stored in an int32 tensor as its two's-complement image).
-        e = (self.tokens_done * self.kv.shape[0]) & 0xFFFFFFFF
-        self._h_epoch[0] = e - (1 << 32) if e >= 1 << 31 else e
+        self._h_epoch[0] = epoch_base(self.tokens_done, self.kv.shape[0])
         self.tokens_done += 1
         self.slot.copy_(self._h_slot, non_blocking=True)
         self.ctx.copy_(self._h_ctx, non_blocking=True)
