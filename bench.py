@@ -70,7 +70,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-config1", action="store_true",
-                    help="skip the config-1 chunked-prefill, GDN-front and 8-bit KV measurements")
+                    help="skip the measurements beside config 3: configs 2 and 4 (every rank, "
+                         "sharded), configs 0 and 1, the GDN front and 8-bit KV (rank 0)")
     ap.add_argument("--front-only", action="store_true",
                     help="only time one GDN layer run from its projections (fused glue) "
                          "against the plain state update, with --batch rows; prints a JSON "
@@ -205,11 +206,17 @@ def balanced_share(args, rank: int, world: int) -> np.ndarray:
     sequences with nearly equal resident K/V bytes."""
     glob = np.random.default_rng(SEED).integers(args.min_len, args.max_len + 1,
                                                 size=args.batch * world)
-    order = np.argsort(-glob, kind="stable")
+    return glob[snake_deal(glob, rank, world)]
+
+
+def snake_deal(lengths: np.ndarray, rank: int, world: int) -> np.ndarray:
+    """Indices of `lengths` that rank `rank` holds when they are dealt longest first in
+    snake order (seats 0..N-1, then N-1..0, ...): the per-rank sums stay nearly equal."""
+    order = np.argsort(-np.asarray(lengths), kind="stable")
     pos = np.arange(order.size)
     turn, seat = pos // world, pos % world
     owner = np.where(turn % 2 == 0, seat, world - 1 - seat)
-    return glob[order[owner == rank]]
+    return order[owner == rank]
 
 
 class Workload:
@@ -421,11 +428,18 @@ def run_ours(args, world, rank, local):
     peaks = measured_peaks()
     hbm = peaks["hbm_gbs"]
 
-    prefill_c1 = front = kv8 = decode_c0 = attention_c2 = None
+    prefill_c1 = front = kv8 = decode_c0 = attention_c2 = long_c4 = None
+    if not args.no_config1:
+        # The sharded configs, on every rank (each one's own collectives, in the
+        # same order everywhere): config 2 by sequence, config 4 by KV page.
+        barrier(world)
+        attention_c2 = config2_attention(device, rank=rank, world=world)
+        long_c4 = config4_measure(args, world, rank, local, steps=200, warmup=5,
+                                  exchange=args.exchange)
+        barrier(world)
     if not args.no_config1 and rank == 0:
         prefill_c1 = config1_prefill(device)
         decode_c0 = config0_decode(device)
-        attention_c2 = config2_attention(device)
         front = gdn_front_layer(device)
         kv8 = kv8_attention_layer(wl, device)
 
@@ -486,10 +500,12 @@ def run_ours(args, world, rank, local):
     }
     if e2e is not None:
         line["e2e"] = e2e
+    if attention_c2 is not None:
+        line["config2_attention"] = attention_c2
+        line["config4_long_sequence"] = long_c4
     if prefill_c1 is not None:
         line["config1_prefill"] = prefill_c1
         line["config0_decode"] = decode_c0
-        line["config2_attention"] = attention_c2
     if front is not None:
         line["gdn_front"] = front
     if kv8 is not None:
@@ -771,20 +787,29 @@ def config0_decode(device, steps: int = 256, rounds: int = 5) -> dict:
             "launches": steps}
 
 
-def config2_attention(device, steps: int = 20, warmup: int = 3) -> dict:
+def config2_attention(device, steps: int = 20, warmup: int = 3, rank: int = 0,
+                      world: int = 1) -> dict | None:
     """Config 2: paged KV append + split-K decode attention, bf16. 64 sequences with
     contexts U[1k, 32k], 16 query / 2 KV heads, D 256, pages of 16 tokens handed out from a
     random permutation of a 150k-page pool. Each step appends one token per sequence and
     attends over the grown context. Slots, lengths and the launch order (longest first) of
-    every step are made before the timed region; 2.2 GB per step, well above L2."""
+    every step are made before the timed region; 2.2 GB per step, well above L2.
+
+    Sharded by sequence over `world` ranks with no collective on the data path (every
+    rank calls this): the 64 sequences are dealt longest first in snake order, each rank
+    runs its share on its own pool, and the step time is the max over ranks (strong
+    scaling: the 64 sequences are fixed). Returns the record on rank 0, else None."""
     import torch
 
     from shellsmith_b200 import paged
 
-    B, hq, hkv, D, P, NP = 64, 16, 2, 256, 16, 150_000
+    B_all, hq, hkv, D, P, NP = 64, 16, 2, 256, 16, 150_000
     total = warmup + steps
     rng = np.random.default_rng(2)
-    lengths = rng.integers(1024, 32 * 1024 + 1, size=B)
+    lengths_all = rng.integers(1024, 32 * 1024 + 1, size=B_all)
+    lengths = lengths_all[np.sort(snake_deal(lengths_all, rank, world))] if world > 1 \
+        else lengths_all
+    B = len(lengths)
     need = -(-(lengths + total) // P)
     perm = rng.permutation(NP).astype(np.int32)
     table = np.zeros((B, int(need.max())), np.int32)
@@ -835,16 +860,21 @@ def config2_attention(device, steps: int = 20, warmup: int = 3) -> dict:
     from shellsmith_b200 import _capi
 
     _capi.check_device()
-    ms = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     c = ctx[warmup:].astype(np.float64)
     nbytes = (c.sum() * hkv * D * 2 * 2 + steps * B * hkv * D * 2 * 2
               + steps * B * hq * D * 2 * 2 + np.ceil(c / P).sum() * 4) / steps
-    gbs = nbytes / (ms / 1e3) / 1e9
+    nbytes = sum_over_ranks(float(nbytes), world)
+    gbs = nbytes / world / (ms / 1e3) / 1e9   # per GPU
     peak = measured_peaks()["hbm_gbs"]
     del pool
+    if rank != 0:
+        return None
     return {"workload": "config2 paged append + split-K decode attention, 64 seqs ctx U[1k,32k], "
                         "16/2 heads D256, 150k-page pool (random permutation)",
-            "ms_per_step": round(ms, 4), "tokens_per_s": round(B / (ms / 1e3), 1),
+            "n_gpus": world, "scaling": "strong",
+            "parallelism": f"sequence-sharded x{world} (snake deal by length), no collective",
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(B_all / (ms / 1e3), 1),
             "bytes_per_step": int(nbytes), "gbs": round(gbs, 1),
             "hbm_frac": round(gbs / peak, 4), "launches_per_step": 3}
 
@@ -1006,15 +1036,17 @@ def cpu_baseline(args, wl):
                       f"float64/fp32 NumPy oracle, {threads} threads"}
 
 
-def run_config4(args, world, rank, local):
+def config4_measure(args, world, rank, local, steps: int, warmup: int,
+                    exchange: str = "p2p") -> dict | None:
     """Config 4: one sequence of --ctx4 tokens; its KV pages are split evenly across the
     ranks (contiguous ranges), the GDN state (32 heads) is updated on every rank, and each
     attention layer sends the per-rank (out, lse) partial to every rank: NVLink peer
-    stores with epoch flags (--exchange p2p, default) or an NCCL all-gather (nccl)."""
+    stores with epoch flags (exchange p2p or fused) or an NCCL all-gather (nccl).
+    Every rank calls it; returns the measurement on rank 0, else None."""
     import torch
     import torch.distributed as dist
 
-    from shellsmith_b200 import _build, _capi, numerics, paged
+    from shellsmith_b200 import _build, _capi, numerics
     from shellsmith_b200.longctx import ShardedSequence
     from shellsmith_b200.workloads import gdn_token_inputs_device
 
@@ -1023,11 +1055,14 @@ def run_config4(args, world, rank, local):
     torch.cuda.set_device(device)
     L, n_attn = 48, 12
     hq, hkv, d = 16, 2, 256
+    # Page headroom on the tail rank for every token this run appends (the
+    # warm-up, the captured pass, the first replay and the timed steps).
+    headroom = -(-(warmup + steps + 4) // 16) + 1
     shard = ShardedSequence(args.ctx4, rank, world, attention_layers=n_attn, kv_heads=hkv,
-                            head_dim=d, q_heads=hq, headroom_pages=8, device=device)
-    use_p2p = world > 1 and args.exchange != "nccl"
+                            head_dim=d, q_heads=hq, headroom_pages=headroom, device=device)
+    use_p2p = world > 1 and exchange != "nccl"
     if use_p2p:
-        shard.enable_peer_exchange(fused=args.exchange == "fused")
+        shard.enable_peer_exchange(fused=exchange == "fused")
     gen = torch.Generator(device=device)
     gen.manual_seed(4)
     block = torch.randn(1 << 26, generator=gen, device=device).to(torch.bfloat16)
@@ -1057,7 +1092,7 @@ def run_config4(args, world, rank, local):
                 numerics.gdn_decode(*gdn_in[g_i], state[g_i], out=gdn_out, chained=True)
                 g_i += 1
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         shard.begin_token()
         layers()
     torch.cuda.synchronize()
@@ -1067,6 +1102,7 @@ def run_config4(args, world, rank, local):
     with torch.cuda.graph(graph):
         layers()
     torch.cuda.synchronize()
+
     def step():
         shard.begin_token()
         graph.replay()
@@ -1076,7 +1112,7 @@ def run_config4(args, world, rank, local):
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record(stream)
     torch.cuda.synchronize()
@@ -1113,32 +1149,48 @@ def run_config4(args, world, rank, local):
     shard.close()
     bytes_rank = n_attn * (shard.local_tokens * hkv * d * 2 * 2) + 36 * 4210944
     bytes_all = sum_over_ranks(float(bytes_rank), world)
+    del shard, state
     if rank != 0:
         return None
     peaks = measured_peaks()
-    per_step = ms / 1e3 / args.steps
-    line = {
-        "metric": "config4 long-context decode tokens/sec (one 128k sequence, KV sharded)",
-        "value": round(1 / per_step, 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16 kv / fp32 gdn state", "data": "synthetic",
-        "config": {"workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN "
-                               f"replicated + 12 attention with KV pages split over {world} GPU)",
-                   "parallelism": f"KV-page sharding x{world}, "
-                                  + {"fused": "attention merge stores (out, lse) into the "
-                                              "peers over NVLink, epoch flags",
-                                     "p2p": "put/wait kernels store (out, lse) into the peers "
-                                            "over NVLink, epoch flags",
-                                     "nccl": "NCCL all-gather of (out, lse)"}[args.exchange]},
+    per_step = ms / 1e3 / steps
+    return {
+        "workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN replicated "
+                    f"+ 12 attention with KV pages split over {world} GPU)",
+        "n_gpus": world, "scaling": "strong", "steps": steps, "warmup": warmup,
+        "ms_per_step": round(per_step * 1e3, 4), "tokens_per_s": round(1 / per_step, 1),
+        "parallelism": f"KV-page sharding x{world}, "
+                       + {"fused": "attention merge stores (out, lse) into the peers over "
+                                   "NVLink, epoch flags",
+                          "p2p": "put/wait kernels store (out, lse) into the peers over "
+                                 "NVLink, epoch flags",
+                          "nccl": "NCCL all-gather of (out, lse)"}[exchange],
         "hbm": {"bytes_per_step_all_ranks": bytes_all,
                 "gbs_per_gpu": round(bytes_all / world / per_step / 1e9, 1),
                 "frac_per_gpu": round(bytes_all / world / per_step / 1e9 / peaks["hbm_gbs"], 4)},
         # One layer's partial to every rank, timed alone: the put/wait kernel pair
         # (fused and p2p) or the all-gather (nccl).
         "exchange_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
-        "exchange": args.exchange if world > 1 else None,
+        "exchange": exchange if world > 1 else None,
         "all_gather_bytes_per_rank": hq * (d + 1) * 4,
+        "launch": "one CUDA graph per step",
+    }
+
+
+def run_config4(args, world, rank, local):
+    """--config 4: the config-4 measurement as the run's own JSON line."""
+    c4 = config4_measure(args, world, rank, local, args.steps, args.warmup, args.exchange)
+    if c4 is None:
+        return None
+    line = {
+        "metric": "config4 long-context decode tokens/sec (one 128k sequence, KV sharded)",
+        "value": c4["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": c4["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 kv / fp32 gdn state", "data": "synthetic",
+        "config": {"workload": c4["workload"], "parallelism": c4["parallelism"]},
+        "hbm": c4["hbm"], "exchange_us": c4["exchange_us"], "exchange": c4["exchange"],
+        "all_gather_bytes_per_rank": c4["all_gather_bytes_per_rank"],
     }
     print(json.dumps(line), flush=True)
     return line

@@ -18,3 +18,13 @@ def test_balanced_share_partitions_the_global_draw(world):
     assert np.array_equal(np.sort(np.concatenate(shares)), np.sort(glob))
     sums = np.array([s.sum() for s in shares], np.float64)
     assert sums.max() / sums.min() < 1.001
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_config2_snake_deal_partitions_the_64_sequences(world):
+    lengths = np.random.default_rng(2).integers(1024, 32 * 1024 + 1, size=64)
+    shares = [bench.snake_deal(lengths, r, world) for r in range(world)]
+    assert sorted(np.concatenate(shares).tolist()) == list(range(64))
+    assert all(len(s) == 64 // world for s in shares)
+    sums = np.array([lengths[s].sum() for s in shares], np.float64)
+    assert sums.max() / sums.min() < 1.05
