@@ -243,13 +243,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   kq_last[0] = 0;
   v_last = 0;
   if (tid < 64) fetch_gates(0);
-  auto wait_mma = [&]() {
+  // `extra` = 0 from any thread fails the step (thread 0's wait for the next
+  // chunk's K/Q tiles before it queued that chunk's G0).
+  auto wait_mma = [&](int extra = 1) {
     const int done = mbar_wait_bounded(bar_mma, mma_phase, status) ? 1 : 0;
-    if (done) mma_phase ^= 1;
-    ok = __syncthreads_and(done && ok);
-    if (ok) pending_mma = 0;
+    if (done) {
+      mma_phase ^= 1;
+      pending_mma = 0;
+    }
+    ok = __syncthreads_and(done && ok && extra);
     tc::fence_after();
     return ok;
+  };
+  // G0 of a chunk, [K;Q] K^T -> TMEM cols T_KK (lanes 0-63 KK^T, 64-127 QK^T),
+  // issued by thread 0 once the chunk's K/Q tiles have landed; no commit.
+  auto issue_g0 = [&](int chunk) {
+    const uint32_t kq = (chunk & 1) ? OFF_KQ2 : OFF_KQ;
+    constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t a = smem_addr(sm + kq + kb * 16384) + ks * 32;
+        tc::mma_bf16(tmem + T_KK, tc::desc_kmajor(a), tc::desc_kmajor(a), id, (kb | ks) != 0);
+      }
   };
 
 #pragma unroll 1
@@ -292,21 +309,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       kq_last[(c + 1) & 1] = c + 1;
     }
 
-    // ---- (2) G0: [K;Q] K^T -> TMEM cols T_KK (lanes 0-63 KK^T, 64-127 QK^T).
-    if (tid == 0) {
-      tc::fence_after();
-      constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint32_t a = smem_addr(sm + off_kq + kb * 16384) + ks * 32;
-          tc::mma_bf16(tmem + T_KK, tc::desc_kmajor(a), tc::desc_kmajor(a), id, (kb | ks) != 0);
-        }
-      tc::commit(bar_mma);
+    // ---- (2) G0: [K;Q] K^T -> TMEM cols T_KK. Chunk 0 issues it here; every
+    //          later chunk's G0 went out with the previous chunk's GS and is done.
+    if (c == 0) {
+      if (tid == 0) {
+        tc::fence_after();
+        issue_g0(0);
+        tc::commit(bar_mma);
+      }
+      pending_mma = 1;
+      if (!wait_mma()) break;
     }
-    pending_mma = 1;
-    if (!wait_mma()) break;
 
     // ---- (3) A rows (lanes 0-63) in fp32 smem and m rows (lanes 64-127) as
     //          bf16 hi/lo; this warp owns columns [32 hf, 32 hf + 32).
@@ -445,25 +458,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           make_float2(-acc[2], -acc[3]);
     }
     __syncthreads();
-    // X -> bf16 hi/lo: X^T rows (B of the Y GEMM) and X rows (rows 0-63 of [X;Y]).
+    // X -> bf16 hi/lo: X^T rows (B of the Y GEMM) first.
+    const int xj = tid & 63, xpart = tid >> 6;
     {
-      const int j = tid & 63, part = tid >> 6;
       float xc[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) xc[e] = Xf[(16 * part + e) * kAStride + j];
-      store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, j, 2 * part, xc);
-      store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, j, 2 * part + 1, xc + 8);
-      const float4* xr = reinterpret_cast<const float4*>(Xf + j * kAStride + 16 * part);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float4 x4 = xr[e];
-        xc[4 * e] = x4.x;
-        xc[4 * e + 1] = x4.y;
-        xc[4 * e + 2] = x4.z;
-        xc[4 * e + 3] = x4.w;
-      }
-      store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part, xc);
-      store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part + 1, xc + 8);
+      for (int e = 0; e < 16; ++e) xc[e] = Xf[(16 * xpart + e) * kAStride + xj];
+      store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, xj, 2 * xpart, xc);
+      store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, xj, 2 * xpart + 1, xc + 8);
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -485,6 +487,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::commit(bar_mma);
     }
     pending_mma = 1;
+    // X rows (rows 0-63 of [X;Y], read by G34) while Y runs: Y reads the m and
+    // X^T tiles only.
+    {
+      const int j = xj, part = xpart;
+      float xc[16];
+      const float4* xr = reinterpret_cast<const float4*>(Xf + j * kAStride + 16 * part);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float4 x4 = xr[e];
+        xc[4 * e] = x4.x;
+        xc[4 * e + 1] = x4.y;
+        xc[4 * e + 2] = x4.z;
+        xc[4 * e + 3] = x4.w;
+      }
+      store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part, xc);
+      store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part + 1, xc + 8);
+    }
     if (!wait_mma()) break;
     if (quarter < 2) {
       float y[32];
@@ -492,20 +511,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_chunks_hilo(sm + OFF_XYH, sm + OFF_XYL, 64 + row, 4 * hf, y);
     }
 
-    // ---- (6) S hi/lo -> smem (A of G12); decay_63 * S -> TMEM. Columns [64 hf, +64).
-    {
-      const float dl = s_decay[63];
+    // ---- (6) S hi/lo -> smem (A of G12). Columns [64 hf, +64).
 #pragma unroll 1
-      for (int q = 0; q < 2; ++q) {
-        float v[32];
-        const uint32_t col = T_S + 64 * hf + 32 * q;
-        tc::tmem_ld32(tmem + lane + col, v);
-        store_chunks_hilo(sm + OFF_SH + hf * 16384, sm + OFF_SL + hf * 16384, row, 4 * q, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] *= dl;
-        tc::tmem_st32(tmem + lane + col, v);
-      }
-      tc::tmem_wait_st();
+    for (int q = 0; q < 2; ++q) {
+      float v[32];
+      tc::tmem_ld32(tmem + lane + T_S + 64 * hf + 32 * q, v);
+      store_chunks_hilo(sm + OFF_SH + hf * 16384, sm + OFF_SL + hf * 16384, row, 4 * q, v);
     }
     fence_proxy_async_smem();
     tc::fence_before();
@@ -529,6 +540,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::commit(bar_mma);
     }
     pending_mma = 1;
+    // ---- (6b) decay_63 * S -> TMEM while G12 runs (G12 reads shared memory
+    //           and writes the T_P columns only).
+    {
+      const float dl = s_decay[63];
+#pragma unroll 1
+      for (int q = 0; q < 2; ++q) {
+        float v[32];
+        const uint32_t col = T_S + 64 * hf + 32 * q;
+        tc::tmem_ld32(tmem + lane + col, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] *= dl;
+        tc::tmem_st32(tmem + lane + col, v);
+      }
+      tc::tmem_wait_st();
+      tc::fence_before();
+    }
     if (!wait_mma()) break;
 
     // ---- (8) W^T row i for tokens [32 hf, +32); zero those U^T columns;
@@ -589,14 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     pending_mma = 1;
     if (!wait_mma()) break;
 
-    // ---- (10) O^T -> out (bf16) for tokens [32 hf, +32); (U^T r) hi/lo -> smem.
+    // ---- (10) (U^T r) hi/lo -> smem for tokens [32 hf, +32).
     {
       float u[32];
-      tc::tmem_ld32(tmem + lane + T_P + 64 + 32 * hf, u);
-      uint16_t* orow = out + ((size_t)(tok0 + 32 * hf) * Hv + h) * kD + row;
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (32 * hf + e < valid) orow[(size_t)e * Hv * kD] = f_to_bf16(u[e]);
       tc::tmem_ld32(tmem + lane + T_P + 32 * hf, u);
 #pragma unroll
       for (int e = 0; e < 32; ++e) u[e] *= s_r[32 * hf + e];
@@ -607,6 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // ---- (11) GS: S += (U^T r) K, K as an MN-major operand (dk halves 16 KiB apart).
+    int g0_ok = 1;
     if (tid == 0) {
       tc::fence_after();
       constexpr uint32_t id = tc::idesc_bf16(128, 128, false, true);
@@ -616,10 +639,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WH) + ks * 32), kd, id, true);
         tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WL) + ks * 32), kd, id, true);
       }
+      // The next chunk's K/Q tiles were fetched a chunk ahead: its G0 joins
+      // this commit, so the next chunk starts with KK^T / QK^T in TMEM.
+      if (c + 1 < nchunks) {
+        if (mbar_wait_bounded(&bar_kq[(c + 1) & 1], ((c + 1) >> 1) & 1, status))
+          issue_g0(c + 1);
+        else
+          g0_ok = 0;
+      }
       tc::commit(bar_mma);
     }
     pending_mma = 1;
-    if (!wait_mma()) break;
+    // ---- (10b) O^T -> out (bf16) for tokens [32 hf, +32) while GS and the next
+    //            G0 run (they write the T_S and T_KK columns only).
+    {
+      float o[32];
+      tc::tmem_ld32(tmem + lane + T_P + 64 + 32 * hf, o);
+      uint16_t* orow = out + ((size_t)(tok0 + 32 * hf) * Hv + h) * kD + row;
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (32 * hf + e < valid) orow[(size_t)e * Hv * kD] = f_to_bf16(o[e]);
+    }
+    if (!wait_mma(g0_ok)) break;
   }
 
   if (!ok) {
