@@ -97,31 +97,73 @@ def parse():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples the SM clock and the clock-event (throttle) reasons while the timed region
+    runs: through NVML every 20 ms when its binding loads, else nvidia-smi every 200 ms.
+    It only reads: no GPU setting is changed."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index: int):
         visible = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
         self.index = visible[index].strip() if index < len(visible) and visible[index].strip() \
             else str(index)
-        self.rows = []
+        self.rows = []   # (sm MHz, max sm MHz, frozenset of active reasons)
+        self._nvml = self._open_nvml(index)
+        self.source = "nvml" if self._nvml is not None else "nvidia-smi"
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
 
+    def _open_nvml(self, local: int):
+        """NVML handle of CUDA device `local`, found by its UUID (the CUDA and NVML
+        orders can differ), or None."""
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+            handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self._pynvml = pynvml
+            self._bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                          "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                          "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                          "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+            return handle
+        except Exception:  # noqa: BLE001 -- fall back to nvidia-smi
+            return None
+
+    def _sample_nvml(self):
+        p, h = self._pynvml, self._nvml
+        sm = p.nvmlDeviceGetClockInfo(h, p.NVML_CLOCK_SM)
+        mx = p.nvmlDeviceGetMaxClockInfo(h, p.NVML_CLOCK_SM)
+        bits = p.nvmlDeviceGetCurrentClocksEventReasons(h)
+        return float(sm), float(mx), frozenset(n for n, b in self._bits.items() if bits & b)
+
+    def _sample_smi(self):
+        out = subprocess.run(
+            ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+             "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+        r = [x.strip() for x in out.stdout.strip().split(",")]
+        if out.returncode != 0 or len(r) < 9:
+            return None
+        num = lambda x: float(x) if x.replace(".", "").isdigit() else None  # noqa: E731
+        return num(r[1]), num(r[2]), frozenset(
+            n for i, n in enumerate(self.REASONS) if r[5 + i].lower() == "active")
+
     def _run(self):
+        sample = self._sample_nvml if self._nvml is not None else self._sample_smi
+        period = 0.02 if self._nvml is not None else 0.2
         while not self._stop.is_set():
             try:
-                out = subprocess.run(
-                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                if out.returncode == 0 and out.stdout.strip():
-                    self.rows.append([x.strip() for x in out.stdout.strip().split(",")])
+                row = sample()
+                if row is not None:
+                    self.rows.append(row)
             except Exception:  # noqa: BLE001 -- clocks are advisory
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(period)
 
     def __enter__(self):
         self._thread.start()
@@ -132,16 +174,15 @@ class ClockSampler:
         self._thread.join(timeout=10)
 
     def summary(self) -> dict:
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+        sm = [r[0] for r in self.rows if r[0] is not None]
+        mx = [r[1] for r in self.rows if r[1] is not None]
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clocks unavailable"],
+                    "samples": 0, "source": self.source}
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(set().union(*(r[2] for r in self.rows))),
+                "samples": len(self.rows), "source": self.source}
 
 
 def measured_peaks() -> dict:
