@@ -28,3 +28,27 @@ def test_config2_snake_deal_partitions_the_64_sequences(world):
     assert all(len(s) == 64 // world for s in shares)
     sums = np.array([lengths[s].sum() for s in shares], np.float64)
     assert sums.max() / sums.min() < 1.05
+
+
+def test_split_floor_only_where_the_wave_rule_splits_long_sequences_finely():
+    """bf16 attention splits grow to 128 pages while half a wave of CTAs remains: config 2
+    sharded over 4 or 8 GPUs (long sequences, few rows) moves from 64 / 32 to 128 pages;
+    one or two GPUs, the config-3 batch and a batch of short sequences keep their split."""
+    from shellsmith_b200 import paged
+
+    lengths = np.random.default_rng(2).integers(1024, 32 * 1024 + 1, size=64)
+    picks = {}
+    for world in (1, 2, 4, 8):
+        share = lengths[bench.snake_deal(lengths, 0, world)]
+        pages = -(-(share + 3) // 16)
+        args = (int(pages.max()), None, int(pages.sum()) * 2, 148)
+        kw = dict(waves=3, cap=1024, rows=2 * len(share))
+        picks[world] = (paged.split_plan(*args, **kw)[0],
+                        paged.split_plan(*args, **kw, min_pages=128)[0])
+    assert picks == {1: (256, 256), 2: (128, 128), 4: (64, 128), 8: (32, 128)}
+    ctx = np.random.default_rng(3).integers(512, 16385, size=256)
+    pages = -(-ctx // 16)
+    assert paged.split_plan(int(pages.max()), None, int(pages.sum()) * 2, 148, waves=3,
+                            cap=1024, rows=512, min_pages=128)[0] == 1024
+    assert paged.split_plan(64, None, 8 * 64 * 2, 148, waves=3, cap=1024, rows=16,
+                            min_pages=128)[0] == 16
