@@ -380,7 +380,7 @@ class Workload:
 def run_ours(args, world, rank, local):
     import torch
 
-    from shellsmith_b200 import _build, _capi
+    from shellsmith_b200 import _build, _capi, paged
 
     _build.build()
     device = torch.device("cuda", local)
@@ -392,7 +392,9 @@ def run_ours(args, world, rank, local):
 
     # Launch counter: kernels this build launches per decode step.
     def launches_per_step():
-        return len(cfg.gdn_layers) + len(cfg.attention_layers) * 3  # append, split, combine
+        # one update per GDN layer; append + split-K per attention layer (the merges, which
+        # run only when a sequence spans more than one split, are counted as they launch)
+        return len(cfg.gdn_layers) + len(cfg.attention_layers) * 2
 
     def step(timed_events=None, layer_events=None):
         new = wl.churn()
@@ -440,6 +442,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     events, layer_events = [], []
     launches_before = wl.prefill_launches
+    merges_before = paged.merge_launches
     with ClockSampler(local) as clocks:
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -448,7 +451,8 @@ def run_ours(args, world, rank, local):
         wall = time.perf_counter() - t0
     barrier(world)
     _capi.check_device()
-    timed_launches = launches_per_step() * args.steps + wl.prefill_launches - launches_before
+    timed_launches = (launches_per_step() * args.steps + paged.merge_launches - merges_before
+                      + wl.prefill_launches - launches_before)
 
     decode_ms = [s0.elapsed_time(s1) for s0, s1, *_ in events]
     prefill_ms = [p0.elapsed_time(p1) for _, _, p0, p1, *_ in events]

@@ -125,6 +125,10 @@ def kv_copy_pages(kv_pool: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -
 
 _SM_COUNT: dict = {}
 
+# Merge kernels launched by paged_decode_attention so far: a call launches one only when
+# some sequence spans more than one split. Benchmarks read it to count their launches.
+merge_launches = 0
+
 
 def sm_count(device) -> int:
     index = torch.device(device).index or 0
@@ -249,6 +253,9 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     _capi.call(name, ptr(q), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len),
                ptr(seq_order), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
                ptr(part_out), ptr(part_lse), ptr(out), ptr(lse_out), stream_of(q))
+    if nsplit > 1:
+        global merge_launches
+        merge_launches += 1
     return out
 
 
