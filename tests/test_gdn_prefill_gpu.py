@@ -79,6 +79,35 @@ def test_varlen_packed_sequences_with_slots(cuda):
     assert np.array_equal(state[untouched], rows[untouched])
 
 
+def test_varlen_ranked_two_waves_with_ties_empty_and_skipped(cuda):
+    """40 packed sequences x 4 value heads = 160 CTAs (two waves on 148 SMs), launched
+    longest first with tied lengths ranked by index; empty sequences and a skipped slot
+    (-1) leave their state rows untouched."""
+    rng = np.random.default_rng(8)
+    lengths = list(rng.choice([0, 1, 17, 64, 65, 100], size=40))
+    Hk, Hv, d = 2, 4, 128
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    n = int(cu[-1])
+    q, k, v, g, beta = gdn_sequence_inputs(rng, 1, n, Hk, Hv, d, d)
+    rows = (rng.standard_normal((44, Hv, d, d)) * 0.1).astype(np.float32)
+    slots = [int(x) for x in rng.permutation(44)[:40]]
+    skipped = next(b for b, L in enumerate(lengths) if L > 0)
+    slots[skipped] = -1
+    out, state = _run(q[0], k[0], v[0], g[0], beta[0], None, cu=list(cu), slots=slots,
+                      state_rows=rows)
+    for b, L in enumerate(lengths):
+        if L == 0 or slots[b] < 0:
+            continue
+        a, e = cu[b], cu[b + 1]
+        y, s = ogdn.sequential(q[:, a:e], k[:, a:e], v[:, a:e], g[:, a:e], beta[:, a:e],
+                               rows[slots[b]][None])
+        np.testing.assert_allclose(out[a:e], y[0], rtol=RTOL, atol=ATOL)
+        assert np.abs(state[slots[b]] - s[0]).max() <= STATE_ATOL
+    untouched = [r for r in range(44)
+                 if r not in [sl for b, sl in enumerate(slots) if sl >= 0 and lengths[b] > 0]]
+    assert np.array_equal(state[untouched], rows[untouched])
+
+
 def test_config1_shapes_one_sequence(cuda):
     """Config-1 head shapes (16 key / 32 value heads) on a 1k-token sequence."""
     rng = np.random.default_rng(1)
