@@ -199,14 +199,16 @@ def test_launch_order_changes_nothing_but_the_schedule(cuda):
         _capi.check_device()
 
 
-def test_config2_scale_sample_matches_oracle(cuda):
+@pytest.mark.parametrize("B", [64, 8])
+def test_config2_scale_sample_matches_oracle(cuda, B):
     """Config 2's shapes at full size: 64 sequences with contexts U[1k, 32k] whose pages
-    come from a random permutation of a 150k-page pool (4.9 GB). One append + attention
-    step with the default split plan and longest-first launch order: every appended token
-    reads back bit for bit, and three sequences (shortest, longest, one more) match the
-    oracle."""
+    come from a random permutation of a 150k-page pool (4.9 GB), and the 8 sequences one
+    GPU holds when config 2 is sharded over 8 (there the split floor picks 128-page
+    splits). One append + attention step with the default split plan and longest-first
+    launch order: every appended token reads back bit for bit, and three sequences
+    (shortest, longest, one more) match the oracle."""
     rng = np.random.default_rng(20)
-    B, hq, hkv, D, P, NP = 64, 16, 2, 256, paged.PAGE_SIZE, 150_000
+    hq, hkv, D, P, NP = 16, 2, 256, paged.PAGE_SIZE, 150_000
     lengths = rng.integers(1024, 32 * 1024 + 1, size=B)
     need = -(-(lengths + 1) // P)
     perm = rng.permutation(NP).astype(np.int32)
@@ -228,6 +230,11 @@ def test_config2_scale_sample_matches_oracle(cuda):
     vn = torch.randn((B, hkv, D), device=cuda).to(torch.bfloat16)
     order = torch.from_numpy(np.argsort(-ctx, kind="stable").astype(np.int32)).to(cuda)
     scale = 1.0 / math.sqrt(D)
+    if B == 8:
+        pps, _ = paged.split_plan(int(need.max()), None, int(need.sum()) * hkv,
+                                  paged.sm_count(cuda), waves=3, cap=1024, rows=B * hkv,
+                                  min_pages=128)
+        assert pps == 128
     paged.kv_append(kn, vn, pool, slots)
     out = paged.paged_decode_attention(q, pool, torch.from_numpy(table).to(cuda),
                                        torch.from_numpy(ctx.astype(np.int32)).to(cuda), scale,
