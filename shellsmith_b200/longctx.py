@@ -270,12 +270,13 @@ class ShardedSequence:
         # captured); CTAs past the context return at once. One sequence makes
         # equal CTAs, so the split is sized for one wave on every SM (the batch
         # rule's two waves only add CTA overhead and partials here), rounded up to
-        # a power of two: per layer 59.0 -> 56.7 us at one rank's 8,207 pages
-        # (111 -> 128), 29.6 -> 27.1 us at 1,039 (14 -> 16).
+        # a power of two and at least 32 pages: per layer 59.0 -> 56.7 us at one
+        # rank's 8,207 pages (111 -> 128), 29.6 -> 26.1 us at 1,039 (14 -> 32;
+        # 16 pages: 27.1).
         if self.workspace is None:
             sms = paged.sm_count(q.device)
             one_wave = max(1, -(-self.capacity * self.groups() // sms))
-            self.pages_per_split = 1 << (one_wave - 1).bit_length()
+            self.pages_per_split = max(32, 1 << (one_wave - 1).bit_length())
             _, self.num_splits = paged.split_plan(self.capacity, self.pages_per_split)
             self.workspace = paged.AttentionWorkspace(1, self.q_heads, self.head_dim,
                                                       max(1, self.num_splits), device=q.device)
