@@ -250,6 +250,15 @@ def balanced_share(args, rank: int, world: int) -> np.ndarray:
     return glob[snake_deal(glob, rank, world)]
 
 
+def strong_share(args, rank: int, world: int) -> np.ndarray:
+    """This rank's running sequences when config 3's one batch of `batch` sequences (the
+    draw the 1-GPU run uses) is sharded over `world` GPUs: batch / world per GPU, dealt
+    longest first in snake order (strong scaling: the global batch is fixed)."""
+    glob = np.random.default_rng(SEED).integers(args.min_len, args.max_len + 1,
+                                                size=args.batch)
+    return glob[snake_deal(glob, rank, world)]
+
+
 def snake_deal(lengths: np.ndarray, rank: int, world: int) -> np.ndarray:
     """Indices of `lengths` that rank `rank` holds when they are dealt longest first in
     snake order (seats 0..N-1, then N-1..0, ...): the per-rank sums stay nearly equal."""
@@ -298,6 +307,7 @@ class Workload:
         lengths = self.rng.integers(args.min_len, args.max_len + 1, size=args.batch)
         if world > 1:
             lengths = balanced_share(args, rank, world)
+        self.initial = np.asarray(lengths).copy()
         self.next_id = 0
         for length in lengths:
             self.engine.blocks.admit(self._new_id(), int(length) - 1)
@@ -344,6 +354,17 @@ class Workload:
         self.next_id += 1
         return self.next_id
 
+    def reset(self, lengths) -> None:
+        """Release every running sequence and admit `lengths` afresh (contexts already
+        prefilled; the next decode step appends token `length`), so a timed window
+        starts from the config's stated draw rather than a batch the churn of earlier
+        phases has shortened. Churn draws continue from the same generator."""
+        blocks = self.engine.blocks
+        for slot in np.flatnonzero(blocks.active).tolist():
+            self.engine.release(slot)
+        for length in lengths:
+            blocks.admit(self._new_id(), int(length) - 1)
+
     def churn(self) -> list:
         """Retire Bernoulli(p) finishers and admit replacements; returns new slots."""
         blocks = self.engine.blocks
@@ -375,6 +396,127 @@ class Workload:
                 group.append((slot, prompt))
                 total += prompt
                 self.prefill_tokens += prompt
+
+
+# ------------------------------------------------------------------ parity checks
+# Checks of the measured paths, run on the device after their timed windows (never
+# timed): plain PyTorch float64 restatements of the kernels' math, so every rank of a
+# multi-GPU run checks its own share. The test suite checks the same kernels against
+# the CPU oracle.
+ATTN_RTOL, ATTN_ATOL = 2e-2, 3e-3   # bf16 outputs; the kernel's P.V uses bf16 probabilities
+GDN_RTOL, GDN_ATOL, STATE_ATOL = 2e-2, 2e-3, 1e-4
+
+
+def pool_tokens(pool, pages, length: int):
+    """Logical K, V [length, Hkv, D] of one sequence from a bf16 page pool
+    [num_pages, Hkv, 2, P, D], whose token row t stores its 16-byte chunk c at chunk
+    position c ^ (t & 7) (the layout include/shellcache.h documents)."""
+    import torch
+
+    dev = pool.device
+    P, D = pool.shape[3], pool.shape[4]
+    n = -(-length // P)
+    idx = torch.as_tensor(np.asarray(pages[:n], np.int64), device=dev)
+    blocks = pool.index_select(0, idx)                              # [n, Hkv, 2, P, D]
+    hkv, ch = blocks.shape[1], D // 8
+    swz = torch.arange(ch, device=dev)[None, :] ^ (torch.arange(P, device=dev)[:, None] & 7)
+    x = torch.gather(blocks.view(n, hkv, 2, P, ch, 8), 4,
+                     swz.view(1, 1, 1, P, ch, 1).expand(n, hkv, 2, P, ch, 8))
+    x = x.reshape(n, hkv, 2, P, D).permute(2, 0, 3, 1, 4).reshape(2, n * P, hkv, D)
+    return x[0, :length], x[1, :length]
+
+
+def partial_fp64(q, k, v, scale: float) -> tuple:
+    """Attention of query rows q [R, D] over k, v [L, D] in float64: (normalised out
+    [R, D], natural-log lse [R])."""
+    import torch
+
+    s = (k.double() @ q.double().T) * scale                         # [L, R]
+    m = s.max(dim=0).values
+    p = torch.exp(s - m)
+    total = p.sum(dim=0)
+    return (p.T @ v.double()) / total[:, None], m + torch.log(total)
+
+
+def merge_fp64(parts) -> tuple:
+    """Merge (out [R, D], lse [R]) float64 partials of disjoint key ranges."""
+    import torch
+
+    lse = torch.stack([p[1] for p in parts])
+    top = lse.max(dim=0).values
+    w = torch.exp(lse - top)
+    out = (w[:, :, None] * torch.stack([p[0] for p in parts])).sum(dim=0) / w.sum(dim=0)[:, None]
+    return out, top + torch.log(w.sum(dim=0))
+
+
+def close(got, want, rtol: float, atol: float) -> bool:
+    import torch
+
+    return bool(torch.all((got.double().cpu() - want.double().cpu()).abs()
+                          <= atol + rtol * want.double().cpu().abs()))
+
+
+def attention_row_ok(out, q, k, v, scale: float) -> bool:
+    """out, q [Hq, D] of one sequence against float64 attention over its k, v
+    [L, Hkv, D] (query head h reads kv head h // (Hq / Hkv))."""
+    hq, hkv = q.shape[0], k.shape[1]
+    g = hq // hkv
+    ok = True
+    for j in range(hkv):
+        want, _ = partial_fp64(q[j * g:(j + 1) * g], k[:, j], v[:, j], scale)
+        ok &= close(out[j * g:(j + 1) * g], want, ATTN_RTOL, ATTN_ATOL)
+    return ok
+
+
+def gdn_row_ok(before, after, out, q, k, v, decay, beta) -> bool:
+    """One sequence's GDN token update against float64: state [Hv, dv, dk] before and
+    after, out [Hv, dv]; q, k [Hk, dk], v [Hv, dv], decay, beta [Hv]; key head of
+    value head h is h // (Hv / Hk). Decayed S = a S; pred = S k; S' = S + beta (v -
+    pred) k^T; out = S' q."""
+    import torch
+
+    g = v.shape[0] // q.shape[0]
+    qq = q.double().repeat_interleave(g, 0)
+    kk = k.double().repeat_interleave(g, 0)
+    dec = decay.double()[:, None, None] * before.double()
+    pred = torch.einsum("hvk,hk->hv", dec, kk)
+    want = dec + (beta.double()[:, None] * (v.double() - pred))[:, :, None] * kk[:, None, :]
+    o = torch.einsum("hvk,hk->hv", want, qq)
+    state_ok = float((after.double() - want).abs().max()) <= STATE_ATOL
+    return state_ok and close(out, o, GDN_RTOL, GDN_ATOL)
+
+
+def step_parity(wl) -> tuple:
+    """One more decode step of the workload (untimed) with two of this rank's rows
+    checked, its longest and its shortest sequence: the first GDN layer's state update
+    and output, and the first attention layer's output over the row's whole paged
+    context, its appended token included. Returns (rows failing, rows checked)."""
+    import torch
+
+    eng, cfg = wl.engine, wl.cfg
+    active = np.flatnonzero(eng.blocks.active)
+    lens = eng.blocks.lengths[active]
+    rows = sorted({int(active[np.argmax(lens)]), int(active[np.argmin(lens)])})
+    gl, al = cfg.gdn_layers[0], cfg.attention_layers[0]
+    gi = eng.gdn_index[gl]
+    before = eng.state[gi, rows].clone()
+    eng.begin_step()
+    eng.decode_step(wl.inputs, wl.outputs)
+    torch.cuda.synchronize()
+    bad = 0
+    q, k, v, decay, beta = wl.inputs[gl]
+    for i, r in enumerate(rows):
+        bad += not gdn_row_ok(before[i], eng.state[gi, r], wl.outputs[gl][r], q[r], k[r], v[r],
+                              decay[r], beta[r])
+    pool = eng.kv[eng.attn_index[al]]
+    for r in rows:
+        kk, vv = pool_tokens(pool, eng.blocks.pages[r], int(eng.blocks.lengths[r]))
+        bad += not attention_row_ok(wl.outputs[al][r], wl.inputs[al][0][r], kk, vv, eng.scale)
+    return bad, 2 * len(rows)
+
+
+def parity_word(bad: float, checked: float) -> str:
+    return "ok" if bad == 0 else f"FAILED {int(bad)} of {int(checked)}"
 
 
 def run_ours(args, world, rank, local):
@@ -430,14 +572,16 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     _capi.check_device()
 
-    # The end-to-end phase runs first, on the longer contexts the workload
-    # starts with (churn shortens them over time), so it is never measured
-    # on an easier batch than `value`.
+    # Each measured window starts from config 3's stated draw (contexts U[min, max]):
+    # churn replaces finished sequences with shorter prompts, so a window that ran after
+    # earlier phases would measure a lighter batch.
     e2e = None
     if not args.no_e2e:
+        wl.reset(wl.initial)
         e2e = run_e2e(args, wl, world)
         _capi.check_device()
 
+    wl.reset(wl.initial)
     barrier(world)
     torch.cuda.synchronize()
     events, layer_events = [], []
@@ -466,18 +610,30 @@ def run_ours(args, world, rank, local):
                      for le in layer_events if le[0])
     n_attn_launch = sum(1 for le in layer_events if le[0])
     n_gdn_launch = sum(1 for le in layer_events if not le[0])
+    timed_ctx = np.concatenate([e[5] for e in events]).astype(np.float64)
+    ctx_stats = [float(timed_ctx.sum()), float(timed_ctx.size), float(timed_ctx.min()),
+                 float(timed_ctx.max())]
 
     decode_s_max = max_over_ranks(decode_s, world)
     tokens_all = sum_over_ranks(tokens, world)
     wall_max = max_over_ranks(wall, world)
+    ctx_sum, ctx_n = sum_over_ranks(ctx_stats[0], world), sum_over_ranks(ctx_stats[1], world)
+    ctx_min = -max_over_ranks(-ctx_stats[2], world)
+    ctx_max = max_over_ranks(ctx_stats[3], world)
     peaks = measured_peaks()
     hbm = peaks["hbm_gbs"]
+    bad, checked = step_parity(wl)
+    bad, checked = sum_over_ranks(bad, world), sum_over_ranks(checked, world)
+    _capi.check_device()
 
-    prefill_c1 = front = kv8 = decode_c0 = attention_c2 = long_c4 = None
+    strong = attention_c2 = long_c4 = None
+    prefill_c1 = front = kv8 = decode_c0 = None
     if not args.no_config1:
-        # The sharded configs, on every rank (each one's own collectives, in the
+        # Config 3 as stated (256 sequences in all, sharded over the GPUs), then the
+        # other sharded configs, on every rank (each with its own collectives, in the
         # same order everywhere): config 2 by sequence, config 4 by KV page.
         barrier(world)
+        strong = config3_strong(args, wl, world, rank, step)
         attention_c2 = config2_attention(device, rank=rank, world=world)
         long_c4 = config4_measure(args, world, rank, local, steps=200, warmup=5,
                                   exchange=args.exchange)
@@ -516,11 +672,15 @@ def run_ours(args, world, rank, local):
                         f"{args.batch} ragged sequences per GPU, ctx U[{args.min_len},"
                         f"{args.max_len}], churn {args.churn}/step",
             "global_batch": args.batch * world, "seq_len": f"U[{args.min_len},{args.max_len}]",
+            "mean_ctx_timed": round(ctx_sum / ctx_n, 1),
+            "ctx_timed_range": [int(ctx_min), int(ctx_max)],
+            "timed_from": "the stated draw (batch re-admitted at U[min, max] before the window)",
             "parallelism": f"sequence-sharded x{world}, no collective",
             "gdn": "Hk16/Hv32 dk=dv=128 fp32 state", "attention": "Hq16/Hkv2 D256 page16",
             "pages_per_split": args.pages_per_split or "adaptive (<= 1024, >= 3 waves of CTAs)",
             "l2": "working set ~90 GB/step > L2 (no flush needed)",
         },
+        "parity": parity_word(bad, checked),
         "hbm": {"step_gbs": round(step_gbs, 1), "peak_gbs": hbm,
                 "frac": round(step_gbs / hbm, 4), "peak_source": peaks["source"],
                 "bytes_per_step": round(bytes_total / max(1, len(events))),
@@ -545,9 +705,6 @@ def run_ours(args, world, rank, local):
     }
     if e2e is not None:
         line["e2e"] = e2e
-    if attention_c2 is not None:
-        line["config2_attention"] = attention_c2
-        line["config4_long_sequence"] = long_c4
     if prefill_c1 is not None:
         line["config1_prefill"] = prefill_c1
         line["config0_decode"] = decode_c0
@@ -557,8 +714,66 @@ def run_ours(args, world, rank, local):
         line["kv8_attention"] = kv8
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if strong is not None:
+        # The sharded configs last and compact, so the tail of the line carries them.
+        line["sharded_workloads"] = SHARDED_WORKLOADS
+        line["config3_strong"] = strong
+        line["config2_attention"] = attention_c2
+        line["config4_long_sequence"] = long_c4
     print(json.dumps(line), flush=True)
     return line
+
+
+SHARDED_WORKLOADS = (
+    "config3_strong: config 3's 256 sequences in all (the 1-GPU draw) dealt longest first in "
+    "snake order, 256/N per GPU, same step and churn; config2_attention: 64 sequences "
+    "U[1k,32k], append + split-K attention, dealt the same way; config4_long_sequence: one "
+    "131,072-token sequence, its KV pages split over the N GPUs, partials exchanged over "
+    "NVLink. tokens_per_s = all GPUs; hbm_frac_per_gpu of measured; parity: rows checked "
+    "against float64 on every rank (config 4: the peer exchange also equals an NCCL "
+    "all-gather bit for bit)")
+
+
+def config3_strong(args, wl, world, rank, step, warmup: int = 2) -> dict | None:
+    """Config 3 as stated: one batch of `batch` sequences (the 1-GPU draw) sharded by
+    sequence over the ranks, batch / world per GPU (strong scaling), timed like the
+    headline window from the stated draw. Every rank calls it; returns the record on
+    rank 0."""
+    import torch
+
+    from shellsmith_b200 import _capi
+
+    eng = wl.engine
+    wl.reset(strong_share(args, rank, world))
+    for _ in range(warmup):
+        step()
+    wl.reset(strong_share(args, rank, world))
+    torch.cuda.synchronize()
+    barrier(world)
+    events = []
+    for _ in range(args.steps):
+        step(events)
+    torch.cuda.synchronize()
+    _capi.check_device()
+    decode_s = sum(e[0].elapsed_time(e[1]) for e in events) / 1e3
+    tokens = sum(e[4] for e in events)
+    nbytes = sum(eng.step_bytes(e[5])["total"] for e in events)
+    ctx = np.concatenate([e[5] for e in events]).astype(np.float64)
+    seqs = len(events[0][5])
+    decode_max = max_over_ranks(decode_s, world)
+    tokens_all = sum_over_ranks(tokens, world)
+    gbs_per_gpu = sum_over_ranks(nbytes, world) / world / decode_max / 1e9
+    ctx_sum, ctx_n = sum_over_ranks(float(ctx.sum()), world), sum_over_ranks(ctx.size, world)
+    bad, checked = step_parity(wl)
+    bad, checked = sum_over_ranks(bad, world), sum_over_ranks(checked, world)
+    _capi.check_device()
+    if rank != 0:
+        return None
+    return {"n_gpus": world, "seqs_per_gpu": seqs, "steps": args.steps,
+            "ms_per_step": round(decode_max * 1e3 / args.steps, 3),
+            "tokens_per_s": round(tokens_all / decode_max, 1),
+            "hbm_frac_per_gpu": round(gbs_per_gpu / measured_peaks()["hbm_gbs"], 4),
+            "mean_ctx": round(ctx_sum / ctx_n), "parity": parity_word(bad, checked)}
 
 
 def gdn_front_layer(device, batch: int = 256, rounds: int = 5) -> dict:
@@ -912,16 +1127,20 @@ def config2_attention(device, steps: int = 20, warmup: int = 3, rank: int = 0,
     nbytes = sum_over_ranks(float(nbytes), world)
     gbs = nbytes / world / (ms / 1e3) / 1e9   # per GPU
     peak = measured_peaks()["hbm_gbs"]
+    # Parity of the last step on this rank's longest and shortest sequence.
+    bad = 0
+    for b in sorted({int(np.argmax(lengths)), int(np.argmin(lengths))}):
+        L = int(ctx[-1, b])
+        kk, vv = pool_tokens(pool, table[b], L)
+        bad += not attention_row_ok(out[b], q[b], kk, vv, 1 / 16)
+    bad = sum_over_ranks(bad, world)
+    checked = sum_over_ranks(min(2, B), world)
     del pool
     if rank != 0:
         return None
-    return {"workload": "config2 paged append + split-K decode attention, 64 seqs ctx U[1k,32k], "
-                        "16/2 heads D256, 150k-page pool (random permutation)",
-            "n_gpus": world, "scaling": "strong",
-            "parallelism": f"sequence-sharded x{world} (snake deal by length), no collective",
-            "ms_per_step": round(ms, 4), "tokens_per_s": round(B_all / (ms / 1e3), 1),
-            "bytes_per_step": int(nbytes), "gbs": round(gbs, 1),
-            "hbm_frac": round(gbs / peak, 4), "launches_per_step": 3}
+    return {"n_gpus": world, "seqs_per_gpu": B, "ms_per_step": round(ms, 4),
+            "tokens_per_s": round(B_all / (ms / 1e3), 1), "hbm_frac_per_gpu": round(gbs / peak, 4),
+            "parity": parity_word(bad, checked)}
 
 
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:
@@ -1163,7 +1382,9 @@ def config4_measure(args, world, rank, local, steps: int, warmup: int,
     torch.cuda.synchronize()
     local_ms = e0.elapsed_time(e1)
     ms = max_over_ranks(local_ms, world)
-    # The exchange alone: one layer's packed partial to every rank.
+    parity = config4_parity(shard, attn_in[0], world, rank)
+    # The exchange alone: one layer's packed partial to every rank. It runs last: its
+    # epochs lie above every layer epoch this run still had to use.
     ag_ms = None
     if use_p2p:
         for i in range(5):
@@ -1199,27 +1420,74 @@ def config4_measure(args, world, rank, local, steps: int, warmup: int,
         return None
     peaks = measured_peaks()
     per_step = ms / 1e3 / steps
+    # Compact: this record closes the bench line. exchange_us is one layer's partial to
+    # every rank timed alone (the put/wait kernel pair for p2p and fused, the all-gather
+    # for nccl); the step is one CUDA graph replay.
     return {
-        "workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN replicated "
-                    f"+ 12 attention with KV pages split over {world} GPU)",
-        "n_gpus": world, "scaling": "strong", "steps": steps, "warmup": warmup,
+        "n_gpus": world, "steps": steps,
         "ms_per_step": round(per_step * 1e3, 4), "tokens_per_s": round(1 / per_step, 1),
-        "parallelism": f"KV-page sharding x{world}, "
-                       + {"fused": "attention merge stores (out, lse) into the peers over "
-                                   "NVLink, epoch flags",
-                          "p2p": "put/wait kernels store (out, lse) into the peers over "
-                                 "NVLink, epoch flags",
-                          "nccl": "NCCL all-gather of (out, lse)"}[exchange],
-        "hbm": {"bytes_per_step_all_ranks": bytes_all,
-                "gbs_per_gpu": round(bytes_all / world / per_step / 1e9, 1),
-                "frac_per_gpu": round(bytes_all / world / per_step / 1e9 / peaks["hbm_gbs"], 4)},
-        # One layer's partial to every rank, timed alone: the put/wait kernel pair
-        # (fused and p2p) or the all-gather (nccl).
-        "exchange_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
+        "hbm_frac_per_gpu": round(bytes_all / world / per_step / 1e9 / peaks["hbm_gbs"], 4),
         "exchange": exchange if world > 1 else None,
-        "all_gather_bytes_per_rank": hq * (d + 1) * 4,
-        "launch": "one CUDA graph per step",
+        "exchange_us": None if ag_ms is None else round(ag_ms * 1e3, 2),
+        "parity": parity,
     }
+
+
+def config4_parity(shard, attn_in, world: int, rank: int) -> str:
+    """One more token through attention layer 0 on the measured path (untimed). At
+    N > 1 the same per-rank partials through an NCCL all-gather and the packed merge
+    must give the same bits; on every N, query heads 0, 9 and 15 must match float64
+    attention over the whole context (each rank's float64 partial over its own pages,
+    merged on rank 0). Every rank calls it (its collectives run on all ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from shellsmith_b200 import _capi, paged
+
+    q, k, v = attn_in
+    shard.begin_token()
+    got = shard.attention(0, q, k, v, 1 / 16).clone()
+    identical = True
+    if world > 1:
+        paged.paged_decode_attention_packed(q, shard.kv[0], shard.table, shard.ctx, 1 / 16,
+                                            packed=shard.packed,
+                                            max_pages_in_batch=shard.capacity,
+                                            pages_per_split=shard.pages_per_split,
+                                            total_pages=shard.capacity,
+                                            workspace=shard.workspace)
+        dist.all_gather_into_tensor(shard.gathered, shard.packed)
+        ref, _ = paged.attention_combine_packed(shard.gathered)
+        torch.cuda.synchronize()
+        identical = torch.equal(ref, got)
+    torch.cuda.synchronize()
+    _capi.check_device()
+    heads = (0, 9, 15)
+    group = shard.q_heads // shard.kv.shape[2]
+    mine = [(torch.zeros((1, shard.head_dim), dtype=torch.float64),
+             torch.full((1,), -math.inf, dtype=torch.float64))] * len(heads)
+    if shard.local_tokens:
+        kk, vv = pool_tokens(shard.kv[0], list(range(shard.capacity)), shard.local_tokens)
+        mine = []
+        for h in heads:
+            o, l = partial_fp64(q[0, h:h + 1], kk[:, h // group], vv[:, h // group], 1 / 16)
+            mine.append((o.cpu(), l.cpu()))
+        del kk, vv
+    parts = [mine]
+    if world > 1:
+        parts = [None] * world
+        dist.all_gather_object(parts, mine)
+        identical = bool(sum_over_ranks(float(not identical), world) == 0)
+    if rank != 0:
+        return ""
+    ok = True
+    for i, h in enumerate(heads):
+        want, _ = merge_fp64([p[i] for p in parts])
+        ok &= close(got[h:h + 1], want, ATTN_RTOL, ATTN_ATOL)
+    if ok and identical:
+        return "ok" + (" (exchange == nccl bit for bit)" if world > 1 else "")
+    fails = ([] if ok else ["FAILED vs float64 (heads 0, 9, 15)"]) + (
+        [] if identical else ["FAILED exchange != nccl"])
+    return "; ".join(fails)
 
 
 def run_config4(args, world, rank, local):
@@ -1233,9 +1501,13 @@ def run_config4(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": c4["ms_per_step"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 kv / fp32 gdn state", "data": "synthetic",
-        "config": {"workload": c4["workload"], "parallelism": c4["parallelism"]},
-        "hbm": c4["hbm"], "exchange_us": c4["exchange_us"], "exchange": c4["exchange"],
-        "all_gather_bytes_per_rank": c4["all_gather_bytes_per_rank"],
+        "config": {"workload": f"config4: one sequence of {args.ctx4} tokens, 48 layers (36 GDN "
+                               f"replicated + 12 attention with KV pages split over {world} "
+                               f"GPU)",
+                   "parallelism": f"KV-page sharding x{world}, exchange {c4['exchange']}",
+                   "all_gather_bytes_per_rank": 16 * 257 * 4},
+        "hbm_frac_per_gpu": c4["hbm_frac_per_gpu"], "exchange_us": c4["exchange_us"],
+        "parity": c4["parity"],
     }
     print(json.dumps(line), flush=True)
     return line

@@ -165,7 +165,10 @@ int sc_gdn_decode_fused(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
  * (launched as a programmatic dependent of the front, so its state loads
  * overlap it) and the gated norm. Same arguments, plus a device workspace of
  * at least sc_gdn_decode_glue_workspace(B, Hk, Hv) bytes, 256-byte aligned,
- * that holds q/k/v/g/beta and the pre-norm output between the kernels.
+ * that holds q/k/v/g/beta and the pre-norm output between the kernels. After
+ * the call it holds, each part starting on a 256-byte boundary in this order:
+ * q, k [B, Hk, 128] bf16, v [B, Hv, 128] bf16, y [B, Hv, 128] bf16 (the
+ * recurrence output before the gated norm), g, beta [B, Hv] fp32.
  * Slots must be distinct across rows (state_slot NULL: row b uses slot b). */
 size_t sc_gdn_decode_glue_workspace(int B, int Hk, int Hv);
 int sc_gdn_decode_glue(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
@@ -199,6 +202,22 @@ int sc_gdn_prefill_front(const sc_bf16* qkv, const sc_bf16* a, const sc_bf16* b,
 int sc_gdn_taps_store(const sc_bf16* qkv, sc_bf16* taps, const int32_t* cu_seqlens,
                       const int32_t* seq_slot, const int32_t* seq_start, int nseq,
                       int channels, int num_slots, void* stream);
+
+/* Gates of the fused chunk path from their logits, for gated_delta_chunks.
+ *
+ * Replaces the gate math that the reference's fused chunk kernel makes per row
+ * (numerics/metal/gdn_chunk_common.metal:61-75 `sampler_gate`, `sampler_beta`,
+ * behind numerics/gdn_fused.py:86-122 `gated_delta_chunks`): with each step in
+ * fp32 and rounded to bf16,
+ *   g    = bf16(exp(bf16(-bf16(exp(bf16(A_log))) * sp))),
+ *   sp   = bf16(max(x, 0) + log(1 + exp(-|x|))),  x = bf16(a + bf16(dt_bias)),
+ *   beta = bf16(1 / (1 + exp(-b))).
+ * a, b [rows, Hv] bf16 logits (-inf marks a padded row: g = 1, beta = 0);
+ * A_log, dt_bias [Hv] fp32; g, beta [rows, Hv] fp32 out. g is not clamped:
+ * sc_gdn_chunk_prefill clamps it at 1e-6 before its log, as the reference does. */
+int sc_gdn_sampler_gates(const sc_bf16* a, const sc_bf16* b, const float* A_log,
+                         const float* dt_bias, float* g, float* beta, int64_t rows, int Hv,
+                         void* stream);
 
 /* out = rms_norm(y, w, eps) * silu(z) over rows of `width` (a multiple of 128):
  * bf16.py:129-135 for any number of rows (the prefill output). y, z, out
@@ -395,8 +414,12 @@ int sc_attention_combine_exchange(const float* gathered, const unsigned int* fla
  * loads the library holds until the process exits. A call needs
  * B * Hq * num_splits * (D + 1) floats when num_splits > 1 and returns
  * SC_ERR_INVALID (nothing launched) when that exceeds the array.
- * The first call on a device looks up the array's device address (a one-time
- * set-up per device); make that first call before any stream capture.
+ * The first call on a device that needs the array (num_splits > 1) looks up
+ * its device address (a one-time set-up per device) and caches it for the
+ * life of the process; make that first call before any stream capture. The
+ * cached address belongs to the device's primary context: after
+ * cudaDeviceReset (or anything else that destroys that context) this entry
+ * point must not be called again in the same process.
  * All calls share the one array and it keeps the last call's contents;
  * nothing in it needs to start at zero, because every partial a call reads
  * is written earlier in the same call. Calls that overlap on the GPU (other

@@ -77,6 +77,73 @@ def gates_bf16(a, b, a_log, dt_bias):
     return g, beta
 
 
+LOG_GATE_MIN = np.float32(np.log(1e-6))    # the chunk path clamps a gate at 1e-6
+
+
+def _f32(x):
+    """A float64 result rounded to float32: one correctly rounded fp32 operation."""
+    return np.asarray(x, np.float64).astype(np.float32)
+
+
+def _near_bf16_tie(x64, margin=2.0 ** -19):
+    """True where a value about to be rounded to bf16 lies within `margin` (relative,
+    16 fp32 ulps) of a bf16 rounding boundary: a device exp or log that is a few fp32
+    ulps from the correctly rounded result may round to the other bf16 there."""
+    x = np.abs(np.asarray(x64, np.float64))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        e = np.floor(np.log2(np.where(x > 0, x, 1.0)))
+        frac = x / 2.0 ** e * 128.0                # 7 stored mantissa bits of bf16
+        dist = np.abs(frac - np.floor(frac) - 0.5) / 128.0
+    return np.isfinite(x) & (x > 0) & (dist < margin)
+
+
+def sampler_gates(a, b, a_log, dt_bias):
+    """The gates of the fused chunk path from their logits: `sampler_gate` and
+    `sampler_beta` of src/studio_compute/numerics/metal/gdn_chunk_common.metal:61-75,
+    called per chunk row by `load_gates` (:79-96) for gdn_fused.py:86-122
+    `gated_delta_chunks`. Every step is fp32 and rounded to bf16 as MLX does:
+
+        scale = bf16(exp(bf16(a_log)))
+        x     = bf16(a + bf16(dt_bias))
+        sp    = bf16(max(x, 0) + log(1 + exp(-|x|)))
+        gate  = bf16(exp(bf16(-scale * sp)))
+        log_gate = log(1e-6) if gate < 1e-6 else log(gate)      (fp32)
+        beta  = bf16(1 / (1 + exp(-b)))
+
+    a, b [..., H] (bf16 values, +-inf allowed: a padded row has a = b = -inf, which
+    gives gate 1 and beta 0); a_log, dt_bias [H] fp32. Returns float32 arrays
+    (gate, log_gate, beta) and `tie` [..., H] bool: elements where one of the steps
+    rounds a value within 16 fp32 ulps of a bf16 rounding boundary, so a device exp or
+    log a few ulps from the correctly rounded result may give the neighbouring bf16
+    (every other element is determined bit for bit). exp and log here are correctly
+    rounded fp32 operations (float64 math, one rounding)."""
+    a = bf(np.asarray(a, np.float32))
+    b = bf(np.asarray(b, np.float32))
+    a_log = np.asarray(a_log, np.float32)
+    dt_bias = np.asarray(dt_bias, np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        e_scale = np.exp(bf(a_log).astype(np.float64))
+        scale = bf(_f32(e_scale))
+        x = bf(_f32(a.astype(np.float64) + bf(dt_bias).astype(np.float64)))
+        e = _f32(np.exp(-np.abs(x.astype(np.float64))))
+        t = _f32(1.0 + e.astype(np.float64))
+        lg = _f32(np.log(t.astype(np.float64)))
+        sp64 = np.maximum(x, np.float32(0)).astype(np.float64) + lg.astype(np.float64)
+        sp = bf(_f32(sp64))
+        arg = bf(_f32(-scale.astype(np.float64) * sp.astype(np.float64)))
+        g64 = np.exp(arg.astype(np.float64))
+        gate = bf(_f32(g64))
+        clamped = gate < np.float32(1e-6)
+        log_gate = np.where(clamped, LOG_GATE_MIN,
+                            _f32(np.log(np.where(clamped, 1.0, gate).astype(np.float64))))
+        eb = _f32(np.exp(-b.astype(np.float64)))
+        beta64 = 1.0 / _f32(1.0 + eb.astype(np.float64)).astype(np.float64)
+        beta = bf(_f32(beta64))
+    tie = (_near_bf16_tie(e_scale) | _near_bf16_tie(sp64) | _near_bf16_tie(g64)
+           | _near_bf16_tie(beta64))
+    return gate, log_gate.astype(np.float32), beta, np.broadcast_to(tie, gate.shape)
+
+
 def split_heads(x, Hk, Hv, dk=128, dv=128):
     """Channels q | k | v -> q, k [..., Hk, dk], v [..., Hv, dv]."""
     q = x[..., :Hk * dk].reshape(*x.shape[:-1], Hk, dk)

@@ -35,6 +35,7 @@ SIGNATURES = {
     "sc_gdn_prefill_front": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,
                              _I, _I, _I, _P],
     "sc_gdn_taps_store": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "sc_gdn_sampler_gates": [_P, _P, _P, _P, _P, _P, _I64, _I, _P],
     "sc_gated_rmsnorm": [_P, _P, _P, _F, _P, _I64, _I, _P],
     "sc_exchange_put": [_P, ctypes.c_longlong, _P, _P, _P, ctypes.c_uint, _I, _P],
     "sc_exchange_wait": [_P, _I, _P, ctypes.c_uint, _P],

@@ -38,6 +38,22 @@ __device__ __forceinline__ void flag_device(unsigned int* status, unsigned int b
   if (status != nullptr) atomicOr(status, bits);
 }
 
+// Context length a split-K decode may attend for a sequence whose ctx_len entry
+// is L: a negative length, or one whose pages exceed the block-table row
+// (max_pages) or what the launch's splits cover (num_splits x pages_per_split),
+// is flagged DEV_BAD_INDEX (by the CTA with `report` set) and clamped, so no
+// read goes past the sequence's row of the block table and no page is dropped
+// silently.
+__device__ __forceinline__ int checked_ctx_len(int L, int page, int max_pages,
+                                               int pages_per_split, int num_splits,
+                                               unsigned int* status, bool report) {
+  const long long cap_pages = min((long long)max_pages, (long long)num_splits * pages_per_split);
+  const long long cap = cap_pages * page;
+  if (L >= 0 && (long long)L <= cap) return L;
+  if (report) flag_device(status, DEV_BAD_INDEX);
+  return L < 0 ? 0 : (int)cap;
+}
+
 // ---------------------------------------------------------------- dependent launch
 // Kernels of one decode step are launched as programmatic dependents of the
 // kernel before them (launch_pdl): the next grid is scheduled while the

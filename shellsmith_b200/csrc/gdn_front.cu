@@ -29,6 +29,8 @@
 // feed sc_gdn_chunk_prefill; K10 gdn_taps_store writes each prompt's last
 // three inputs into its ring afterwards; K11 gated_rmsnorm is the output norm
 // for any number of rows.
+#include <algorithm>
+
 #include "common.cuh"
 #include "gdn_internal.cuh"
 
@@ -75,6 +77,38 @@ __device__ __forceinline__ void make_gates(float a, float b, float a_log, float 
   const float rate = bfr(expf(bfr(a_log)));
   g = bfr(expf(bfr(-rate * sp)));
   beta = bfr(sigmoid_f(bfr(b)));
+}
+
+// Gates of the fused chunk path from their logits: the reference's sampler_gate
+// and sampler_beta (numerics/metal/gdn_chunk_common.metal:61-75), which the
+// chunk kernel behind gdn_fused.py:86-122 `gated_delta_chunks` makes per row.
+// fp32 math rounded to bf16 after each step; softplus as max(x, 0) +
+// log(1 + exp(-|x|)). The gate is returned as its bf16 value (not clamped: the
+// chunk kernel clamps it at 1e-6 before its log, as the reference does).
+__device__ __forceinline__ void sampler_gates(float a, float b, float a_log, float dt_bias,
+                                              float& g, float& beta) {
+  const float scale = bfr(expf(bfr(a_log)));
+  const float x = bfr(a + bfr(dt_bias));
+  const float sp = bfr(fmaxf(x, 0.f) + logf(1.f + expf(-fabsf(x))));
+  g = bfr(expf(bfr(-scale * sp)));
+  beta = bfr(1.f / (1.f + expf(-b)));
+}
+
+// One thread per (token, value head); a and b are [rows][Hv] bf16.
+__global__ void __launch_bounds__(256)
+    sampler_gates_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
+                         const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                         float* __restrict__ g, float* __restrict__ beta, long long n, int Hv) {
+  pdl_wait();
+  pdl_trigger();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int h = (int)(i % Hv);
+    float gi, bi;
+    sampler_gates(bf16_to_f(a[i]), bf16_to_f(b[i]), a_log[h], dt_bias[h], gi, bi);
+    g[i] = gi;
+    beta[i] = bi;
+  }
 }
 
 __device__ __forceinline__ void cluster_arrive() {
@@ -637,6 +671,23 @@ extern "C" int sc_gdn_taps_store(const sc_bf16* qkv, sc_bf16* taps, const int32_
   dim3 grid(nseq, (channels + 255) / 256);
   gdn_taps_store_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       qkv, taps, cu_seqlens, seq_slot, seq_start, channels, num_slots, device_status_word());
+  return check_launch(name);
+}
+
+extern "C" int sc_gdn_sampler_gates(const sc_bf16* a, const sc_bf16* b, const float* a_log,
+                                    const float* dt_bias, float* g, float* beta, int64_t rows,
+                                    int Hv, void* stream) {
+  using namespace sc;
+  const char* name = "sc_gdn_sampler_gates";
+  SC_REQUIRE(a && b && a_log && dt_bias && g && beta, SC_ERR_INVALID, "%s: null pointer", name);
+  SC_REQUIRE(rows >= 0 && Hv > 0 && rows <= (int64_t)1 << 40, SC_ERR_INVALID,
+             "%s: rows=%lld Hv=%d", name, (long long)rows, Hv);
+  const long long n = (long long)rows * Hv;
+  if (n == 0) return SC_OK;
+  const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+  launch_pdl(sampler_gates_kernel, dim3((unsigned)blocks), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), reinterpret_cast<const uint16_t*>(a),
+             reinterpret_cast<const uint16_t*>(b), a_log, dt_bias, g, beta, n, Hv);
   return check_launch(name);
 }
 

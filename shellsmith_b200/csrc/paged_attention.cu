@@ -72,7 +72,8 @@ __global__ void __launch_bounds__(NW * 32)
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
     return;
   }
-  const int L = ctx_len[b];
+  const int L = checked_ctx_len(ctx_len[b], kPage, max_pages, pages_per_split, num_splits,
+                                status, split == 0 && blockIdx.y == 0 && threadIdx.x == 0);
   const int npages = (L + kPage - 1) / kPage;
   const int p_begin = split * pages_per_split;
   if (npages == 0 && split == 0) {  // nothing to attend: zero output, lse = -inf
@@ -821,10 +822,14 @@ extern "C" int sc_paged_decode_attention_noalloc(const sc_bf16* q, const sc_bf16
              "(32 MiB); use fewer splits (larger pages_per_split) or sc_paged_decode_attention "
              "with caller scratch",
              name, need, SC_NOALLOC_SCRATCH_FLOATS);
-  float* scratch = sc::noalloc_scratch(name);
-  if (scratch == nullptr) return SC_ERR_CUDA;
-  float* part_out = num_splits > 1 ? scratch : nullptr;
-  float* part_lse = num_splits > 1 ? scratch + rows * D : nullptr;
+  float* part_out = nullptr;
+  float* part_lse = nullptr;
+  if (num_splits > 1) {  // one split writes the output directly and needs no scratch
+    float* scratch = sc::noalloc_scratch(name);
+    if (scratch == nullptr) return SC_ERR_CUDA;
+    part_out = scratch;
+    part_lse = scratch + rows * D;
+  }
   return sc_paged_decode_attention(q, kv_pool, num_pages, block_table, ctx_len, nullptr, B, Hq,
                                    Hkv, D, P,
                                    max_pages, pages_per_split, num_splits, scale, part_out,

@@ -239,7 +239,8 @@ __global__ void __launch_bounds__(NW * 32)
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) flag_device(status, DEV_BAD_INDEX);
     return;
   }
-  const int L = ctx_len[b];
+  const int L = checked_ctx_len(ctx_len[b], kPage, max_pages, pages_per_split, num_splits,
+                                status, split == 0 && blockIdx.y == 0 && threadIdx.x == 0);
   const int npages = (L + kPage - 1) / kPage;
   const int p_begin = split * pages_per_split;
   if (npages == 0 && split == 0) {  // nothing to attend: zero output, lse = -inf

@@ -49,6 +49,7 @@ class HybridConfig:
     gdn_taps: bool = False               # keep conv tap rings (layers run with their glue)
     gdn_glue_fused: bool = False         # one-launch cluster kernel instead of the 3-kernel step
     kv_precision: str = "bf16"           # "8bit": quantised pages (paged.new_pool_q8)
+    sms: int | None = None               # SM count the split size is planned for (None: device's)
 
     def is_attention(self, layer: int) -> bool:
         return layer % self.attention_every == self.attention_every - 1
@@ -367,7 +368,7 @@ class HybridCacheEngine:
                                      pages_per_split=self.cfg.pages_per_split,
                                      total_pages=self.total_pages,
                                      workspace=self.workspace, out=out,
-                                     seq_order=self.seq_order)
+                                     seq_order=self.seq_order, sms=self.cfg.sms)
 
     def decode_step(self, inputs: dict, outputs: dict) -> None:
         """Run every layer's cache work for the staged token of each active row.

@@ -150,6 +150,27 @@ class SplitWorkspace:
                                                                     weights.value_heads))
         self.buffer = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
 
+    def views(self, B: int, Hk: int, Hv: int) -> tuple:
+        """The intermediates of the last call over B rows, in the layout
+        sc_gdn_decode_glue documents: q, k [B, Hk, 128], v and the recurrence output
+        y [B, Hv, 128] bf16, g and beta [B, Hv] fp32 (for checking each stage)."""
+        def up(n):
+            return (n + 255) // 256 * 256
+
+        qk, vy, gb = up(B * Hk * HEAD * 2), up(B * Hv * HEAD * 2), up(B * Hv * 4)
+        buf = self.buffer
+
+        def part(off, n, dtype, shape):
+            size = n * torch.empty((), dtype=dtype).element_size()
+            return buf[off:off + size].view(dtype).view(shape)
+
+        return (part(0, B * Hk * HEAD, torch.bfloat16, (B, Hk, HEAD)),
+                part(qk, B * Hk * HEAD, torch.bfloat16, (B, Hk, HEAD)),
+                part(2 * qk, B * Hv * HEAD, torch.bfloat16, (B, Hv, HEAD)),
+                part(2 * qk + vy, B * Hv * HEAD, torch.bfloat16, (B, Hv, HEAD)),
+                part(2 * qk + 2 * vy, B * Hv, torch.float32, (B, Hv)),
+                part(2 * qk + 2 * vy + gb, B * Hv, torch.float32, (B, Hv)))
+
 
 def gdn_decode_split(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                      weights: GDNWeights, taps: torch.Tensor, position: torch.Tensor,

@@ -170,3 +170,78 @@ def gated_delta_chunked(q, k, v, g, beta, state, chunk=64, *, compute_dtype=None
         g.float().reshape(B * T, Hv).contiguous(), beta.float().reshape(B * T, Hv).contiguous(),
         s, T=T)
     return y.reshape(B, T, Hv, dv).to(v.dtype), s
+
+
+def gdn_sampler_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor,
+                      dt_bias: torch.Tensor) -> tuple:
+    """Gates of the fused chunk path from their logits (sc_gdn_sampler_gates).
+
+    a, b [..., Hv] bf16 (gate and beta logits; -inf marks a padded row: gate 1,
+    beta 0); a_log, dt_bias [Hv] fp32. Returns (g, beta) fp32 of a's shape: g is
+    the bf16 gate value exp(-exp(A_log) softplus(a + dt_bias)) and beta =
+    sigmoid(b), each step rounded to bf16 as the reference's sampler_gate /
+    sampler_beta round them (numerics/metal/gdn_chunk_common.metal:61-75).
+    """
+    Hv = a.shape[-1]
+    require_cuda("a", a, torch.bfloat16, None, align=2)
+    require_cuda("b", b, torch.bfloat16, None, align=2)
+    for name, t in (("a_log", a_log), ("dt_bias", dt_bias)):
+        require_cuda(name, t, torch.float32, 1, align=4)
+        if t.shape[0] != Hv:
+            raise ValueError(f"gdn_sampler_gates: {name} must be [{Hv}]")
+    if b.shape != a.shape:
+        raise ValueError("gdn_sampler_gates: a and b must have the same shape")
+    g = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+    beta = torch.empty_like(g)
+    _capi.call("sc_gdn_sampler_gates", ptr(a), ptr(b), ptr(a_log), ptr(dt_bias), ptr(g),
+               ptr(beta), a.numel() // max(1, Hv), Hv, stream_of(a))
+    return g, beta
+
+
+HEAD_WIDTH = 128
+
+
+def gated_delta_chunks(q_BLGD: torch.Tensor, k_BLGD: torch.Tensor, v_BLHD: torch.Tensor,
+                       a_BLH: torch.Tensor, b_BLH: torch.Tensor, a_log_H: torch.Tensor,
+                       dt_bias_H: torch.Tensor, state_BHDD: torch.Tensor) -> tuple:
+    """The chunked gated delta rule of one GDN layer from its gate and beta logits.
+
+    Same contract as the reference (numerics/gdn_fused.py:86-122): normalized q, k
+    [B, L, G, 128] for G key heads, v [B, L, H, 128], gate logits a and beta logits b
+    [B, L, H], all bf16; the per-head A_log and dt_bias [H]; the state [B, H, 128,
+    128]. Returns (y [B, L, H, 128] bf16, final state) for g = exp(-exp(A_log)
+    softplus(a + dt_bias)) and beta = sigmoid(b), made with the reference's bf16
+    rounding points (gdn_sampler_gates). Violations raise AssertionError as there.
+
+    The reference pads L to a multiple of 64 with rows of g = 1 and beta = 0; the
+    tensor-core kernel stops at the sequence's last row instead, which leaves the
+    state and the real rows' outputs the same. The state may be bf16 (the
+    reference's dtype: the update runs on an fp32 copy, rounded back once at the
+    end) or fp32 (this build's pools: advanced in place). a_log and dt_bias may
+    be fp32 or bf16 (the gates round them to bf16 first either way).
+    """
+    batch, length, key_heads, width = q_BLGD.shape
+    heads = v_BLHD.shape[2]
+    assert width == HEAD_WIDTH == v_BLHD.shape[3] and heads % key_heads == 0
+    assert k_BLGD.shape == q_BLGD.shape and a_BLH.shape == b_BLH.shape
+    assert v_BLHD.shape[:2] == (batch, length) and a_BLH.shape == (batch, length, heads)
+    assert all(value.dtype == torch.bfloat16
+               for value in (q_BLGD, k_BLGD, v_BLHD, a_BLH, b_BLH))
+    assert state_BHDD.dtype in (torch.bfloat16, torch.float32)
+    assert state_BHDD.shape == (batch, heads, HEAD_WIDTH, HEAD_WIDTH)
+    assert a_log_H.shape == dt_bias_H.shape == (heads,)
+    a_log = a_log_H.float().contiguous()
+    dt_bias = dt_bias_H.float().contiguous()
+    g, beta = gdn_sampler_gates(a_BLH.contiguous(), b_BLH.contiguous(), a_log, dt_bias)
+    in_place = state_BHDD.dtype == torch.float32 and state_BHDD.is_contiguous()
+    state = state_BHDD if in_place else state_BHDD.float().contiguous()
+    tokens = batch * length
+    y = gdn_chunk_prefill(q_BLGD.reshape(tokens, key_heads, width).contiguous(),
+                          k_BLGD.reshape(tokens, key_heads, width).contiguous(),
+                          v_BLHD.reshape(tokens, heads, width).contiguous(),
+                          g.view(tokens, heads), beta.view(tokens, heads), state, T=length)
+    if not in_place:
+        if state_BHDD.dtype == torch.float32:
+            return y.view(batch, length, heads, width), state
+        state = state.to(torch.bfloat16)
+    return y.view(batch, length, heads, width), state

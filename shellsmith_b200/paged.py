@@ -138,10 +138,13 @@ def sm_count(device) -> int:
 
 
 def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
-               total_work: int | None = None, sms: int = 148, waves: int = 2,
+               total_work: int | None = None, sms: int | None = None, waves: int = 2,
                cap: int = 256, rows: int | None = None,
                min_pages: int | None = None) -> tuple:
     """(pages_per_split, num_splits) for a batch whose longest sequence has that many pages.
+
+    sms is the SM count of the device that runs the launch (`sm_count(device)`);
+    it is required whenever the size adapts to the batch (total_work given).
 
     Without an explicit size, a split is the largest power of two of pages, at
     most `cap`, whose CTAs still fill `waves` waves (one CTA per SM). The CTA
@@ -165,6 +168,9 @@ def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
     if pages_per_split:
         pps = pages_per_split
     elif total_work:
+        if not sms or sms < 1:
+            raise ValueError("split_plan: an adaptive split needs the device's SM count (sms)")
+
         def ctas(p):
             return total_work / p + (rows / 2 if rows else 0)
         pps = 16
@@ -209,8 +215,12 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
                            workspace: AttentionWorkspace | None = None,
                            out: torch.Tensor | None = None,
                            lse_out: torch.Tensor | None = None,
-                           seq_order: torch.Tensor | None = None) -> torch.Tensor:
+                           seq_order: torch.Tensor | None = None,
+                           sms: int | None = None) -> torch.Tensor:
     """Decode attention of q [B, Hq, D] over each sequence's ctx_len[b] cached tokens.
+
+    sms overrides the SM count the split size is planned for (default: the count
+    of q's device).
 
     seq_order [B] int32 (a permutation) launches the sequences' CTAs in that
     order; longest first shortens the last wave of a ragged batch.
@@ -232,7 +242,8 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     q8 = kv_pool.dtype == torch.uint8
     pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
                              None if total_pages is None else total_pages * groups,
-                             sm_count(q.device), waves=2 if q8 else 3, cap=256 if q8 else 1024,
+                             sms or sm_count(q.device), waves=2 if q8 else 3,
+                             cap=256 if q8 else 1024,
                              rows=None if q8 else B * groups, min_pages=None if q8 else 128)
     if out is None:
         out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)

@@ -52,3 +52,28 @@ def test_split_floor_only_where_the_wave_rule_splits_long_sequences_finely():
                             cap=1024, rows=512, min_pages=128)[0] == 1024
     assert paged.split_plan(64, None, 8 * 64 * 2, 148, waves=3, cap=1024, rows=16,
                             min_pages=128)[0] == 16
+
+
+def test_split_plan_follows_the_device_sm_count():
+    """The adaptive split is planned for the SM count it is given: a part with fewer SMs
+    reaches the wave target with larger splits, and no count means no adaptive plan."""
+    import pytest
+
+    from shellsmith_b200 import paged
+    from shellsmith_b200.engine import HybridConfig
+
+    ctx = np.random.default_rng(3).integers(512, 16385, size=64)
+    pages = -(-ctx // 16)
+    args = (int(pages.max()), None, int(pages.sum()) * 2)
+    kw = dict(waves=3, cap=1024, rows=128)
+    picks = {sms: paged.split_plan(*args, sms, **kw)[0] for sms in (74, 132, 148, 296)}
+    assert picks[74] >= picks[132] >= picks[148] >= picks[296]
+    assert picks[74] > picks[296]
+    for sms, pps in picks.items():   # each is the largest split that still fills 3 waves
+        ctas = lambda p: args[2] / p + kw["rows"] / 2  # noqa: E731
+        assert pps == 16 or ctas(pps) >= 3 * sms
+        assert pps == 1024 or ctas(2 * pps) < 3 * sms
+    with pytest.raises(ValueError, match="SM count"):
+        paged.split_plan(*args, **kw)
+    assert paged.split_plan(100, 16) == (16, 7)          # an explicit size needs no count
+    assert HybridConfig().sms is None and HybridConfig(sms=132).sms == 132

@@ -1,13 +1,20 @@
 """GDN layer glue on the GPU (conv taps, SiLU, q/k norm, gates, gated RMS norm)
 against the CPU restatement in oracle.front.
 
-Bars. Tap rings are bit-exact (they are copies of the inputs). The front's
-q, k, v, g, beta are bf16 values that the kernel computes in fp32 and the
-oracle in float64 before the same roundings, so an element may land one bf16
-step (2^-8 relative) away: at most 1% of elements may differ and none by more
-than 2 steps. The layer output (after the recurrence and the gated norm) is
-within rtol 3e-2 / atol 3e-2 of the oracle, the fp32 state within 2e-2
-absolute (a one-step difference in v moves a state row by beta * 2^-8 |v|).
+Bars, stage by stage (the three-kernel decode and the prefill expose every stage):
+  * tap rings are bit-exact (they are copies of the inputs);
+  * the front's q, k, v, g, beta are bf16 values that the kernel computes in fp32
+    and the oracle in float64 before the same roundings, so an element may land one
+    bf16 step (2^-8 relative) away: at most 1 % of elements may differ and none by
+    more than 2 steps;
+  * the recurrence, fed the GPU's own front values and its state before the step:
+    state within 1e-4, its output y within rtol 2e-2 / atol 2e-3 (the north-star
+    bars; a front element one bf16 step away would move a state row by
+    beta 2^-8 |v|, which is why the recurrence is checked on the GPU's own inputs);
+  * the gated norm of the GPU's y: at most 1 % of elements one or two bf16 steps off.
+The one-launch fused decode (experimental: measured slower than the three-kernel
+step) hides its stages; it is checked end to end with looser bars (outputs
+rtol/atol 3e-2, state 2e-2), as are the integration tests further down.
 """
 
 import numpy as np
@@ -16,7 +23,7 @@ import torch
 
 from oracle import front as ofront
 from oracle import gdn as ogdn
-from shellsmith_b200 import gdn_layer
+from shellsmith_b200 import gdn_layer, numerics
 from shellsmith_b200.gdn_layer import GDNWeights
 
 pytestmark = pytest.mark.gpu
@@ -61,12 +68,56 @@ def _close_bf16(got, want, name):
     assert near.mean() <= 0.01, (name, near.mean())
 
 
-# B = 64 with 8 value heads: the fused form launches 1024 CTAs, more than are
-# resident at once.
+def _check_stages(front_got, front_want, y_got, state_before, state_after, z, out,
+                  norm_w):
+    """Per-stage bars for rows of one step (see the module docstring)."""
+    q, k, v, g, beta = front_got
+    for name, got, want in zip("q k v g beta".split(), front_got, front_want):
+        _close_bf16(got, want, name)
+    y_ref, s_ref = ogdn.token_step(q, k, v, g, beta, state_before)
+    assert np.abs(state_after - s_ref).max() <= 1e-4
+    np.testing.assert_allclose(y_got, y_ref, rtol=2e-2, atol=2e-3)
+    B, Hv = v.shape[:2]
+    want_out = ofront.gated_rms_norm(y_got, z.reshape(B, Hv, 128), norm_w, 1e-6)
+    _close_bf16(out.reshape(B, Hv, 128), want_out, "gated norm")
+
+
+# B = 64 with 8 value heads: 1024 update CTAs, more than are resident at once.
 @pytest.mark.parametrize("Hk,Hv,B", [(2, 4, 3), (16, 32, 5), (2, 8, 64)])
-@pytest.mark.parametrize("path", ["fused", "split"])
-def test_decode_matches_oracle_over_steps(cuda, Hk, Hv, B, path):
-    decode = getattr(gdn_layer, f"gdn_decode_{path}")
+def test_split_decode_stages_match_oracle_over_steps(cuda, Hk, Hv, B):
+    """Five decode steps of the three-kernel form, every stage at its bar."""
+    rng = np.random.default_rng(Hk * 10 + Hv)
+    w, (conv_w, a_log, dt_bias, norm_w) = _weights(rng, Hk, Hv, cuda)
+    slots = B + 2
+    perm = rng.permutation(slots)[:B].astype(np.int32)
+    idx = perm.astype(np.int64)
+    taps = gdn_layer.new_taps(slots, w, device=cuda)
+    state = torch.zeros((slots, Hv, 128, 128), dtype=torch.float32, device=cuda)
+    ws = gdn_layer.SplitWorkspace(B, w, cuda)
+    ref_taps = np.zeros((B, 3, w.channels), np.float32)
+    slot_t = _dev(perm, cuda, torch.int32)
+    for step in range(5):
+        qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
+        pos = torch.full((B,), step, dtype=torch.int32, device=cuda)
+        before = state[idx].double().cpu().numpy()
+        out = gdn_layer.gdn_decode_split(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda),
+                                         _dev(b, cuda), w, taps, pos, state, slot_t,
+                                         workspace=ws)
+        torch.cuda.synchronize()
+        q, k, v, y, g, beta = (t.float().cpu().numpy() for t in ws.views(B, Hk, Hv))
+        *want_front, ref_taps = ofront.front(qkv[:, None], a[:, None], b[:, None], ref_taps,
+                                             conv_w, a_log, dt_bias, Hk, Hv)
+        _check_stages((q, k, v, g, beta), [x[:, 0] for x in want_front], y, before,
+                      state[idx].double().cpu().numpy(), z, out.float().cpu().numpy(), norm_w)
+        for r in range(B):
+            window = gdn_layer.ring_window(taps, int(perm[r]), step + 1)
+            assert np.array_equal(window.float().cpu().numpy(), ref_taps[r])
+    assert torch.count_nonzero(state[np.setdiff1d(np.arange(slots), perm)]) == 0
+
+
+@pytest.mark.parametrize("Hk,Hv,B", [(2, 4, 3), (16, 32, 5), (2, 8, 64)])
+def test_fused_decode_matches_oracle_over_steps(cuda, Hk, Hv, B):
+    """The experimental one-launch form, end to end against the oracle layer."""
     rng = np.random.default_rng(Hk * 10 + Hv)
     w, (conv_w, a_log, dt_bias, norm_w) = _weights(rng, Hk, Hv, cuda)
     slots = B + 2
@@ -79,8 +130,8 @@ def test_decode_matches_oracle_over_steps(cuda, Hk, Hv, B, path):
     for step in range(5):
         qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
         pos = torch.full((B,), step, dtype=torch.int32, device=cuda)
-        out = decode(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda), w, taps, pos,
-                     state, slot_t)
+        out = gdn_layer.gdn_decode_fused(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda),
+                                         _dev(b, cuda), w, taps, pos, state, slot_t)
         want, ref_taps, ref_state = ofront.decode_layer(qkv, z, a, b, ref_taps, ref_state, conv_w,
                                                         a_log, dt_bias, norm_w, 1e-6, Hk, Hv)
         np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=3e-2, atol=3e-2)
@@ -148,9 +199,13 @@ def test_prefill_front_and_layer_match_oracle_ragged_with_history(cuda):
     start_t = torch.tensor(starts, dtype=torch.int32, device=cuda)
     front = gdn_layer.gdn_prefill_front(_dev(qkv, cuda), _dev(a, cuda), _dev(b, cuda), w, taps,
                                         cu, slot_t, start_t)
+    # The recurrence on the GPU's own front values, on a copy of the state.
+    state_y = state.clone()
+    y = numerics.gdn_chunk_prefill(*front, state_y, slot_t, cu)
     out = gdn_layer.gdn_prefill(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda), _dev(b, cuda), w,
                                 taps, state, cu, slot_t, start_t)
     torch.cuda.synchronize()
+    assert torch.equal(state, state_y)      # the layer runs the same kernels
     offs = [0, 100, 137]
     for i, (L, start, slot) in enumerate(zip(lengths, starts, slots)):
         sl = slice(offs[i], offs[i + 1])
@@ -158,8 +213,18 @@ def test_prefill_front_and_layer_match_oracle_ragged_with_history(cuda):
         s_init = np.zeros((Hv, 128, 128)) if start == 0 else s0
         want_front, want_out, want_taps, want_s = _oracle_prefill(
             qkv[sl], z[sl], a[sl], b[sl], t3, s_init, weights_np, Hk, Hv)
-        for name, got, want in zip("q k v g beta".split(), front, want_front):
-            _close_bf16(got[sl].float().cpu().numpy(), want, name)
+        got_front = [t[sl].float().cpu().numpy() for t in front]
+        for name, got, want in zip("q k v g beta".split(), got_front, want_front):
+            _close_bf16(got, want, name)
+        # Recurrence stage at the north-star bars, fed the GPU's front values.
+        y_ref, s_ref = ogdn.sequential(*(x[None] for x in got_front), s_init[None])
+        assert np.abs(state[slot].cpu().numpy() - s_ref[0]).max() <= 1e-4
+        y_got = y[sl].float().cpu().numpy()
+        np.testing.assert_allclose(y_got, y_ref[0], rtol=2e-2, atol=2e-3)
+        _close_bf16(out[sl].float().cpu().numpy().reshape(L, Hv, 128),
+                    ofront.gated_rms_norm(y_got, z[sl].reshape(L, Hv, 128), weights_np[3],
+                                          1e-6), "gated norm")
+        # End to end against the all-oracle layer (front roundings propagate).
         np.testing.assert_allclose(out[sl].float().cpu().numpy(), want_out, rtol=3e-2,
                                    atol=3e-2)
         window = gdn_layer.ring_window(taps, slot, start + L).float().cpu().numpy()

@@ -176,6 +176,57 @@ def test_bad_page_index_sets_device_status(cuda):
     assert _capi.device_status() == 0
 
 
+def test_context_beyond_its_table_row_or_its_splits_is_flagged(cuda):
+    """A ctx_len whose pages exceed the block-table row, or the pages the launch's
+    splits cover, or a negative ctx_len, sets the device status word; the kernel
+    attends the clamped context (never past the row, never dropping pages silently)
+    and the other sequences of the launch stay exact."""
+    from shellsmith_b200 import _capi
+    from shellsmith_b200._torch import ptr, stream_of
+
+    rng = np.random.default_rng(31)
+    hq, hkv, D, P = 16, 2, 256, paged.PAGE_SIZE
+    lengths = [64, 40]                       # 4 and 3 pages: the rows hold 4
+    pool, q, table = _build_case(rng, lengths, hq, hkv, D, 12, cuda, pages_per_seq=4)
+    bt = torch.from_numpy(table).to(cuda)
+    want, _ = _oracle(pool.float().cpu().numpy(), q.float().cpu().numpy(), table, lengths, hkv,
+                      D, 1 / 16)
+
+    def run(ctx_values, pps, nsplit):
+        ctx = torch.tensor(ctx_values, dtype=torch.int32, device=cuda)
+        part_out = torch.empty((2, hq, nsplit, D), dtype=torch.float32, device=cuda)
+        part_lse = torch.empty((2, hq, nsplit), dtype=torch.float32, device=cuda)
+        out = torch.empty((2, hq, D), dtype=torch.bfloat16, device=cuda)
+        _capi.call("sc_paged_decode_attention", ptr(q), ptr(pool), pool.shape[0], ptr(bt),
+                   ptr(ctx), None, 2, hq, hkv, D, P, 4, pps, nsplit, 1 / 16, ptr(part_out),
+                   ptr(part_lse), ptr(out), None, stream_of(q))
+        torch.cuda.synchronize()
+        return out.float().cpu().numpy()
+
+    _capi.device_status()
+    assert np.allclose(run([64, 40], 2, 2), want, rtol=RTOL, atol=ATOL)
+    _capi.check_device()
+    # 100 tokens need 7 pages; the row holds 4: only the row's 64 tokens are read.
+    got = run([100, 40], 2, 2)
+    with pytest.raises(_capi.DeviceFault, match="outside the pool"):
+        _capi.check_device()
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    # 64 tokens, but one split of 2 pages covers only 32 of them.
+    got = run([64, 40], 2, 1)
+    with pytest.raises(_capi.DeviceFault):
+        _capi.check_device()
+    want32, _ = _oracle(pool.float().cpu().numpy(), q.float().cpu().numpy(), table, [32, 32],
+                        hkv, D, 1 / 16)
+    np.testing.assert_allclose(got, want32, rtol=RTOL, atol=ATOL)
+    # A negative length attends nothing (zero output); the other row is unaffected.
+    got = run([-5, 40], 2, 2)
+    with pytest.raises(_capi.DeviceFault):
+        _capi.check_device()
+    assert not np.any(got[0])
+    np.testing.assert_allclose(got[1], want[1], rtol=RTOL, atol=ATOL)
+    assert _capi.device_status() == 0
+
+
 def test_launch_order_changes_nothing_but_the_schedule(cuda):
     """Any permutation as seq_order gives bit-identical outputs; an entry outside
     0..B-1 is reported through the device status word."""

@@ -57,10 +57,10 @@ def _regular(pool, q, table, ctx, width, pps, nsplit):
     return out, lse
 
 
-def _noalloc(pool, q, table, ctx, width, pps, nsplit):
+def _noalloc(pool, q, table, ctx, width, pps, nsplit, with_lse=True):
     B, hq, D = q.shape
     out = torch.empty((B, hq, D), dtype=torch.bfloat16, device=q.device)
-    lse = torch.empty((B * hq,), dtype=torch.float32, device=q.device)
+    lse = torch.empty((B * hq,), dtype=torch.float32, device=q.device) if with_lse else None
     _capi.call("sc_paged_decode_attention_noalloc", ptr(q), ptr(pool), pool.shape[0], ptr(table),
                ptr(ctx), B, hq, pool.shape[1], D, pool.shape[3], width, pps, nsplit, 1.0 / 16,
                ptr(out), ptr(lse), stream_of(q))
@@ -82,6 +82,26 @@ def test_noalloc_matches_caller_scratch_on_two_calls_in_a_row(cuda):
                                    rtol=RTOL, atol=ATOL)
         np.testing.assert_allclose(got_lse.cpu().numpy(), want_lse.cpu().numpy(), rtol=1e-5,
                                    atol=1e-5)
+    _capi.check_device()
+
+
+def test_noalloc_single_split_and_no_lse_match_caller_scratch(cuda):
+    """One split (the kernel writes the output itself and the built-in array is not
+    touched) and a call without lse_out, each against the caller-scratch path."""
+    _build.build()
+    rng = np.random.default_rng(23)
+    lengths = [1, 300, 1000, 2500, 33]
+    pool, q, table, ctx, width = _case(rng, cuda, lengths)
+    for pps, with_lse in ((width, True), (width + 7, False), (8, False)):
+        nsplit = math.ceil(width / pps)
+        want, want_lse = _regular(pool, q, table, ctx, width, pps, nsplit)
+        got, got_lse = _noalloc(pool, q, table, ctx, width, pps, nsplit, with_lse=with_lse)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(got.float().cpu().numpy(), want.float().cpu().numpy(),
+                                   rtol=RTOL, atol=ATOL)
+        if with_lse:
+            np.testing.assert_allclose(got_lse.cpu().numpy(), want_lse.cpu().numpy(),
+                                       rtol=1e-5, atol=1e-5)
     _capi.check_device()
 
 
