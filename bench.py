@@ -534,9 +534,9 @@ def run_ours(args, world, rank, local):
 
     # Launch counter: kernels this build launches per decode step.
     def launches_per_step():
-        # one update per GDN layer; append + split-K per attention layer (the merges, which
-        # run only when a sequence spans more than one split, are counted as they launch)
-        return len(cfg.gdn_layers) + len(cfg.attention_layers) * 2
+        # one update per GDN layer; one launch per attention layer (append + split-K +
+        # merge in sc_paged_decode_attention_fused)
+        return len(cfg.gdn_layers) + len(cfg.attention_layers)
 
     def step(timed_events=None, layer_events=None):
         new = wl.churn()
@@ -589,8 +589,11 @@ def run_ours(args, world, rank, local):
     merges_before = paged.merge_launches
     with ClockSampler(local) as clocks:
         t0 = time.perf_counter()
-        for _ in range(args.steps):
-            step(events, layer_events)
+        # Per-layer events (the roofline of each kernel) on every other step: an event
+        # between two layers keeps the next layer's launch from overlapping the tail of
+        # the one before it, which the other steps keep.
+        for i in range(args.steps):
+            step(events, layer_events if i % 2 == 1 or args.steps == 1 else None)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     barrier(world)
@@ -603,7 +606,9 @@ def run_ours(args, world, rank, local):
     tokens = sum(e[4] for e in events)
     decode_s = sum(decode_ms) / 1e3
     bytes_total = sum(eng.step_bytes(e[5])["total"] for e in events)
-    gdn_bytes = sum(eng.step_bytes(e[5])["gdn"] for e in events)
+    # Per-layer bytes over the steps that carried per-layer events.
+    gdn_bytes = sum(eng.step_bytes(le[3])["gdn"] / len(cfg.gdn_layers)
+                    for le in layer_events if not le[0])
     attn_ms = sum(a.elapsed_time(b) for is_attn, a, b, _ in layer_events if is_attn)
     gdn_ms = sum(a.elapsed_time(b) for is_attn, a, b, _ in layer_events if not is_attn)
     attn_bytes = sum(eng.step_bytes(le[3])["attention_per_layer"]
@@ -687,7 +692,9 @@ def run_ours(args, world, rank, local):
                 "gdn_gbs": round(gdn_gbs, 1), "attention_gbs": round(attn_gbs, 1),
                 "gdn_traffic_per_launch": round(GDN_TRAFFIC_RATIO * gdn_bytes
                                                 / max(1, n_gdn_launch))},
-        "roofline": {"bound": "hbm", "kernel": "paged_decode_attention (append+split+combine)",
+        "roofline": {"bound": "hbm",
+                     "kernel": "paged_decode_attention_fused (append + split-K + merge, one "
+                               "launch)",
                      "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(attn_gbs / hbm, 4),
                      "traffic": round(ATTN_TRAFFIC_RATIO * attn_bytes / max(1, n_attn_launch)),
@@ -884,6 +891,15 @@ def kv8_attention_layer(wl, device, rounds: int = 5) -> dict:
     stream = torch.cuda.current_stream(device)
 
     def run(pool):
+        if pool.dtype == torch.bfloat16:     # the engine's one-launch layer
+            paged.paged_decode_attention_fused(q, k, v, eng.slot_map, pool, eng.table,
+                                               eng.ctx_len, eng.scale,
+                                               max_pages_in_batch=eng.max_pages_in_batch,
+                                               pages_per_split=cfg.pages_per_split,
+                                               total_pages=eng.total_pages,
+                                               workspace=eng.workspace, out=out,
+                                               seq_order=eng.seq_order)
+            return
         paged.kv_append(k, v, pool, eng.slot_map)
         paged.paged_decode_attention(q, pool, eng.table, eng.ctx_len, eng.scale,
                                      max_pages_in_batch=eng.max_pages_in_batch,
@@ -967,6 +983,11 @@ def kv8_layer_standalone(args, device, rounds: int = 10) -> dict:
             row = Hkv * D * 4
 
         def run():
+            if pool.dtype == torch.bfloat16:
+                paged.paged_decode_attention_fused(q, kn, kn, slot_t, pool, bt, ctx, 1.0 / 16,
+                                                   max_pages_in_batch=width, total_pages=total,
+                                                   workspace=ws, out=out)
+                return
             paged.kv_append(kn, kn, pool, slot_t)
             paged.paged_decode_attention(q, pool, bt, ctx, 1.0 / 16, max_pages_in_batch=width,
                                          total_pages=total, workspace=ws, out=out)
@@ -1103,10 +1124,10 @@ def config2_attention(device, steps: int = 20, warmup: int = 3, rank: int = 0,
     stream = torch.cuda.current_stream(device)
 
     def step(s):
-        paged.kv_append(kn, vn, pool, slots_d[s])
-        paged.paged_decode_attention(q, pool, table_d, ctx_d[s], 1 / 16,
-                                     max_pages_in_batch=max_pages, total_pages=total_pages,
-                                     workspace=ws, out=out, seq_order=order)
+        paged.paged_decode_attention_fused(q, kn, vn, slots_d[s], pool, table_d, ctx_d[s], 1 / 16,
+                                           max_pages_in_batch=max_pages,
+                                           total_pages=total_pages, workspace=ws, out=out,
+                                           seq_order=order)
 
     for s in range(warmup):
         step(s)
@@ -1140,7 +1161,7 @@ def config2_attention(device, steps: int = 20, warmup: int = 3, rank: int = 0,
         return None
     return {"n_gpus": world, "seqs_per_gpu": B, "ms_per_step": round(ms, 4),
             "tokens_per_s": round(B_all / (ms / 1e3), 1), "hbm_frac_per_gpu": round(gbs / peak, 4),
-            "parity": parity_word(bad, checked)}
+            "launches_per_step": 1, "parity": parity_word(bad, checked)}
 
 
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:
@@ -1449,12 +1470,16 @@ def config4_parity(shard, attn_in, world: int, rank: int) -> str:
     got = shard.attention(0, q, k, v, 1 / 16).clone()
     identical = True
     if world > 1:
-        paged.paged_decode_attention_packed(q, shard.kv[0], shard.table, shard.ctx, 1 / 16,
-                                            packed=shard.packed,
-                                            max_pages_in_batch=shard.capacity,
-                                            pages_per_split=shard.pages_per_split,
-                                            total_pages=shard.capacity,
-                                            workspace=shard.workspace)
+        # The same partial again, by the kernel the measured path used (the fused layer
+        # rewrites the same appended rows), gathered by NCCL instead.
+        plan = dict(max_pages_in_batch=shard.capacity, pages_per_split=shard.pages_per_split,
+                    total_pages=shard.capacity, workspace=shard.workspace, packed=shard.packed)
+        if shard.peer_fused:
+            paged.paged_decode_attention_packed(q, shard.kv[0], shard.table, shard.ctx, 1 / 16,
+                                                **plan)
+        else:
+            paged.paged_decode_attention_fused(q, k, v, shard.slot, shard.kv[0], shard.table,
+                                               shard.ctx, 1 / 16, **plan)
         dist.all_gather_into_tensor(shard.gathered, shard.packed)
         ref, _ = paged.attention_combine_packed(shard.gathered)
         torch.cuda.synchronize()

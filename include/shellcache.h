@@ -398,6 +398,41 @@ int sc_attention_combine_exchange(const float* gathered, const unsigned int* fla
                                   int nparts, int rows, int D, sc_bf16* out, float* lse_out,
                                   void* stream);
 
+/* One attention layer of a decode step in one launch: the KV append of the
+ * step's new token (sc_kv_append) folded into split-K decode attention
+ * (sc_paged_decode_attention), with the split merge done by the last split of
+ * each sequence to finish when num_splits <= 16 (no separate merge launch;
+ * above 16 splits a separate merge kernel follows, as in
+ * sc_paged_decode_attention).
+ *
+ * Replaces, as one kernel, the KV write of mlx_request_cache.py:59-63
+ * (`OwnedKV.update_and_fetch`) and the per-request SDPA of mlx_decode.py:80-106
+ * (`_attention_rows`); math of scripts/mlx_attention_qualify.py:234-275.
+ *
+ * k_new, v_new [B, Hkv, D] bf16 (16-byte aligned) are each row's new token;
+ * slot_mapping [B] int64 its slot (page * 16 + offset, < 0: nothing appended).
+ * ctx_len counts the new token. The rows are written to the pool once, and a
+ * CTA whose pages include the slot's page takes the rows from k_new / v_new, so
+ * the result equals sc_kv_append followed by sc_paged_decode_attention; the
+ * slot's page must not be shared with another row of the launch (copy-on-write
+ * of a partial page guarantees that). Other arguments as in
+ * sc_paged_decode_attention, with exactly one of out (bf16 rows, lse_out
+ * optional) or packed ([B * Hq][D + 1] fp32, lse at index D, as
+ * sc_paged_decode_attention_packed); out 8-byte aligned. num_splits > 1 needs
+ * part_out and part_lse, and 1 < num_splits <= 16 also `counters`:
+ * B * Hkv * ceil(Hq / Hkv / 8) uint32, zero before the first call; each launch
+ * leaves them zero (after a DeviceFault, zero them again).
+ * Launches that share counters or scratch must not overlap on the GPU. */
+int sc_paged_decode_attention_fused(const sc_bf16* q, const sc_bf16* k_new,
+                                    const sc_bf16* v_new, const int64_t* slot_mapping,
+                                    sc_bf16* kv_pool, int64_t num_pages,
+                                    const int32_t* block_table, const int32_t* ctx_len,
+                                    const int32_t* seq_order, int B, int Hq, int Hkv, int D,
+                                    int P, int max_pages, int pages_per_split, int num_splits,
+                                    float scale, float* part_out, float* part_lse,
+                                    unsigned int* counters, sc_bf16* out, float* lse_out,
+                                    float* packed, void* stream);
+
 /* Split-K decode attention that allocates nothing and takes no scratch.
  *
  * No counterpart in the reference: it exists for callers of this library

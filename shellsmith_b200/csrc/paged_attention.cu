@@ -42,7 +42,87 @@ struct AttnShape {
   static constexpr int KSTEPS = D / 16;
 };
 
-template <int D, int NW, int NSTAGE>
+// The most parts the in-kernel merge of the one-launch layer takes; a launch with
+// more splits (a few very long sequences) merges in the separate combine kernel,
+// whose (row, 32-dim) CTAs spread the reads over the SMs.
+constexpr int kFusedMergeParts = 16;
+
+// The last CTA of a (sequence, kv head, head group) to finish merges the
+// normalised partials of the sequence's `ns` <= kFusedMergeParts splits for its
+// `heads` query heads: out = sum_s e^(lse_s - M) o_s / sum_s e^(lse_s - M). All
+// heads at once: warp w makes the weights of heads w, w + NW, ... into shared
+// memory `w` ([8][kFusedMergeParts]), then each thread sums float4 column
+// groups of every head over the parts, all loads independent. Other CTAs'
+// partials are read through L2 (ld.global.cg): L1 is not coherent across SMs.
+template <int D, int NW>
+__device__ void merge_splits(const float* part_out, const float* part_lse, size_t row0,
+                             int heads, int num_splits, int ns, float* w, uint16_t* out,
+                             float* lse_out, float* packed) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int h = warp; h < heads; h += NW) {
+    const float ls = lane < ns ? __ldcg(part_lse + (row0 + h) * num_splits + lane) : -CUDART_INF_F;
+    float m = ls;
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float e = (ls == -CUDART_INF_F) ? 0.f : __expf(ls - m);
+    float sum = e;
+    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const bool empty = m == -CUDART_INF_F;
+    if (lane < kFusedMergeParts) w[h * kFusedMergeParts + lane] = empty ? 0.f : e / sum;
+    if (lane == 0) {
+      const float l = empty ? -CUDART_INF_F : m + logf(sum);
+      if (packed != nullptr)
+        packed[(row0 + h) * (D + 1) + D] = l;
+      else if (lse_out != nullptr)
+        lse_out[row0 + h] = l;
+    }
+  }
+  __syncthreads();
+  constexpr int kGroups = D / 4;  // float4 column groups per head
+  for (int g = threadIdx.x; g < heads * kGroups; g += NW * 32) {
+    const int h = g / kGroups, c = 4 * (g - h * kGroups);
+    const float* po = part_out + (row0 + h) * (size_t)num_splits * D + c;
+    const float* wh = w + h * kFusedMergeParts;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < ns; ++s) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(po + (size_t)s * D));
+      const float ws = wh[s];
+      acc.x = fmaf(ws, v.x, acc.x);
+      acc.y = fmaf(ws, v.y, acc.y);
+      acc.z = fmaf(ws, v.z, acc.z);
+      acc.w = fmaf(ws, v.w, acc.w);
+    }
+    const size_t row = row0 + h;
+    if (packed != nullptr) {
+      float* dst = packed + row * (D + 1) + c;
+      dst[0] = acc.x;
+      dst[1] = acc.y;
+      dst[2] = acc.z;
+      dst[3] = acc.w;
+    } else {
+      uint2 pk;
+      pk.x = pack_bf16x2(acc.x, acc.y);
+      pk.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(out + row * D + c) = pk;
+    }
+  }
+}
+
+// What the one-launch attention layer (kFused) adds to the split-K kernel: the
+// new token's K/V rows [B][Hkv][D] and their slots (page * 16 + offset, < 0
+// skips a row), the pool written through, and, when the splits merge in the
+// kernel, one arrival counter per (sequence, kv head, head group), zero between
+// launches.
+struct FusedArgs {
+  const uint16_t* k_new = nullptr;
+  const uint16_t* v_new = nullptr;
+  const int64_t* slot_mapping = nullptr;
+  uint16_t* pool = nullptr;
+  unsigned int* counters = nullptr;
+  int merge = 0;  // 1: the splits merge in the kernel (num_splits <= kFusedMergeParts)
+};
+
+template <int D, int NW, int NSTAGE, bool kFused>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kv_pool,
                         const int32_t* __restrict__ block_table,
@@ -52,17 +132,13 @@ __global__ void __launch_bounds__(NW * 32)
                         float* __restrict__ part_out, float* __restrict__ part_lse,
                         uint16_t* __restrict__ out, float* __restrict__ lse_out,
                         float* __restrict__ packed, long long num_pages,
-                        unsigned int* status) {
+                        unsigned int* status, FusedArgs fa) {
   using S = AttnShape<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NW * NSTAGE * S::STAGE_BYTES);
   pdl_wait();
   pdl_trigger();
 
-  // After any bounded wait has given up on this device, later CTAs stop at
-  // once instead of each waiting out its own limit.
-  if (status != nullptr && (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT))
-    return;
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / HG;
   const int hg = blockIdx.y - kvh * HG;
@@ -76,14 +152,56 @@ __global__ void __launch_bounds__(NW * 32)
                                 status, split == 0 && blockIdx.y == 0 && threadIdx.x == 0);
   const int npages = (L + kPage - 1) / kPage;
   const int p_begin = split * pages_per_split;
+  // Splits this sequence fills: with one, the CTA writes the final rows itself.
+  const int ns_seq = (npages + pages_per_split - 1) / pages_per_split;
+  const bool final_here = num_splits == 1 || (kFused && fa.merge && ns_seq <= 1);
+
+  // The appended token (kFused): its page and offset, and its rows written to
+  // the pool once per (sequence, kv head), by split 0 of head group 0. A CTA
+  // whose pages include that page replaces the row in its own stage copy, so no
+  // CTA depends on when the write lands.
+  long long slot_page = -1;
+  int slot_off = 0;
+  if constexpr (kFused) {
+    const int64_t slot = fa.slot_mapping != nullptr ? fa.slot_mapping[b] : -1;
+    if (slot >= 0 && slot / kPage < num_pages) {
+      slot_page = slot / kPage;
+      slot_off = (int)(slot - slot_page * kPage);
+    } else if (slot >= 0 && split == 0 && hg == 0 && threadIdx.x == 0) {
+      flag_device(status, DEV_BAD_INDEX);
+    }
+    if (slot_page >= 0 && split == 0 && hg == 0) {
+      const uint4* kr = reinterpret_cast<const uint4*>(fa.k_new + ((size_t)b * Hkv + kvh) * D);
+      const uint4* vr = reinterpret_cast<const uint4*>(fa.v_new + ((size_t)b * Hkv + kvh) * D);
+      for (int c = threadIdx.x; c < 2 * (D / 8); c += blockDim.x) {
+        const int which = c / (D / 8), cc = c - which * (D / 8);
+        uint16_t* dst = fa.pool + ((((size_t)slot_page * Hkv + kvh) * 2 + which) * kPage +
+                                   slot_off) * D + 8 * (cc ^ (slot_off & 7));
+        *reinterpret_cast<uint4*>(dst) = which ? vr[cc] : kr[cc];
+      }
+    }
+  }
+
+  // After any bounded wait has given up on this device, later CTAs stop at
+  // once instead of each waiting out its own limit (a fused CTA still counts
+  // its arrival, so the counters stay consistent for the next launch).
+  if (status != nullptr && (*reinterpret_cast<volatile unsigned int*>(status) & DEV_WAIT_TIMEOUT)) {
+    if constexpr (kFused) {
+      if (fa.merge && !final_here && p_begin < npages && threadIdx.x == 0) {
+        unsigned int* ctr = fa.counters + ((size_t)b * Hkv + kvh) * HG + hg;
+        if (atomicAdd(ctr, 1u) == (unsigned int)(ns_seq - 1)) *ctr = 0u;
+      }
+    }
+    return;
+  }
   if (npages == 0 && split == 0) {  // nothing to attend: zero output, lse = -inf
     for (int idx = threadIdx.x; idx < min(kHeadsPerTile, G - hg * kHeadsPerTile) * D;
          idx += blockDim.x) {
       const size_t row = (size_t)b * Hq + kvh * G + hg * kHeadsPerTile + idx / D;
-      if (num_splits == 1 && packed != nullptr) {
+      if (final_here && packed != nullptr) {
         packed[row * (D + 1) + idx % D] = 0.f;
         if (idx % D == 0) packed[row * (D + 1) + D] = -CUDART_INF_F;
-      } else if (num_splits == 1) {
+      } else if (final_here) {
         out[row * D + idx % D] = 0;
         if (idx % D == 0 && lse_out != nullptr) lse_out[row] = -CUDART_INF_F;
       }
@@ -165,6 +283,21 @@ __global__ void __launch_bounds__(NW * 32)
            c += 32)
         vrows[c] = make_uint4(0u, 0u, 0u, 0u);
       __syncwarp();
+    }
+    if constexpr (kFused) {
+      // The appended token's page: its row in this stage copy comes from the
+      // new K/V (the copy may predate the pool write).
+      if (slot_page >= 0 && bt_row[p_begin + warp + j * NW] == slot_page) {
+        const uint4* kr = reinterpret_cast<const uint4*>(fa.k_new + ((size_t)b * Hkv + kvh) * D);
+        const uint4* vr = reinterpret_cast<const uint4*>(fa.v_new + ((size_t)b * Hkv + kvh) * D);
+        uint8_t* krow = stage + s * S::STAGE_BYTES + slot_off * S::ROW_BYTES;
+        for (int c = lane; c < D / 8; c += 32) {
+          const int at = (c ^ (slot_off & 7)) << 4;
+          *reinterpret_cast<uint4*>(krow + at) = kr[c];
+          *reinterpret_cast<uint4*>(krow + S::KV_BYTES + at) = vr[c];
+        }
+        __syncwarp();
+      }
     }
 
     float sc4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -272,15 +405,39 @@ __global__ void __launch_bounds__(NW * 32)
     const float val = acc / lsum;
     const float lse = (M + log2f(lsum)) * kLn2;
     const size_t row = (size_t)b * Hq + head0 + n;
-    if (num_splits == 1 && packed != nullptr) {
+    if (final_here && packed != nullptr) {
       packed[row * (D + 1) + d] = val;
       if (d == 0) packed[row * (D + 1) + D] = lse;
-    } else if (num_splits == 1) {
+    } else if (final_here) {
       out[row * D + d] = f_to_bf16(val);
       if (d == 0 && lse_out != nullptr) lse_out[row] = lse;
     } else {
       part_out[(row * num_splits + split) * D + d] = val;
       if (d == 0) part_lse[row * num_splits + split] = lse;
+    }
+  }
+  if constexpr (kFused) {
+    // Count this split in; the last of the sequence's splits to arrive merges them
+    // (no CTA waits for another) and leaves the counter at zero for the next launch.
+    if (fa.merge && !final_here) {
+      __shared__ int s_last;
+      __threadfence();  // this thread's partials are visible on the device ...
+      __syncthreads();  // ... before thread 0 counts the CTA in
+      if (threadIdx.x == 0) {
+        unsigned int* ctr = fa.counters + ((size_t)b * Hkv + kvh) * HG + hg;
+        const int last = atomicAdd(ctr, 1u) == (unsigned int)(ns_seq - 1);
+        if (last) {
+          *ctr = 0u;
+          __threadfence();  // every other split's partials are visible from here
+        }
+        s_last = last;
+      }
+      __syncthreads();
+      if (s_last) {
+        float* w = reinterpret_cast<float*>(smem);  // the stage memory is free
+        merge_splits<D, NW>(part_out, part_lse, (size_t)b * Hq + head0, heads_here,
+                            num_splits, ns_seq, w, out, lse_out, packed);
+      }
     }
   }
 }
@@ -557,21 +714,23 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
                   int max_pages,
                   int pages_per_split, int num_splits, float scale, float* part_out,
                   float* part_lse, uint16_t* out, float* lse_out, float* packed,
-                  long long num_pages, const PeerPut* put, cudaStream_t s) {
+                  long long num_pages, const PeerPut* put, const FusedArgs* fused,
+                  cudaStream_t s) {
   using S = AttnShape<D>;
   constexpr int NW = kWarpsPerCta, NST = kStages;
   const size_t smem = (size_t)NW * NST * S::STAGE_BYTES + NW * NST * sizeof(uint64_t);
-  auto kernel = paged_decode_kernel<D, NW, NST>;
-  static int configured[64] = {};
+  auto kernel = fused != nullptr ? paged_decode_kernel<D, NW, NST, true>
+                                 : paged_decode_kernel<D, NW, NST, false>;
+  static int configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev >= 0 && dev < 64 && !configured[fused != nullptr][dev]) {
     cudaError_t err =
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess)
       return set_error(SC_ERR_CUDA, "sc_paged_decode_attention: smem attribute: %s",
                        cudaGetErrorString(err));
-    configured[dev] = 1;
+    configured[fused != nullptr][dev] = 1;
   }
   const int G = Hq / Hkv;
   const int HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
@@ -580,11 +739,13 @@ int launch_decode(const uint16_t* q, const uint16_t* kv_pool, const int32_t* blo
   cudaError_t err = launch_pdl(kernel, grid, dim3(NW * 32), smem, s, q, kv_pool, block_table,
                                ctx_len, seq_order, Hq, Hkv, G, HG, max_pages, pages_per_split,
                                num_splits, scale_log2, part_out, part_lse, out, lse_out, packed,
-                               num_pages, device_status_word());
+                               num_pages, device_status_word(),
+                               fused != nullptr ? *fused : FusedArgs{});
   if (err != cudaSuccess)
     return set_error(SC_ERR_CUDA, "sc_paged_decode_attention: launch: %s",
                      cudaGetErrorString(err));
   if (int rc = check_launch("sc_paged_decode_attention")) return rc;
+  if (fused != nullptr && fused->merge) return SC_OK;  // the splits merged themselves
   if (put != nullptr) {  // the entry guarantees num_splits > 1
     dim3 cgrid(B * Hq, (D + 31) / 32);
     launch_pdl(combine_tiled_kernel<true>, cgrid, dim3(kCombineThreads), 0, s,
@@ -611,7 +772,7 @@ int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int
                  int B, int Hq, int Hkv,
                  int D, int P, int max_pages, int pages_per_split, int num_splits, float scale,
                  float* part_out, float* part_lse, sc_bf16* out, float* lse_out, float* packed,
-                 const PeerPut* put, void* stream) {
+                 const PeerPut* put, void* stream, const FusedArgs* fused = nullptr) {
   SC_REQUIRE(q && kv_pool && block_table && ctx_len && (out || packed || put), SC_ERR_INVALID,
              "%s: null pointer", name);
   SC_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, SC_ERR_INVALID,
@@ -632,17 +793,17 @@ int decode_entry(const char* name, const sc_bf16* q, const sc_bf16* kv_pool, int
       return launch_decode<64>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
                                  max_pages,
                                    pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                   lse_out, packed, num_pages, put, s);
+                                   lse_out, packed, num_pages, put, fused, s);
     case 128:
       return launch_decode<128>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
                                  max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                    lse_out, packed, num_pages, put, s);
+                                    lse_out, packed, num_pages, put, fused, s);
     case 256:
       return launch_decode<256>(q, kv_pool, block_table, ctx_len, seq_order, B, Hq, Hkv,
                                  max_pages,
                                     pages_per_split, num_splits, scale, part_out, part_lse, out,
-                                    lse_out, packed, num_pages, put, s);
+                                    lse_out, packed, num_pages, put, fused, s);
     default:
       return set_error(SC_ERR_UNSUPPORTED, "%s: D=%d not in {64,128,256}", name, D);
   }
@@ -663,6 +824,35 @@ extern "C" int sc_paged_decode_attention(const sc_bf16* q, const sc_bf16* kv_poo
                           ctx_len, seq_order, B, Hq, Hkv, D, P, max_pages, pages_per_split,
                           num_splits,
                           scale, part_out, part_lse, out, lse_out, nullptr, nullptr, stream);
+}
+
+extern "C" int sc_paged_decode_attention_fused(
+    const sc_bf16* q, const sc_bf16* k_new, const sc_bf16* v_new, const int64_t* slot_mapping,
+    sc_bf16* kv_pool, int64_t num_pages, const int32_t* block_table, const int32_t* ctx_len,
+    const int32_t* seq_order, int B, int Hq, int Hkv, int D, int P, int max_pages,
+    int pages_per_split, int num_splits, float scale, float* part_out, float* part_lse,
+    unsigned int* counters, sc_bf16* out, float* lse_out, float* packed, void* stream) {
+  const char* name = "sc_paged_decode_attention_fused";
+  SC_REQUIRE(k_new && v_new && slot_mapping, SC_ERR_INVALID, "%s: null pointer", name);
+  SC_REQUIRE((out != nullptr) != (packed != nullptr), SC_ERR_INVALID,
+             "%s: give exactly one of out and packed", name);
+  SC_REQUIRE(num_splits == 1 || num_splits > sc::kFusedMergeParts || counters != nullptr,
+             SC_ERR_INVALID, "%s: 1 < num_splits <= %d needs the arrival counters", name,
+             sc::kFusedMergeParts);
+  SC_REQUIRE(((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) ==
+                 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0,
+             SC_ERR_INVALID, "%s: k_new and v_new must be 16-byte aligned, out 8-byte aligned",
+             name);
+  sc::FusedArgs fa;
+  fa.k_new = reinterpret_cast<const uint16_t*>(k_new);
+  fa.v_new = reinterpret_cast<const uint16_t*>(v_new);
+  fa.slot_mapping = slot_mapping;
+  fa.pool = reinterpret_cast<uint16_t*>(kv_pool);
+  fa.counters = counters;
+  fa.merge = num_splits > 1 && num_splits <= sc::kFusedMergeParts;
+  return sc::decode_entry(name, q, kv_pool, num_pages, block_table, ctx_len, seq_order, B, Hq,
+                          Hkv, D, P, max_pages, pages_per_split, num_splits, scale, part_out,
+                          part_lse, out, lse_out, packed, nullptr, stream, &fa);
 }
 
 extern "C" int sc_paged_decode_attention_packed(const sc_bf16* q, const sc_bf16* kv_pool,

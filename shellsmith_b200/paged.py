@@ -194,6 +194,9 @@ class AttentionWorkspace:
                                     device=device)
         self.part_lse = torch.empty((batch, q_heads, num_splits), dtype=torch.float32,
                                     device=device)
+        # Arrival counters of the one-launch layer (one per sequence, kv head and head
+        # group: at most one per query head); every launch leaves them zero.
+        self.counters = torch.zeros(batch * q_heads, dtype=torch.int32, device=device)
 
     def fits(self, batch: int, q_heads: int, head_dim: int, num_splits: int) -> bool:
         b, h, s, d = self.part_out.shape
@@ -268,6 +271,77 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
         global merge_launches
         merge_launches += 1
     return out
+
+
+def paged_decode_attention_fused(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                                 slot_mapping: torch.Tensor, kv_pool: torch.Tensor,
+                                 block_table: torch.Tensor, ctx_len: torch.Tensor, scale: float,
+                                 *, max_pages_in_batch: int | None = None,
+                                 pages_per_split: int | None = None,
+                                 total_pages: int | None = None,
+                                 workspace: AttentionWorkspace | None = None,
+                                 out: torch.Tensor | None = None,
+                                 lse_out: torch.Tensor | None = None,
+                                 packed: torch.Tensor | None = None,
+                                 seq_order: torch.Tensor | None = None,
+                                 sms: int | None = None) -> torch.Tensor:
+    """kv_append of each row's new token followed by paged_decode_attention, as one
+    launch (sc_paged_decode_attention_fused): the splits of a sequence merge
+    themselves, the last one to finish combining them.
+
+    k_new, v_new [B, Hkv, D] bf16 and slot_mapping [B] int64 (< 0: no append) are
+    the step's new tokens; ctx_len counts them. With `packed` ([B * Hq, D + 1] fp32)
+    the rows come out as the packed per-device partial instead of bf16 `out`.
+    Other arguments as paged_decode_attention (bf16 pools only).
+    """
+    if kv_pool.dtype != torch.bfloat16:
+        raise TypeError("paged_decode_attention_fused takes bf16 pools")
+    num_pages, hkv, page, dim = _pool_dims(kv_pool)
+    require_cuda("q", q, torch.bfloat16, 3)
+    require_cuda("k_new", k_new, torch.bfloat16, 3)
+    require_cuda("v_new", v_new, torch.bfloat16, 3)
+    require_cuda("slot_mapping", slot_mapping, torch.int64, 1, align=8)
+    require_cuda("block_table", block_table, torch.int32, 2, align=4)
+    require_cuda("ctx_len", ctx_len, torch.int32, 1, align=4)
+    B, hq, d = q.shape
+    if (d != dim or hq % hkv or block_table.shape[0] != B or ctx_len.shape[0] != B
+            or k_new.shape != (B, hkv, dim) or v_new.shape != k_new.shape
+            or slot_mapping.shape[0] != B):
+        raise ValueError("paged_decode_attention_fused: inconsistent shapes")
+    max_pages = block_table.shape[1]
+    groups = hkv * ((hq // hkv + 7) // 8)
+    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
+                             None if total_pages is None else total_pages * groups,
+                             sms or sm_count(q.device), waves=3, cap=1024, rows=B * groups,
+                             min_pages=128)
+    if packed is None:
+        if out is None:
+            out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)
+        require_cuda("out", out, torch.bfloat16, 3)
+    else:
+        require_cuda("packed", packed, torch.float32, 2, align=4)
+        if tuple(packed.shape) != (B * hq, dim + 1) or out is not None:
+            raise ValueError("paged_decode_attention_fused: packed is [B * Hq, D + 1], "
+                             "given instead of out")
+    if lse_out is not None:
+        require_cuda("lse_out", lse_out, torch.float32, 1, align=4)
+    if seq_order is not None:
+        require_cuda("seq_order", seq_order, torch.int32, 1, align=4)
+        if seq_order.shape[0] != B:
+            raise ValueError("paged_decode_attention_fused: seq_order needs one entry per "
+                             "sequence")
+    part_out = part_lse = counters = None
+    if nsplit > 1:
+        if workspace is None or not workspace.fits(B, hq, dim, nsplit):
+            workspace = AttentionWorkspace(B, hq, dim, nsplit, device=q.device)
+        part_out, part_lse = workspace.views(B, nsplit)
+        counters = workspace.counters
+    _capi.call("sc_paged_decode_attention_fused", ptr(q), ptr(k_new), ptr(v_new),
+               ptr(slot_mapping), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len),
+               ptr(seq_order), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
+               ptr(part_out), ptr(part_lse), ptr(counters), ptr(out), ptr(lse_out), ptr(packed),
+               stream_of(q))
+    return packed if packed is not None else out
 
 
 def attention_combine(part_out: torch.Tensor, part_lse: torch.Tensor,

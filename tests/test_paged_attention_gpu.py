@@ -300,3 +300,87 @@ def test_config2_scale_sample_matches_oracle(cuda, B):
         np.testing.assert_allclose(out[b].float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
     del pool
     torch.cuda.empty_cache()
+
+
+def _fused_case(rng, cuda, lengths, hq, hkv, D, num_pages, width):
+    """A pool holding each sequence's first L-1 tokens, the new token's K/V and slots."""
+    P = paged.PAGE_SIZE
+    pool, q, table = _build_case(rng, lengths, hq, hkv, D, num_pages, cuda, pages_per_seq=width)
+    B = len(lengths)
+    k_new = torch.randn((B, hkv, D), device=cuda).to(torch.bfloat16)
+    v_new = torch.randn((B, hkv, D), device=cuda).to(torch.bfloat16)
+    slots = np.array([table[b, (L - 1) // P] * P + (L - 1) % P if L > 0 else -1
+                      for b, L in enumerate(lengths)], np.int64)
+    return pool, q, table, k_new, v_new, torch.from_numpy(slots).to(cuda)
+
+
+# 64 one-page splits merge in the separate kernel; 16 (the in-kernel cap) and 8 merge in
+# the last split of each sequence; 64 pages per split is one split.
+@pytest.mark.parametrize("pages_per_split", [1, 4, 8, 64])
+def test_fused_layer_equals_append_then_attention(cuda, pages_per_split):
+    """Append + split-K (+ the merge) against kv_append followed by the unfused
+    attention: the pool bit for bit, the output within tolerance of the oracle over the
+    appended context, the counters back at zero, and a repeated call (counters reused)
+    bit-identical."""
+    from shellsmith_b200 import _capi
+
+    rng = np.random.default_rng(40 + pages_per_split)
+    hq, hkv, D = 16, 2, 256
+    lengths = [1, 15, 16, 17, 33, 200, 517, 0, 64, 1000]
+    pool, q, table, k_new, v_new, slots = _fused_case(rng, cuda, lengths, hq, hkv, D, 200, 64)
+    bt = torch.from_numpy(table).to(cuda)
+    ctx = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    ref_pool = pool.clone()
+    paged.kv_append(k_new, v_new, ref_pool, slots)
+    want_out = paged.paged_decode_attention(q, ref_pool, bt, ctx, 1 / 16,
+                                            pages_per_split=pages_per_split)
+    ws = paged.AttentionWorkspace(len(lengths), hq, D, 64, device=cuda)
+    lse = torch.empty(len(lengths) * hq, dtype=torch.float32, device=cuda)
+    got = paged.paged_decode_attention_fused(q, k_new, v_new, slots, pool, bt, ctx, 1 / 16,
+                                             pages_per_split=pages_per_split, workspace=ws,
+                                             lse_out=lse)
+    torch.cuda.synchronize()
+    assert torch.equal(pool, ref_pool)
+    assert torch.count_nonzero(ws.counters) == 0
+    want, want_lse = _oracle(ref_pool.float().cpu().numpy(), q.float().cpu().numpy(), table,
+                             lengths, hkv, D, 1 / 16)
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(lse.cpu().numpy().reshape(want_lse.shape), want_lse, atol=1e-3)
+    np.testing.assert_allclose(got.float().cpu().numpy(), want_out.float().cpu().numpy(),
+                               rtol=RTOL, atol=ATOL)
+    again = paged.paged_decode_attention_fused(q, k_new, v_new, slots, pool, bt, ctx, 1 / 16,
+                                               pages_per_split=pages_per_split, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(again, got) and torch.count_nonzero(ws.counters) == 0
+    _capi.check_device()
+
+
+def test_fused_layer_packed_many_splits_and_launch_order(cuda):
+    """Packed rows; more splits than one merge window holds (1,100 one-page splits of
+    one sequence); any launch order; rows with no new token (slot -1)."""
+    from shellsmith_b200 import _capi
+
+    rng = np.random.default_rng(47)
+    hq, hkv, D = 8, 1, 128
+    lengths = [17600, 300, 1, 45]
+    pool, q, table, k_new, v_new, slots = _fused_case(rng, cuda, lengths, hq, hkv, D, 1200,
+                                                      1100)
+    slots[2] = -1                  # row 2 appends nothing: its one cached token stays
+    bt = torch.from_numpy(table).to(cuda)
+    ctx = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    ref_pool = pool.clone()
+    paged.kv_append(k_new, v_new, ref_pool, slots)
+    ws = paged.AttentionWorkspace(len(lengths), hq, D, 1100, device=cuda)
+    packed = torch.empty((len(lengths) * hq, D + 1), dtype=torch.float32, device=cuda)
+    order = torch.tensor([2, 0, 3, 1], dtype=torch.int32, device=cuda)
+    paged.paged_decode_attention_fused(q, k_new, v_new, slots, pool, bt, ctx, 1 / 16,
+                                       pages_per_split=1, workspace=ws, packed=packed,
+                                       seq_order=order)
+    torch.cuda.synchronize()
+    assert torch.equal(pool, ref_pool) and torch.count_nonzero(ws.counters) == 0
+    want, want_lse = _oracle(ref_pool.float().cpu().numpy(), q.float().cpu().numpy(), table,
+                             lengths, hkv, D, 1 / 16)
+    got = packed.cpu().numpy().reshape(len(lengths), hq, D + 1)
+    np.testing.assert_allclose(got[..., :D], want, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(got[..., D], want_lse, atol=1e-3)
+    _capi.check_device()
