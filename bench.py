@@ -390,7 +390,9 @@ class Workload:
         group, total = [], 0
         for slot, prompt in new + [(None, None)]:
             if slot is None or total + prompt > self.PROMPT_CAP:
-                self.prefill_launches += self.engine.prefill(group, gdn, kv, self.prompt_out)
+                # GDN chunk launches only: the K/V writes are counted by paged as they launch.
+                launched = self.engine.prefill(group, gdn, kv, self.prompt_out)
+                self.prefill_launches += max(0, launched - len(self.cfg.attention_layers))
                 group, total = [], 0
             if slot is not None:
                 group.append((slot, prompt))
@@ -532,11 +534,12 @@ def run_ours(args, world, rank, local):
     cfg = wl.cfg
     stream = torch.cuda.current_stream(device)
 
-    # Launch counter: kernels this build launches per decode step.
+    # Launch counter: kernels this build launches per decode step: one update per GDN
+    # layer; the attention layers' kernels are counted as they launch (paged counts
+    # them: one when the append folds into the split-K launch, else the append, the
+    # split-K kernel and, when a sequence spans splits, the merge).
     def launches_per_step():
-        # one update per GDN layer; one launch per attention layer (append + split-K +
-        # merge in sc_paged_decode_attention_fused)
-        return len(cfg.gdn_layers) + len(cfg.attention_layers)
+        return len(cfg.gdn_layers)
 
     def step(timed_events=None, layer_events=None):
         new = wl.churn()
@@ -586,7 +589,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     events, layer_events = [], []
     launches_before = wl.prefill_launches
-    merges_before = paged.merge_launches
+    attn_before = paged.attention_launches
     with ClockSampler(local) as clocks:
         t0 = time.perf_counter()
         # Per-layer events (the roofline of each kernel) on every other step: an event
@@ -598,7 +601,7 @@ def run_ours(args, world, rank, local):
         wall = time.perf_counter() - t0
     barrier(world)
     _capi.check_device()
-    timed_launches = (launches_per_step() * args.steps + paged.merge_launches - merges_before
+    timed_launches = (launches_per_step() * args.steps + paged.attention_launches - attn_before
                       + wl.prefill_launches - launches_before)
 
     decode_ms = [s0.elapsed_time(s1) for s0, s1, *_ in events]
@@ -693,8 +696,8 @@ def run_ours(args, world, rank, local):
                 "gdn_traffic_per_launch": round(GDN_TRAFFIC_RATIO * gdn_bytes
                                                 / max(1, n_gdn_launch))},
         "roofline": {"bound": "hbm",
-                     "kernel": "paged_decode_attention_fused (append + split-K + merge, one "
-                               "launch)",
+                     "kernel": "paged_decode_attention_fused (append folded into split-K; "
+                               "+ merge when a sequence spans splits)",
                      "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(attn_gbs / hbm, 4),
                      "traffic": round(ATTN_TRAFFIC_RATIO * attn_bytes / max(1, n_attn_launch)),
@@ -890,32 +893,29 @@ def kv8_attention_layer(wl, device, rounds: int = 5) -> dict:
     pool8[:, :, 32 * D:].view(torch.bfloat16).fill_(0.01)   # scales and biases
     stream = torch.cuda.current_stream(device)
 
-    def run(pool):
-        if pool.dtype == torch.bfloat16:     # the engine's one-launch layer
-            paged.paged_decode_attention_fused(q, k, v, eng.slot_map, pool, eng.table,
-                                               eng.ctx_len, eng.scale,
-                                               max_pages_in_batch=eng.max_pages_in_batch,
-                                               pages_per_split=cfg.pages_per_split,
-                                               total_pages=eng.total_pages,
-                                               workspace=eng.workspace, out=out,
-                                               seq_order=eng.seq_order)
-            return
+    plan = dict(max_pages_in_batch=eng.max_pages_in_batch, pages_per_split=cfg.pages_per_split,
+                total_pages=eng.total_pages, workspace=eng.workspace, out=out,
+                seq_order=eng.seq_order)
+
+    def run(pool):   # the engine's attention layer on either pool
+        paged.append_and_attend(q, k, v, eng.slot_map, pool, eng.table, eng.ctx_len, eng.scale,
+                                **plan)
+
+    def run_two(pool):   # the append and the attention as separate launches
         paged.kv_append(k, v, pool, eng.slot_map)
-        paged.paged_decode_attention(q, pool, eng.table, eng.ctx_len, eng.scale,
-                                     max_pages_in_batch=eng.max_pages_in_batch,
-                                     pages_per_split=cfg.pages_per_split,
-                                     total_pages=eng.total_pages, workspace=eng.workspace,
-                                     out=out, seq_order=eng.seq_order)
+        paged.paged_decode_attention(q, pool, eng.table, eng.ctx_len, eng.scale, **plan)
 
     ms = {}
-    for name, pool in (("bf16", eng.kv[eng.attn_index[layer]]), ("8bit", pool8)):
-        run(pool)
-        run(pool)
+    bf16_pool = eng.kv[eng.attn_index[layer]]
+    for name, fn, pool in (("bf16", run, bf16_pool), ("bf16_two", run_two, bf16_pool),
+                           ("8bit", run, pool8)):
+        fn(pool)
+        fn(pool)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(rounds):
-            run(pool)
+            fn(pool)
         e1.record(stream)
         torch.cuda.synchronize()
         ms[name] = e0.elapsed_time(e1) / rounds
@@ -923,7 +923,8 @@ def kv8_attention_layer(wl, device, rounds: int = 5) -> dict:
     active = np.flatnonzero(eng.blocks.active)
     lengths = eng.blocks.lengths[active].astype(np.float64)
     n = len(lengths)
-    rows = {"bf16": cfg.kv_heads * D * 4, "8bit": cfg.kv_heads * (2 * D + 8 * D / 64)}
+    rows = {"bf16": cfg.kv_heads * D * 4, "bf16_two": cfg.kv_heads * D * 4,
+            "8bit": cfg.kv_heads * (2 * D + 8 * D / 64)}
     extra = n * cfg.q_heads * D * 4 + float(np.ceil(lengths / cfg.page_size).sum()) * 4
     nbytes = {key: float(lengths.sum()) * r + n * r + extra for key, r in rows.items()}
     peaks = measured_peaks()
@@ -931,6 +932,7 @@ def kv8_attention_layer(wl, device, rounds: int = 5) -> dict:
     return {"workload": f"one config-3 attention layer, {n} sequences, mean ctx "
                         f"{lengths.mean():.0f}, Hq{cfg.q_heads}/Hkv{cfg.kv_heads} D{D}",
             "bf16_ms": round(ms["bf16"], 4), "kv8_ms": round(ms["8bit"], 4),
+            "bf16_two_launch_ms": round(ms["bf16_two"], 4),
             "speedup": round(ms["bf16"] / ms["8bit"], 3),
             "bf16_gbs": round(gbs["bf16"], 1), "kv8_gbs": round(gbs["8bit"], 1),
             "kv8_frac": round(gbs["8bit"] / peaks["hbm_gbs"], 4),
@@ -983,14 +985,9 @@ def kv8_layer_standalone(args, device, rounds: int = 10) -> dict:
             row = Hkv * D * 4
 
         def run():
-            if pool.dtype == torch.bfloat16:
-                paged.paged_decode_attention_fused(q, kn, kn, slot_t, pool, bt, ctx, 1.0 / 16,
-                                                   max_pages_in_batch=width, total_pages=total,
-                                                   workspace=ws, out=out)
-                return
-            paged.kv_append(kn, kn, pool, slot_t)
-            paged.paged_decode_attention(q, pool, bt, ctx, 1.0 / 16, max_pages_in_batch=width,
-                                         total_pages=total, workspace=ws, out=out)
+            paged.append_and_attend(q, kn, kn, slot_t, pool, bt, ctx, 1.0 / 16,
+                                    max_pages_in_batch=width, total_pages=total, workspace=ws,
+                                    out=out)
 
         for _ in range(3):
             run()
@@ -1124,19 +1121,20 @@ def config2_attention(device, steps: int = 20, warmup: int = 3, rank: int = 0,
     stream = torch.cuda.current_stream(device)
 
     def step(s):
-        paged.paged_decode_attention_fused(q, kn, vn, slots_d[s], pool, table_d, ctx_d[s], 1 / 16,
-                                           max_pages_in_batch=max_pages,
-                                           total_pages=total_pages, workspace=ws, out=out,
-                                           seq_order=order)
+        paged.append_and_attend(q, kn, vn, slots_d[s], pool, table_d, ctx_d[s], 1 / 16,
+                                max_pages_in_batch=max_pages, total_pages=total_pages,
+                                workspace=ws, out=out, seq_order=order)
 
     for s in range(warmup):
         step(s)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    launched = paged.attention_launches
     e0.record(stream)
     for s in range(warmup, total):
         step(s)
     e1.record(stream)
+    launched = paged.attention_launches - launched
     torch.cuda.synchronize()
     from shellsmith_b200 import _capi
 
@@ -1161,7 +1159,8 @@ def config2_attention(device, steps: int = 20, warmup: int = 3, rank: int = 0,
         return None
     return {"n_gpus": world, "seqs_per_gpu": B, "ms_per_step": round(ms, 4),
             "tokens_per_s": round(B_all / (ms / 1e3), 1), "hbm_frac_per_gpu": round(gbs / peak, 4),
-            "launches_per_step": 1, "parity": parity_word(bad, checked)}
+            "launches_per_step": launched / steps,
+            "parity": parity_word(bad, checked)}
 
 
 def config1_prefill(device, steps: int = 5, warmup: int = 2) -> dict:
@@ -1474,7 +1473,7 @@ def config4_parity(shard, attn_in, world: int, rank: int) -> str:
         # rewrites the same appended rows), gathered by NCCL instead.
         plan = dict(max_pages_in_batch=shard.capacity, pages_per_split=shard.pages_per_split,
                     total_pages=shard.capacity, workspace=shard.workspace, packed=shard.packed)
-        if shard.peer_fused:
+        if shard.peer_fused or shard.num_splits > 1:
             paged.paged_decode_attention_packed(q, shard.kv[0], shard.table, shard.ctx, 1 / 16,
                                                 **plan)
         else:

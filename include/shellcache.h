@@ -398,12 +398,12 @@ int sc_attention_combine_exchange(const float* gathered, const unsigned int* fla
                                   int nparts, int rows, int D, sc_bf16* out, float* lse_out,
                                   void* stream);
 
-/* One attention layer of a decode step in one launch: the KV append of the
- * step's new token (sc_kv_append) folded into split-K decode attention
- * (sc_paged_decode_attention), with the split merge done by the last split of
- * each sequence to finish when num_splits <= 16 (no separate merge launch;
- * above 16 splits a separate merge kernel follows, as in
- * sc_paged_decode_attention).
+/* One attention layer of a decode step: the KV append of the step's new token
+ * (sc_kv_append) folded into split-K decode attention
+ * (sc_paged_decode_attention), one launch plus the split merge. The merge is
+ * the separate kernel of sc_paged_decode_attention when a sequence needs more
+ * than one split, or, with in_kernel_merge != 0 and num_splits <= 16, done by
+ * the last split of each sequence to finish (no merge launch).
  *
  * Replaces, as one kernel, the KV write of mlx_request_cache.py:59-63
  * (`OwnedKV.update_and_fetch`) and the per-request SDPA of mlx_decode.py:80-106
@@ -419,7 +419,7 @@ int sc_attention_combine_exchange(const float* gathered, const unsigned int* fla
  * sc_paged_decode_attention, with exactly one of out (bf16 rows, lse_out
  * optional) or packed ([B * Hq][D + 1] fp32, lse at index D, as
  * sc_paged_decode_attention_packed); out 8-byte aligned. num_splits > 1 needs
- * part_out and part_lse, and 1 < num_splits <= 16 also `counters`:
+ * part_out and part_lse, and the in-kernel merge also `counters`:
  * B * Hkv * ceil(Hq / Hkv / 8) uint32, zero before the first call; each launch
  * leaves them zero (after a DeviceFault, zero them again).
  * Launches that share counters or scratch must not overlap on the GPU. */
@@ -431,7 +431,7 @@ int sc_paged_decode_attention_fused(const sc_bf16* q, const sc_bf16* k_new,
                                     int P, int max_pages, int pages_per_split, int num_splits,
                                     float scale, float* part_out, float* part_lse,
                                     unsigned int* counters, sc_bf16* out, float* lse_out,
-                                    float* packed, void* stream);
+                                    float* packed, int in_kernel_merge, void* stream);
 
 /* Split-K decode attention that allocates nothing and takes no scratch.
  *

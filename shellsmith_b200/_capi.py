@@ -60,7 +60,7 @@ SIGNATURES = {
                                          _F, _P, _P, _P, _P],
     "sc_attention_combine_packed": [_P, _I, _I, _I, _P, _P, _P],
     "sc_paged_decode_attention_fused": [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _I,
-                                        _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P],
+                                        _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _I, _P],
     "sc_paged_decode_attention_noalloc": [_P, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                           _F, _P, _P, _P],
 }

@@ -421,10 +421,10 @@ __global__ void __launch_bounds__(NW * 32)
     // (no CTA waits for another) and leaves the counter at zero for the next launch.
     if (fa.merge && !final_here) {
       __shared__ int s_last;
-      __threadfence();  // this thread's partials are visible on the device ...
-      __syncthreads();  // ... before thread 0 counts the CTA in
+      __syncthreads();  // every thread's partials precede thread 0's release below
       if (threadIdx.x == 0) {
         unsigned int* ctr = fa.counters + ((size_t)b * Hkv + kvh) * HG + hg;
+        __threadfence();  // cumulative: the CTA's partials are visible before the count
         const int last = atomicAdd(ctr, 1u) == (unsigned int)(ns_seq - 1);
         if (last) {
           *ctr = 0u;
@@ -831,14 +831,15 @@ extern "C" int sc_paged_decode_attention_fused(
     sc_bf16* kv_pool, int64_t num_pages, const int32_t* block_table, const int32_t* ctx_len,
     const int32_t* seq_order, int B, int Hq, int Hkv, int D, int P, int max_pages,
     int pages_per_split, int num_splits, float scale, float* part_out, float* part_lse,
-    unsigned int* counters, sc_bf16* out, float* lse_out, float* packed, void* stream) {
+    unsigned int* counters, sc_bf16* out, float* lse_out, float* packed, int in_kernel_merge,
+    void* stream) {
   const char* name = "sc_paged_decode_attention_fused";
   SC_REQUIRE(k_new && v_new && slot_mapping, SC_ERR_INVALID, "%s: null pointer", name);
   SC_REQUIRE((out != nullptr) != (packed != nullptr), SC_ERR_INVALID,
              "%s: give exactly one of out and packed", name);
-  SC_REQUIRE(num_splits == 1 || num_splits > sc::kFusedMergeParts || counters != nullptr,
-             SC_ERR_INVALID, "%s: 1 < num_splits <= %d needs the arrival counters", name,
-             sc::kFusedMergeParts);
+  const bool merge = in_kernel_merge && num_splits > 1 && num_splits <= sc::kFusedMergeParts;
+  SC_REQUIRE(!merge || counters != nullptr, SC_ERR_INVALID,
+             "%s: the in-kernel merge needs the arrival counters", name);
   SC_REQUIRE(((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) ==
                  0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0,
              SC_ERR_INVALID, "%s: k_new and v_new must be 16-byte aligned, out 8-byte aligned",
@@ -849,7 +850,7 @@ extern "C" int sc_paged_decode_attention_fused(
   fa.slot_mapping = slot_mapping;
   fa.pool = reinterpret_cast<uint16_t*>(kv_pool);
   fa.counters = counters;
-  fa.merge = num_splits > 1 && num_splits <= sc::kFusedMergeParts;
+  fa.merge = merge ? 1 : 0;
   return sc::decode_entry(name, q, kv_pool, num_pages, block_table, ctx_len, seq_order, B, Hq,
                           Hkv, D, P, max_pages, pages_per_split, num_splits, scale, part_out,
                           part_lse, out, lse_out, packed, nullptr, stream, &fa);

@@ -7,10 +7,11 @@ attention layers run one request at a time (`_attention_rows`, 80-106). Here
 the caches are persistent device pools and one launch covers every row:
 
   GDN layer        sc_gdn_decode over all rows, state rows = sequence slots
-  attention layer  sc_paged_decode_attention_fused: the new token's KV append,
-                   split-K attention over each row's pages and the split merge,
-                   one launch (8-bit pages: sc_kv_append_q8 then
-                   sc_paged_decode_attention_q8)
+  attention layer  the new token's KV append and split-K attention over each
+                   row's pages: one launch (sc_paged_decode_attention_fused) when
+                   every sequence fits one split, else sc_kv_append,
+                   sc_paged_decode_attention and its merge (8-bit pages:
+                   sc_kv_append_q8 then sc_paged_decode_attention_q8)
 
 A sequence's slot is its batch row, its block-table row and its GDN state row,
 so no gather/scatter of caches happens per step; inactive rows are skipped by
@@ -363,26 +364,15 @@ class HybridCacheEngine:
         return launched
 
     def attention_layer(self, layer: int, q, k_new, v_new, out) -> None:
-        """Append each row's new token and attend over its pages: one launch on bf16
-        pages (sc_paged_decode_attention_fused), append + split-K (+ merge) on
-        8-bit pages."""
-        pool = self.kv[self.attn_index[layer]]
-        if pool.dtype == torch.bfloat16:
-            paged.paged_decode_attention_fused(q, k_new, v_new, self.slot_map, pool, self.table,
-                                               self.ctx_len, self.scale,
-                                               max_pages_in_batch=self.max_pages_in_batch,
-                                               pages_per_split=self.cfg.pages_per_split,
-                                               total_pages=self.total_pages,
-                                               workspace=self.workspace, out=out,
-                                               seq_order=self.seq_order, sms=self.cfg.sms)
-            return
-        paged.kv_append(k_new, v_new, pool, self.slot_map)
-        paged.paged_decode_attention(q, pool, self.table, self.ctx_len, self.scale,
-                                     max_pages_in_batch=self.max_pages_in_batch,
-                                     pages_per_split=self.cfg.pages_per_split,
-                                     total_pages=self.total_pages,
-                                     workspace=self.workspace, out=out,
-                                     seq_order=self.seq_order, sms=self.cfg.sms)
+        """Append each row's new token and attend over its pages (paged.append_and_attend:
+        one launch when the batch fits one split per sequence, else append, split-K and
+        merge)."""
+        paged.append_and_attend(q, k_new, v_new, self.slot_map, self.kv[self.attn_index[layer]],
+                                self.table, self.ctx_len, self.scale,
+                                max_pages_in_batch=self.max_pages_in_batch,
+                                pages_per_split=self.cfg.pages_per_split,
+                                total_pages=self.total_pages, workspace=self.workspace, out=out,
+                                seq_order=self.seq_order, sms=self.cfg.sms)
 
     def decode_step(self, inputs: dict, outputs: dict) -> None:
         """Run every layer's cache work for the staged token of each active row.

@@ -4,10 +4,11 @@ The reference runs one device; a 128k-token context there is one concatenated
 cache read by one SDPA (mlx_decode.py:94-103). Here each rank holds a
 contiguous range of the sequence's pages in its own pool, and per attention
 layer and decode token:
-  1.+2. every rank computes its split-K partial over its own pages, normalised
-     fp32 output and lse packed [Hq, D + 1], in one launch that also appends the
-     new token's K/V on the rank that owns the tail page
-     (sc_paged_decode_attention_fused with a packed output);
+  1.+2. the rank that owns the tail page appends the new token's K/V, and every
+     rank computes its split-K partial over its own pages: normalised fp32 output
+     and lse packed [Hq, D + 1] (sc_paged_decode_attention_packed, or, when the
+     rank's pages are one split, sc_paged_decode_attention_fused with the append
+     folded in);
   3. the ranks exchange the packed partials (Hq (D + 1) 4 bytes = 16.4 KB per
      rank at Hq 16, D 256) -- the one exchange of the path: either each rank
      stores its block straight into every peer's receive buffer over NVLink and
@@ -281,15 +282,13 @@ class ShardedSequence:
             self.workspace = paged.AttentionWorkspace(1, self.q_heads, self.head_dim,
                                                       max(1, self.num_splits), device=q.device)
         if self.world == 1 and all_gather is None:
-            # One rank holds every page: one launch appends the token, attends and merges
-            # the splits into the final rows.
-            paged.paged_decode_attention_fused(q, k_new, v_new, self.slot, pool, self.table,
-                                               self.ctx, scale, max_pages_in_batch=self.capacity,
-                                               pages_per_split=self.pages_per_split,
-                                               total_pages=self.capacity,
-                                               workspace=self.workspace,
-                                               out=self.out.view(1, self.q_heads,
-                                                                 self.head_dim))
+            # One rank holds every page: append the token and attend; the split merge
+            # writes the final rows.
+            paged.append_and_attend(q, k_new, v_new, self.slot, pool, self.table, self.ctx,
+                                    scale, max_pages_in_batch=self.capacity,
+                                    pages_per_split=self.pages_per_split,
+                                    total_pages=self.capacity, workspace=self.workspace,
+                                    out=self.out.view(1, self.q_heads, self.head_dim))
             return self.out
         if self.peer is not None and self.peer_fused and self.num_splits > 1:
             paged.kv_append(k_new, v_new, pool, self.slot)
@@ -301,12 +300,17 @@ class ShardedSequence:
                                     parity=parity)
             self.peer.merge(self.out, self.epoch, layer + 1, parity)
             return self.out
-        # This rank's packed partial: append, attend and merge the splits in one launch.
-        paged.paged_decode_attention_fused(q, k_new, v_new, self.slot, pool, self.table, self.ctx,
-                                           scale, max_pages_in_batch=self.capacity,
-                                           pages_per_split=self.pages_per_split,
-                                           total_pages=self.capacity, workspace=self.workspace,
-                                           packed=self.packed)
+        # This rank's packed partial: the append folded into the attention launch when it
+        # is one split, else the append, the split-K kernel and the merge.
+        plan = dict(max_pages_in_batch=self.capacity, pages_per_split=self.pages_per_split,
+                    total_pages=self.capacity, workspace=self.workspace)
+        if self.num_splits == 1:
+            paged.paged_decode_attention_fused(q, k_new, v_new, self.slot, pool, self.table,
+                                               self.ctx, scale, packed=self.packed, **plan)
+        else:
+            paged.kv_append(k_new, v_new, pool, self.slot)
+            paged.paged_decode_attention_packed(q, pool, self.table, self.ctx, scale,
+                                                packed=self.packed, **plan)
         if self.peer is not None:
             parity = (layer + 1) & 1   # the parity of this call's epoch (even layer count)
             self.peer.put_and_wait(self.packed, self.epoch, layer + 1, parity)

@@ -82,6 +82,7 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, kv_pool: torch.Tensor,
     name = "sc_kv_append_q8" if kv_pool.dtype == torch.uint8 else "sc_kv_append"
     _capi.call(name, ptr(k), ptr(v), ptr(kv_pool), ptr(slot_mapping), ntok, hkv, dim, page,
                num_pages, stream_of(kv_pool))
+    _count(1 if ntok else 0)
 
 
 def kv_gather_q8(kv_pool: torch.Tensor, slot_mapping: torch.Tensor) -> tuple:
@@ -125,9 +126,15 @@ def kv_copy_pages(kv_pool: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -
 
 _SM_COUNT: dict = {}
 
-# Merge kernels launched by paged_decode_attention so far: a call launches one only when
-# some sequence spans more than one split. Benchmarks read it to count their launches.
-merge_launches = 0
+# Kernels launched so far by the attention entry points of this module (appends, split-K
+# kernels and their merges; a merge runs only when some sequence spans more than one
+# split). Benchmarks read the difference over a timed region to count their launches.
+attention_launches = 0
+
+
+def _count(n: int) -> None:
+    global attention_launches
+    attention_launches += n
 
 
 def sm_count(device) -> int:
@@ -182,6 +189,19 @@ def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
     else:
         pps = 64
     return pps, max(1, math.ceil(max(1, max_pages_in_batch) / pps))
+
+
+def decode_plan(batch: int, q_heads: int, kv_heads: int, max_pages_in_batch: int,
+                pages_per_split: int | None, total_pages: int | None, sms: int,
+                q8: bool = False) -> tuple:
+    """(pages_per_split, num_splits) that paged_decode_attention and its fused form pick
+    for a batch: bf16 pages three waves, splits up to 1,024 pages and at least 128
+    while half a wave remains; 8-bit pages two waves up to 256 pages."""
+    groups = kv_heads * ((q_heads // kv_heads + 7) // 8)
+    return split_plan(max_pages_in_batch, pages_per_split,
+                      None if total_pages is None else total_pages * groups, sms,
+                      waves=2 if q8 else 3, cap=256 if q8 else 1024,
+                      rows=None if q8 else batch * groups, min_pages=None if q8 else 128)
 
 
 class AttentionWorkspace:
@@ -241,13 +261,9 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     if d != dim or hq % hkv or block_table.shape[0] != B or ctx_len.shape[0] != B:
         raise ValueError("paged_decode_attention: inconsistent shapes")
     max_pages = block_table.shape[1]
-    groups = hkv * ((hq // hkv + 7) // 8)
     q8 = kv_pool.dtype == torch.uint8
-    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
-                             None if total_pages is None else total_pages * groups,
-                             sms or sm_count(q.device), waves=2 if q8 else 3,
-                             cap=256 if q8 else 1024,
-                             rows=None if q8 else B * groups, min_pages=None if q8 else 128)
+    pps, nsplit = decode_plan(B, hq, hkv, max_pages_in_batch or max_pages, pages_per_split,
+                              total_pages, sms or sm_count(q.device), q8=q8)
     if out is None:
         out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)
     require_cuda("out", out, torch.bfloat16, 3)
@@ -267,9 +283,7 @@ def paged_decode_attention(q: torch.Tensor, kv_pool: torch.Tensor, block_table: 
     _capi.call(name, ptr(q), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len),
                ptr(seq_order), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
                ptr(part_out), ptr(part_lse), ptr(out), ptr(lse_out), stream_of(q))
-    if nsplit > 1:
-        global merge_launches
-        merge_launches += 1
+    _count(1 + (nsplit > 1) if B else 0)
     return out
 
 
@@ -284,10 +298,14 @@ def paged_decode_attention_fused(q: torch.Tensor, k_new: torch.Tensor, v_new: to
                                  lse_out: torch.Tensor | None = None,
                                  packed: torch.Tensor | None = None,
                                  seq_order: torch.Tensor | None = None,
-                                 sms: int | None = None) -> torch.Tensor:
-    """kv_append of each row's new token followed by paged_decode_attention, as one
-    launch (sc_paged_decode_attention_fused): the splits of a sequence merge
-    themselves, the last one to finish combining them.
+                                 sms: int | None = None,
+                                 in_kernel_merge: bool = False) -> torch.Tensor:
+    """kv_append of each row's new token folded into paged_decode_attention
+    (sc_paged_decode_attention_fused): one launch, plus the merge kernel when a
+    sequence spans several splits. in_kernel_merge: the last split of each sequence
+    merges them instead (at most 16 splits), which measured slower on B200 (the
+    arrival round trip keeps every split CTA resident longer than the separate merge
+    costs), so it is off by default.
 
     k_new, v_new [B, Hkv, D] bf16 and slot_mapping [B] int64 (< 0: no append) are
     the step's new tokens; ctx_len counts them. With `packed` ([B * Hq, D + 1] fp32)
@@ -309,11 +327,8 @@ def paged_decode_attention_fused(q: torch.Tensor, k_new: torch.Tensor, v_new: to
             or slot_mapping.shape[0] != B):
         raise ValueError("paged_decode_attention_fused: inconsistent shapes")
     max_pages = block_table.shape[1]
-    groups = hkv * ((hq // hkv + 7) // 8)
-    pps, nsplit = split_plan(max_pages_in_batch or max_pages, pages_per_split,
-                             None if total_pages is None else total_pages * groups,
-                             sms or sm_count(q.device), waves=3, cap=1024, rows=B * groups,
-                             min_pages=128)
+    pps, nsplit = decode_plan(B, hq, hkv, max_pages_in_batch or max_pages, pages_per_split,
+                              total_pages, sms or sm_count(q.device))
     if packed is None:
         if out is None:
             out = torch.empty((B, hq, dim), dtype=torch.bfloat16, device=q.device)
@@ -336,12 +351,49 @@ def paged_decode_attention_fused(q: torch.Tensor, k_new: torch.Tensor, v_new: to
             workspace = AttentionWorkspace(B, hq, dim, nsplit, device=q.device)
         part_out, part_lse = workspace.views(B, nsplit)
         counters = workspace.counters
+    merge_in_kernel = bool(in_kernel_merge) and 1 < nsplit <= 16
     _capi.call("sc_paged_decode_attention_fused", ptr(q), ptr(k_new), ptr(v_new),
                ptr(slot_mapping), ptr(kv_pool), num_pages, ptr(block_table), ptr(ctx_len),
                ptr(seq_order), B, hq, hkv, dim, page, max_pages, pps, nsplit, float(scale),
                ptr(part_out), ptr(part_lse), ptr(counters), ptr(out), ptr(lse_out), ptr(packed),
-               stream_of(q))
+               int(merge_in_kernel), stream_of(q))
+    _count(1 + (nsplit > 1 and not merge_in_kernel) if B else 0)
     return packed if packed is not None else out
+
+
+def append_and_attend(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                      slot_mapping: torch.Tensor, kv_pool: torch.Tensor,
+                      block_table: torch.Tensor, ctx_len: torch.Tensor, scale: float, *,
+                      max_pages_in_batch: int | None = None,
+                      pages_per_split: int | None = None, total_pages: int | None = None,
+                      workspace: AttentionWorkspace | None = None,
+                      out: torch.Tensor | None = None, seq_order: torch.Tensor | None = None,
+                      sms: int | None = None) -> torch.Tensor:
+    """One decode step of an attention layer: append each row's new token, then attend.
+
+    When every sequence fits one split (the plan has one), the append is folded into
+    the attention launch (paged_decode_attention_fused: one kernel). Otherwise
+    kv_append, the split-K kernel and the merge run as three launches: on B200 that
+    sequence measured faster than the fused kernel with its splits merged either in
+    the kernel or by the merge kernel (config 2 shares of 8-64 sequences: 1.5-6 %).
+    8-bit pools always take the two kernels of their own.
+    """
+    if kv_pool.dtype == torch.bfloat16:
+        num_pages, hkv, page, dim = _pool_dims(kv_pool)
+        _, nsplit = decode_plan(q.shape[0], q.shape[1], hkv,
+                                max_pages_in_batch or block_table.shape[1], pages_per_split,
+                                total_pages, sms or sm_count(q.device))
+        if nsplit == 1:
+            return paged_decode_attention_fused(
+                q, k_new, v_new, slot_mapping, kv_pool, block_table, ctx_len, scale,
+                max_pages_in_batch=max_pages_in_batch, pages_per_split=pages_per_split,
+                total_pages=total_pages, workspace=workspace, out=out, seq_order=seq_order,
+                sms=sms)
+    kv_append(k_new, v_new, kv_pool, slot_mapping)
+    return paged_decode_attention(q, kv_pool, block_table, ctx_len, scale,
+                                  max_pages_in_batch=max_pages_in_batch,
+                                  pages_per_split=pages_per_split, total_pages=total_pages,
+                                  workspace=workspace, out=out, seq_order=seq_order, sms=sms)
 
 
 def attention_combine(part_out: torch.Tensor, part_lse: torch.Tensor,
@@ -396,6 +448,7 @@ def paged_decode_attention_packed(q: torch.Tensor, kv_pool: torch.Tensor,
     _capi.call("sc_paged_decode_attention_packed", ptr(q), ptr(kv_pool), num_pages,
                ptr(block_table), ptr(ctx_len), B, hq, hkv, dim, page, max_pages, pps, nsplit,
                float(scale), ptr(part_out), ptr(part_lse), ptr(packed), stream_of(q))
+    _count(1 + (nsplit > 1) if B else 0)
     return packed
 
 

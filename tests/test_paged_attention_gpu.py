@@ -314,10 +314,12 @@ def _fused_case(rng, cuda, lengths, hq, hkv, D, num_pages, width):
     return pool, q, table, k_new, v_new, torch.from_numpy(slots).to(cuda)
 
 
-# 64 one-page splits merge in the separate kernel; 16 (the in-kernel cap) and 8 merge in
-# the last split of each sequence; 64 pages per split is one split.
+# 64 one-page splits always merge in the separate kernel; with in_kernel_merge, 16 (the
+# in-kernel cap) and 8 splits merge in the last split of each sequence; 64 pages per
+# split is one split.
+@pytest.mark.parametrize("in_kernel_merge", [False, True])
 @pytest.mark.parametrize("pages_per_split", [1, 4, 8, 64])
-def test_fused_layer_equals_append_then_attention(cuda, pages_per_split):
+def test_fused_layer_equals_append_then_attention(cuda, pages_per_split, in_kernel_merge):
     """Append + split-K (+ the merge) against kv_append followed by the unfused
     attention: the pool bit for bit, the output within tolerance of the oracle over the
     appended context, the counters back at zero, and a repeated call (counters reused)
@@ -338,7 +340,7 @@ def test_fused_layer_equals_append_then_attention(cuda, pages_per_split):
     lse = torch.empty(len(lengths) * hq, dtype=torch.float32, device=cuda)
     got = paged.paged_decode_attention_fused(q, k_new, v_new, slots, pool, bt, ctx, 1 / 16,
                                              pages_per_split=pages_per_split, workspace=ws,
-                                             lse_out=lse)
+                                             lse_out=lse, in_kernel_merge=in_kernel_merge)
     torch.cuda.synchronize()
     assert torch.equal(pool, ref_pool)
     assert torch.count_nonzero(ws.counters) == 0
@@ -349,7 +351,8 @@ def test_fused_layer_equals_append_then_attention(cuda, pages_per_split):
     np.testing.assert_allclose(got.float().cpu().numpy(), want_out.float().cpu().numpy(),
                                rtol=RTOL, atol=ATOL)
     again = paged.paged_decode_attention_fused(q, k_new, v_new, slots, pool, bt, ctx, 1 / 16,
-                                               pages_per_split=pages_per_split, workspace=ws)
+                                               pages_per_split=pages_per_split, workspace=ws,
+                                               in_kernel_merge=in_kernel_merge)
     torch.cuda.synchronize()
     assert torch.equal(again, got) and torch.count_nonzero(ws.counters) == 0
     _capi.check_device()
