@@ -735,13 +735,10 @@ def run_ours(args, world, rank, local):
 
 
 SHARDED_WORKLOADS = (
-    "config3_strong: config 3's 256 sequences in all (the 1-GPU draw) dealt longest first in "
-    "snake order, 256/N per GPU, same step and churn; config2_attention: 64 sequences "
-    "U[1k,32k], append + split-K attention, dealt the same way; config4_long_sequence: one "
-    "131,072-token sequence, its KV pages split over the N GPUs, partials exchanged over "
-    "NVLink. tokens_per_s = all GPUs; hbm_frac_per_gpu of measured; parity: rows checked "
-    "against float64 on every rank (config 4: the peer exchange also equals an NCCL "
-    "all-gather bit for bit)")
+    "config3_strong: config 3's 256 sequences in all, 256/N per GPU; config2_attention: 64 "
+    "seqs U[1k,32k] dealt over the GPUs; config4_long_sequence: one 131,072-token sequence, "
+    "KV pages split over the GPUs, partials exchanged over NVLink. tokens_per_s: all GPUs; "
+    "fractions of measured HBM; parity: float64 checks on every rank")
 
 
 def config3_strong(args, wl, world, rank, step, warmup: int = 2) -> dict | None:
@@ -760,12 +757,18 @@ def config3_strong(args, wl, world, rank, step, warmup: int = 2) -> dict | None:
     wl.reset(strong_share(args, rank, world))
     torch.cuda.synchronize()
     barrier(world)
-    events = []
-    for _ in range(args.steps):
-        step(events)
+    events, layer_events = [], []
+    for i in range(args.steps):
+        step(events, layer_events if i % 2 == 1 else None)
     torch.cuda.synchronize()
     _capi.check_device()
     decode_s = sum(e[0].elapsed_time(e[1]) for e in events) / 1e3
+    # Per-layer rates on the sampled steps: what limits the strong-scaling curve.
+    n_gdn = len(wl.cfg.gdn_layers)
+    attn_s = sum(a.elapsed_time(b) for is_attn, a, b, _ in layer_events if is_attn) / 1e3
+    gdn_s = sum(a.elapsed_time(b) for is_attn, a, b, _ in layer_events if not is_attn) / 1e3
+    attn_b = sum(eng.step_bytes(le[3])["attention_per_layer"] for le in layer_events if le[0])
+    gdn_b = sum(eng.step_bytes(le[3])["gdn"] / n_gdn for le in layer_events if not le[0])
     tokens = sum(e[4] for e in events)
     nbytes = sum(eng.step_bytes(e[5])["total"] for e in events)
     ctx = np.concatenate([e[5] for e in events]).astype(np.float64)
@@ -773,6 +776,9 @@ def config3_strong(args, wl, world, rank, step, warmup: int = 2) -> dict | None:
     decode_max = max_over_ranks(decode_s, world)
     tokens_all = sum_over_ranks(tokens, world)
     gbs_per_gpu = sum_over_ranks(nbytes, world) / world / decode_max / 1e9
+    peak = measured_peaks()["hbm_gbs"]
+    attn_frac = -max_over_ranks(-(attn_b / max(attn_s, 1e-9) / 1e9 / peak), world)
+    gdn_frac = -max_over_ranks(-(gdn_b / max(gdn_s, 1e-9) / 1e9 / peak), world)
     ctx_sum, ctx_n = sum_over_ranks(float(ctx.sum()), world), sum_over_ranks(ctx.size, world)
     bad, checked = step_parity(wl)
     bad, checked = sum_over_ranks(bad, world), sum_over_ranks(checked, world)
@@ -782,7 +788,8 @@ def config3_strong(args, wl, world, rank, step, warmup: int = 2) -> dict | None:
     return {"n_gpus": world, "seqs_per_gpu": seqs, "steps": args.steps,
             "ms_per_step": round(decode_max * 1e3 / args.steps, 3),
             "tokens_per_s": round(tokens_all / decode_max, 1),
-            "hbm_frac_per_gpu": round(gbs_per_gpu / measured_peaks()["hbm_gbs"], 4),
+            "hbm_frac_per_gpu": round(gbs_per_gpu / peak, 4),
+            "layer_frac_min_rank": {"gdn": round(gdn_frac, 3), "attention": round(attn_frac, 3)},
             "mean_ctx": round(ctx_sum / ctx_n), "parity": parity_word(bad, checked)}
 
 

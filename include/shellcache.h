@@ -152,7 +152,10 @@ int sc_gdn_chunk_prefill(const sc_bf16* q, const sc_bf16* k, const sc_bf16* v,
  * position [B] int32: absolute position t of each row's token (>= 0)
  * state, state_slot, num_slots: as sc_gdn_decode (fp32 state, -1 skips a row)
  * out  [B, Hv*128] bf16: rms_norm(y, norm_w, eps) * silu(z)
- * Launches one 2-CTA cluster per (row, value head). */
+ * Launches one 2-CTA cluster per (row, value head). Experimental: on B200 this
+ * one-launch form is slower than the three-kernel sc_gdn_decode_glue (0.24
+ * against 0.18 ms per config-3 layer: the front and the cluster handshake cut
+ * the state bytes each CTA keeps in flight); the engine uses the glue. */
 int sc_gdn_decode_fused(const sc_bf16* qkv, const sc_bf16* z, const sc_bf16* a,
                         const sc_bf16* b, const sc_bf16* conv_w, const float* A_log,
                         const float* dt_bias, const sc_bf16* norm_w, float eps,

@@ -77,3 +77,19 @@ def test_split_plan_follows_the_device_sm_count():
         paged.split_plan(*args, **kw)
     assert paged.split_plan(100, 16) == (16, 7)          # an explicit size needs no count
     assert HybridConfig().sms is None and HybridConfig(sms=132).sms == 132
+
+
+def test_strong_share_partitions_the_one_gpu_draw():
+    """config3_strong: the 1-GPU draw of 256 sequences split over N ranks, 256/N each,
+    disjoint and complete, with nearly equal context sums."""
+    from types import SimpleNamespace
+
+    args = SimpleNamespace(batch=256, min_len=512, max_len=16384)
+    draw = np.random.default_rng(bench.SEED).integers(512, 16385, size=256)
+    for world in (1, 2, 4, 8):
+        shares = [bench.strong_share(args, r, world) for r in range(world)]
+        assert all(len(s) == 256 // world for s in shares)
+        assert sorted(np.concatenate(shares).tolist()) == sorted(draw.tolist())
+        sums = np.array([s.sum() for s in shares], float)
+        assert sums.max() / sums.min() < 1.05
+    assert np.array_equal(np.sort(bench.strong_share(args, 0, 1)), np.sort(draw))
