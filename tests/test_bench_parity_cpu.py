@@ -1,7 +1,7 @@
 """The bench's in-run parity checks (no GPU): its float64 torch restatements of the
 paged-pool read, split attention and the GDN token step agree with the CPU oracle, and
 they reject a planted error. The bench runs them on the device after its timed windows,
-on every rank, so the multi-GPU lines carry a parity verdict."""
+on every rank, so the multi-GPU lines carry a parity result."""
 
 import math
 
