@@ -300,14 +300,17 @@ __global__ void __launch_bounds__(NW * 32)
       }
     }
 
-    float sc4[4] = {0.f, 0.f, 0.f, 0.f};
+    // Two accumulators over the K steps halve the dependent MMA chain of the scores.
+    float sc4[4] = {0.f, 0.f, 0.f, 0.f}, sc4b[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int kk = 0; kk < S::KSTEPS; ++kk) {
       const int chunk = 2 * kk + (mi >> 1);
       uint32_t a0, a1, a2, a3;
       ldsm_x4(kbase + tk * S::ROW_BYTES + ((chunk ^ (tk & 7)) << 4), a0, a1, a2, a3);
-      mma_bf16_16816(sc4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+      mma_bf16_16816((kk & 1) ? sc4b : sc4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sc4[e] += sc4b[e];
 
     const int tok0 = page_tok + (lane >> 2);
     const bool lo_ok = tok0 < L, hi_ok = tok0 + 8 < L;
@@ -501,6 +504,21 @@ __global__ void __launch_bounds__(kCombineThreads)
   const float* lse = pl + (size_t)row * l_row;
   const float* o = po + (size_t)row * o_row;
   constexpr int kDims = 4;  // dims per thread (D <= 512)
+  // Up to kPrefetch parts: this thread's values are loaded into registers before the
+  // weights are made, so those loads overlap the lse loads and the block reductions
+  // (the sums take them in the same order as the general loop).
+  constexpr int kPrefetch = 16;
+  const bool prefetched = ns <= kPrefetch;
+  float pv[kDims][kPrefetch];
+  if (prefetched) {
+#pragma unroll
+    for (int j = 0; j < kDims; ++j) {
+      const int d = threadIdx.x + j * kCombineThreads;
+#pragma unroll
+      for (int s = 0; s < kPrefetch; ++s)
+        pv[j][s] = (s < ns && d < D) ? o[(size_t)s * o_part + d] : 0.f;
+    }
+  }
   float acc[kDims];
 #pragma unroll
   for (int j = 0; j < kDims; ++j) acc[j] = 0.f;
@@ -526,7 +544,13 @@ __global__ void __launch_bounds__(kCombineThreads)
       const int d = threadIdx.x + j * kCombineThreads;
       if (d < D) {
         float a = acc[j] * rescale;
-        for (int s = 0; s < n; ++s) a = fmaf(w[s], o[(size_t)(s0 + s) * o_part + d], a);
+        if (prefetched) {  // one window: s0 = 0, n = ns
+#pragma unroll
+          for (int s = 0; s < kPrefetch; ++s)
+            if (s < n) a = fmaf(w[s], pv[j][s], a);
+        } else {
+          for (int s = 0; s < n; ++s) a = fmaf(w[s], o[(size_t)(s0 + s) * o_part + d], a);
+        }
         acc[j] = a;
       }
     }
@@ -583,6 +607,20 @@ __global__ void __launch_bounds__(kCombineThreads)
   }
   const float* lse = pl + (size_t)row * l_row;
   const float* o = po + (size_t)row * o_row;
+  constexpr int kStride = kCombineThreads / 32;
+  // Up to kPrefetch parts per warp (kStride * kPrefetch parts in all), this lane's
+  // values are loaded into registers before the weights are made, so the part loads
+  // overlap the lse loads and the block reductions; the sums below take them in the
+  // same order as the loads of the general loop.
+  constexpr int kPrefetch = 32;
+  const bool prefetched = ns <= kStride * kPrefetch;
+  const int cnt_w = ns > warp ? (ns - warp + kStride - 1) / kStride : 0;  // parts of this warp
+  float pv[kPrefetch];
+  if (prefetched) {
+#pragma unroll
+    for (int i = 0; i < kPrefetch; ++i)
+      pv[i] = (i < cnt_w && d < D) ? o[(size_t)(warp + kStride * i) * o_part + d] : 0.f;
+  }
   float acc = 0.f, M = -CUDART_INF_F, wsum = 0.f;
   for (int s0 = 0; s0 < ns; s0 += kCombineWindow) {
     const int n = min(kCombineWindow, ns - s0);
@@ -601,9 +639,25 @@ __global__ void __launch_bounds__(kCombineThreads)
     wsum = wsum * rescale + block_sum(part, red);
     M = Mn;
     float a = acc * rescale;
-    if (d < D) {
+    if (d < D && prefetched) {  // one window: s0 = 0, n = ns
+      float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int done = 0;
+#pragma unroll
+      for (int i = 0; i < kPrefetch; i += 4) {
+        if (i + 3 < cnt_w) {
+          a = fmaf(w[warp + kStride * i], pv[i], a);
+          a1 = fmaf(w[warp + kStride * (i + 1)], pv[i + 1], a1);
+          a2 = fmaf(w[warp + kStride * (i + 2)], pv[i + 2], a2);
+          a3 = fmaf(w[warp + kStride * (i + 3)], pv[i + 3], a3);
+          done = i + 4;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kPrefetch; ++i)
+        if (i >= done && i < cnt_w) a = fmaf(w[warp + kStride * i], pv[i], a);
+      a += (a1 + a2) + a3;
+    } else if (d < D) {
       // Four parts in flight per warp: the loads do not wait on the sum chain.
-      constexpr int kStride = kCombineThreads / 32;
       float a1 = 0.f, a2 = 0.f, a3 = 0.f;
       int s = warp;
       for (; s + 3 * kStride < n; s += 4 * kStride) {
