@@ -33,6 +33,10 @@ namespace {
 
 constexpr int kPage = 16;
 constexpr int kHeadsPerTile = 8;
+#ifndef SC_ATTN_QK_ACC
+#define SC_ATTN_QK_ACC 2
+#endif
+constexpr int kQkAcc = SC_ATTN_QK_ACC;  // independent score accumulators per page
 
 template <int D>
 struct AttnShape {
@@ -300,17 +304,22 @@ __global__ void __launch_bounds__(NW * 32)
       }
     }
 
-    // Two accumulators over the K steps halve the dependent MMA chain of the scores.
-    float sc4[4] = {0.f, 0.f, 0.f, 0.f}, sc4b[4] = {0.f, 0.f, 0.f, 0.f};
+    // kQkAcc accumulators over the K steps cut the dependent MMA chain of the scores.
+    float sca[kQkAcc][4];
+#pragma unroll
+    for (int x = 0; x < kQkAcc; ++x) sca[x][0] = sca[x][1] = sca[x][2] = sca[x][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < S::KSTEPS; ++kk) {
       const int chunk = 2 * kk + (mi >> 1);
       uint32_t a0, a1, a2, a3;
       ldsm_x4(kbase + tk * S::ROW_BYTES + ((chunk ^ (tk & 7)) << 4), a0, a1, a2, a3);
-      mma_bf16_16816((kk & 1) ? sc4b : sc4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+      mma_bf16_16816(sca[kk % kQkAcc], a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
     }
+    float sc4[4] = {sca[0][0], sca[0][1], sca[0][2], sca[0][3]};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) sc4[e] += sc4b[e];
+    for (int x = 1; x < kQkAcc; ++x)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc4[e] += sca[x][e];
 
     const int tok0 = page_tok + (lane >> 2);
     const bool lo_ok = tok0 < L, hi_ok = tok0 + 8 < L;
