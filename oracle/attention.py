@@ -6,13 +6,17 @@ Restated from (paths relative to the shellsmith project root):
               j <= query_offset + i, kv head of query head h is h // group,
               query_offset defaults to keys - queries.
   quantize_q8 the 8-bit cache of the cache_precision="8bit" option
-              (src/studio_compute/inference.py:87-94, mlx-vlm
-              QuantizedKVCache: groups of 64 along D, scale and bias per
-              group, w = scale * code + bias). The library's own rounding is
-              not in the reference tree, so this is the build's stated rule
-              (parity unpinned): scale = bf16((max - min) / 255),
-              bias = bf16(min), code = clamp(rint((w - bias) / scale), 0, 255),
-              0 when scale == 0, each op in float32.
+              (src/studio_compute/inference.py:87-94, mlx-vlm 0.7.4
+              QuantizedKVCache over mlx 0.32.3 mx.quantize: groups of 64 along
+              D, scale and bias per group, w = scale * code + bias). The
+              library's code is not in the reference tree; this restates the
+              affine rule MLX documents for mx.quantize (scale = (max - min) /
+              (2^bits - 1), bias = min, code = round((w - bias) / scale)) with
+              scale and bias stored in the cache's bf16 dtype:
+              scale = bf16((max - min) / 255), bias = bf16(min),
+              code = clamp(rint((w - bias) / scale), 0, 255), 0 when
+              scale == 0, each op in float32. Parity with the library itself is
+              unpinned (it cannot run here).
   The split-K partials, their combine and the paged-pool layout have no
   counterpart in the reference (it runs one request's SDPA at a time); they
   restate the algebra softmax(x) = sum_s e^{lse_s - M} softmax_s(x) / sum_s
