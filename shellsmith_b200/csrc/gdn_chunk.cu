@@ -50,7 +50,8 @@ constexpr uint32_t OFF_XYL = 131072;    // lo
 constexpr uint32_t OFF_WH = 147456;     // W^T hi, later (U^T r) hi [128 rows][128 B]
 constexpr uint32_t OFF_WL = 163840;     // lo
 constexpr uint32_t OFF_KQ2 = 180224;    // second [K | Q] buffer: chunk c uses KQ[c & 1]
-constexpr uint32_t OFF_SMALL = 212992;  // lg, beta, decay, r [64] floats; barriers; TMEM base
+constexpr uint32_t OFF_SMALL = 212992;  // two gate sets [lg, beta, decay, r, inv][64] floats;
+                                        // barriers; TMEM base
 // Aliases used while a chunk is prepared (regions free at that time):
 constexpr uint32_t OFF_MH = OFF_SH;            // m hi [128 rows (0-63 used)][128 B]
 constexpr uint32_t OFF_ML = OFF_SH + 16384;    // m lo
@@ -62,7 +63,8 @@ constexpr int kAStride = 68;                   // fp32 row stride of A (conflict
 constexpr int kTStride = 40;                   // fp32 row stride of the inverse scratch
 constexpr int kMaxRankedSeqs = 4096;           // longer varlen batches keep their order
 static_assert(OFF_TBUF + 32 * kTStride * 4 <= OFF_XYH, "inverse scratch overlaps [X;Y]");
-constexpr uint32_t SMEM_BYTES = OFF_SMALL + 5 * 64 * 4 + 64 + 1024;  // + 1024 alignment slack
+constexpr int kGateSet = 5 * 64;  // floats of one chunk's gate arrays
+constexpr uint32_t SMEM_BYTES = OFF_SMALL + 2 * kGateSet * 4 + 64 + 1024;  // + alignment slack
 
 // TMEM columns (512 allocated).
 constexpr uint32_t T_S = 0, T_P = 128, T_KK = 256, T_Y = 320;
@@ -111,12 +113,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  float* s_lg = reinterpret_cast<float*>(sm + OFF_SMALL);  // log2 prefix sums of the gates
-  float* s_beta = s_lg + 64;
-  float* s_decay = s_beta + 64;
-  float* s_r = s_decay + 64;
-  float* s_inv = s_r + 64;  // 2^(lg_0 - lg_j): the column factor of the decay ratios
-  uint64_t* bar_kq = reinterpret_cast<uint64_t*>(s_inv + 64);  // [2]: K/Q tiles of a buffer
+  // Gate arrays of a chunk (set c & 1): log2 prefix sums lg, beta, decay = 2^lg,
+  // r = 2^(lg_63 - lg), inv = 2^(lg_0 - lg) (the column factor of the decay ratios).
+  // The next chunk's set is made while this chunk's G12 runs.
+  float* gate_sets = reinterpret_cast<float*>(sm + OFF_SMALL);
+  uint64_t* bar_kq = reinterpret_cast<uint64_t*>(gate_sets + 2 * kGateSet);  // [2]: K/Q tiles
   uint64_t* bar_v = bar_kq + 2;                               // V tile
   uint64_t* bar_mma = bar_v + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_mma + 1);
@@ -226,14 +227,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int half = 0; half < 2; ++half)
       tc::tma_load_3d(sm + OFF_V + half * 8192, &tm_v, half * 64, h, t0, bar_v);
   };
-  // Gates of the next chunk are read from global memory a chunk ahead.
-  float g_next = 1.f, b_next = 0.f;
-  auto fetch_gates = [&](int chunk) {  // threads 0-63
+  // Gates: warp 2 reads a chunk's g and beta (tokens 2 lane, 2 lane + 1) a chunk
+  // before it makes that chunk's gate set, which it does while the previous chunk's
+  // G12 runs (chunk 0's before the loop).
+  float gn0 = 1.f, gn1 = 1.f, bn0 = 0.f, bn1 = 0.f;
+  auto fetch_gates = [&](int chunk) {  // warp 2
     const int n = min(kC, len - chunk * kC);
-    const bool on = tid < n;
-    const size_t at = (size_t)(start + chunk * kC + tid) * Hv + h;
-    g_next = on ? g[at] : 1.f;
-    b_next = on ? beta[at] : 0.f;
+    const int t0 = 2 * lane_id;
+    const size_t at = (size_t)(start + chunk * kC + t0) * Hv + h;
+    gn0 = t0 < n ? g[at] : 1.f;
+    bn0 = t0 < n ? beta[at] : 0.f;
+    gn1 = t0 + 1 < n ? g[at + Hv] : 1.f;
+    bn1 = t0 + 1 < n ? beta[at + Hv] : 0.f;
+  };
+  auto make_gates = [&](float* gs) {  // warp 2: one inclusive scan over token pairs
+    const float lg0 = log2f(fminf(fmaxf(gn0, 1e-6f), 1.f));
+    const float lg1 = log2f(fminf(fmaxf(gn1, 1e-6f), 1.f));
+    const float pair = lg0 + lg1;
+    float incl = pair;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane_id >= off) incl += y;
+    }
+    const float p0 = (incl - pair) + lg0, p1 = p0 + lg1;
+    const float last = __shfl_sync(0xffffffffu, incl, 31);
+    const float first = __shfl_sync(0xffffffffu, p0, 0);
+    const int t0 = 2 * lane_id;
+    gs[t0] = p0;
+    gs[t0 + 1] = p1;
+    gs[64 + t0] = bn0;
+    gs[64 + t0 + 1] = bn1;
+    gs[128 + t0] = exp2f(p0);
+    gs[128 + t0 + 1] = exp2f(p1);
+    gs[192 + t0] = exp2f(last - p0);
+    gs[192 + t0 + 1] = exp2f(last - p1);
+    gs[256 + t0] = exp2f(first - p0);
+    gs[256 + t0 + 1] = exp2f(first - p1);
   };
   if (tid == 0) {
     issue_kq(0);
@@ -242,7 +272,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   pending_loads = 1 | 4;
   kq_last[0] = 0;
   v_last = 0;
-  if (tid < 64) fetch_gates(0);
+  if (warp == 2) {
+    fetch_gates(0);
+    make_gates(gate_sets);
+    if (1 < nchunks) fetch_gates(1);
+  }
   // `extra` = 0 from any thread fails the step (thread 0's wait for the next
   // chunk's K/Q tiles before it queued that chunk's G0).
   auto wait_mma = [&](int extra = 1) {
@@ -275,26 +309,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int valid = min(kC, len - c * kC);
 
     const uint32_t off_kq = (c & 1) ? OFF_KQ2 : OFF_KQ;
-    // ---- (1) gates (log2 domain) from the values fetched a chunk ahead.
-    if (tid < 64) {
-      s_beta[tid] = b_next;
-      float lg = log2f(fminf(fmaxf(g_next, 1e-6f), 1.f));
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, lg, off);
-        if (lane_id >= off) lg += y;
-      }
-      s_lg[tid] = lg;
-    }
-    __syncthreads();
-    if (tid >= 32 && tid < 64) s_lg[tid] += s_lg[31];
-    __syncthreads();
-    if (tid < 64) {
-      s_decay[tid] = exp2f(s_lg[tid]);
-      s_r[tid] = exp2f(s_lg[63] - s_lg[tid]);
-      s_inv[tid] = exp2f(s_lg[0] - s_lg[tid]);
-      if (c + 1 < nchunks) fetch_gates(c + 1);
-    }
+    // ---- (1) this chunk's gate set was made before (the barrier below publishes it).
+    float* s_lg = gate_sets + (c & 1) * kGateSet;
+    float* s_beta = s_lg + 64;
+    float* s_decay = s_lg + 128;
+    float* s_r = s_lg + 192;
+    float* s_inv = s_lg + 256;
     {
       const int done = mbar_wait_bounded(&bar_kq[c & 1], (c >> 1) & 1, status) ? 1 : 0;
       ok = __syncthreads_and(done && ok);
@@ -555,6 +575,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::tmem_wait_st();
       tc::fence_before();
+    }
+    // The next chunk's gate set, by warp 2 while G12 runs (its barrier publishes it).
+    if (warp == 2 && c + 1 < nchunks) {
+      make_gates(gate_sets + ((c + 1) & 1) * kGateSet);
+      if (c + 2 < nchunks) fetch_gates(c + 2);
     }
     if (!wait_mma()) break;
 
