@@ -321,13 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       pending_loads &= ~(1 << (c & 1));
     }
-    // The other K/Q buffer was last read by the previous chunk's GS, which has
-    // completed: fetch the next chunk's tiles into it now.
-    if (c + 1 < nchunks) {
-      if (tid == 0) issue_kq(c + 1);
-      pending_loads |= 1 << ((c + 1) & 1);
-      kq_last[(c + 1) & 1] = c + 1;
-    }
 
     // ---- (2) G0: [K;Q] K^T -> TMEM cols T_KK. Chunk 0 issues it here; every
     //          later chunk's G0 went out with the previous chunk's GS and is done.
@@ -581,6 +574,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       make_gates(gate_sets + ((c + 1) & 1) * kGateSet);
       if (c + 2 < nchunks) fetch_gates(c + 2);
     }
+    // The next chunk's K/Q tiles, by warp 3 while G12 runs (off the MMA-issuing
+    // thread): the other K/Q buffer was last read by the previous chunk's GS.
+    if (c + 1 < nchunks) {
+      if (tid == 96) issue_kq(c + 1);
+      pending_loads |= 1 << ((c + 1) & 1);
+      kq_last[(c + 1) & 1] = c + 1;
+    }
     if (!wait_mma()) break;
 
     // ---- (8) W^T row i for tokens [32 hf, +32); zero those U^T columns;
@@ -616,8 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     tc::fence_before();
     __syncthreads();
-    if (c + 1 < nchunks) {  // every thread has read this chunk's V
-      if (tid == 0) issue_v(c + 1);
+    if (c + 1 < nchunks) {  // every thread has read this chunk's V; warp 3 loads the next
+      if (tid == 96) issue_v(c + 1);
       pending_loads |= 4;
       v_last = c + 1;
     }
