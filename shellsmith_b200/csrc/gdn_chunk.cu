@@ -120,7 +120,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_kq = reinterpret_cast<uint64_t*>(gate_sets + 2 * kGateSet);  // [2]: K/Q tiles
   uint64_t* bar_v = bar_kq + 2;                               // V tile
   uint64_t* bar_mma = bar_v + 1;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* bar_g0 = bar_mma + 1;  // the next chunk's G0, committed ahead of G34
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_g0 + 1);
   float* Xf = reinterpret_cast<float*>(sm + OFF_AMAT);  // A, inverted in place into X
   float* Tbuf = reinterpret_cast<float*>(sm + OFF_TBUF);
 
@@ -176,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar_kq[1], 1);
     mbar_init(bar_v, 1);
     mbar_init(bar_mma, 1);
+    mbar_init(bar_g0, 1);
     fence_mbar_init();
   }
   if (warp == 0) tc::tmem_alloc(s_tmem, 512);
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc::tmem_wait_st();
 
-  uint32_t mma_phase = 0;
+  uint32_t mma_phase = 0, g0_phase = 0;
   int ok = 1;
   int pending_mma = 0;
   // Loads in flight, for the drain on the error path: bit b = K/Q buffer b,
@@ -303,28 +305,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
   };
 
+  // A/m of a chunk from its KK^T / QK^T (TMEM cols T_KK) and gate set gs: A rows
+  // (lanes 0-63) in fp32 smem, m rows (lanes 64-127) as bf16 hi/lo; this warp owns
+  // columns [32 hf, 32 hf + 32). Both land in the S tiles' region, free from the
+  // end of the previous chunk's G12 until the S split that follows Y.
+  auto build_am = [&](const float* gs) {
+    float v[32];
+    tc::tmem_ld32(tmem + lane + T_KK + 32 * hf, v);
+    const int t = row & 63;
+    const float lgt = gs[t];
+    // R_tj = 2^(lg_t - lg_j). When the chunk's decay spans < 2^-100, write it
+    // as 2^(lg_t - lg_0) * 2^(lg_0 - lg_j): both factors stay in range and the
+    // per-element exponentials become one multiply.
+    float rr[32];
+    if (gs[0] - gs[63] < 100.f) {  // uniform over the CTA
+      const float at = exp2f(lgt - gs[0]);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) rr[e] = at * gs[256 + 32 * hf + e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) rr[e] = exp2f(lgt - gs[32 * hf + e]);
+    }
+    if (quarter < 2) {
+      const float bt = gs[64 + t];
+      float4* arow = reinterpret_cast<float4*>(Xf + t * kAStride + 32 * hf);
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        float a[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 32 * hf + 4 * j4 + e;
+          a[e] = j < t ? bt * rr[4 * j4 + e] * v[4 * j4 + e] : 0.f;
+        }
+        arow[j4] = make_float4(a[0], a[1], a[2], a[3]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int j = 32 * hf + e;
+        v[e] = j <= t ? rr[e] * v[e] : 0.f;
+      }
+      store_chunks_hilo(sm + OFF_MH, sm + OFF_ML, t, 4 * hf, v);
+    }
+  };
+
 #pragma unroll 1
   for (int c = 0; c < nchunks; ++c) {
     const int tok0 = start + c * kC;
     const int valid = min(kC, len - c * kC);
 
     const uint32_t off_kq = (c & 1) ? OFF_KQ2 : OFF_KQ;
-    // ---- (1) this chunk's gate set was made before (the barrier below publishes it).
+    // ---- (1) this chunk's gate set, made while the previous chunk's G12 ran (or
+    //          before the loop) and published by a barrier since.
     float* s_lg = gate_sets + (c & 1) * kGateSet;
     float* s_beta = s_lg + 64;
     float* s_decay = s_lg + 128;
     float* s_r = s_lg + 192;
-    float* s_inv = s_lg + 256;
-    {
-      const int done = mbar_wait_bounded(&bar_kq[c & 1], (c >> 1) & 1, status) ? 1 : 0;
+    // ---- (2) G0 and A/m. Chunk 0 makes them here; every later chunk's went
+    //          out during the previous chunk's G34 and are in place (thread 0
+    //          waited for this chunk's K/Q tiles before it issued that G0).
+    if (c == 0) {
+      const int done = mbar_wait_bounded(&bar_kq[0], 0, status) ? 1 : 0;
       ok = __syncthreads_and(done && ok);
       if (!ok) break;
-      pending_loads &= ~(1 << (c & 1));
-    }
-
-    // ---- (2) G0: [K;Q] K^T -> TMEM cols T_KK. Chunk 0 issues it here; every
-    //          later chunk's G0 went out with the previous chunk's GS and is done.
-    if (c == 0) {
       if (tid == 0) {
         tc::fence_after();
         issue_g0(0);
@@ -332,49 +375,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pending_mma = 1;
       if (!wait_mma()) break;
+      build_am(s_lg);
+      __syncthreads();
+    }
+    pending_loads &= ~(1 << (c & 1));
+    // The other K/Q buffer was last read by the previous chunk's GS, which has
+    // completed: warp 3 fetches the next chunk's tiles into it.
+    if (c + 1 < nchunks) {
+      if (tid == 96) issue_kq(c + 1);
+      pending_loads |= 1 << ((c + 1) & 1);
+      kq_last[(c + 1) & 1] = c + 1;
     }
 
-    // ---- (3) A rows (lanes 0-63) in fp32 smem and m rows (lanes 64-127) as
-    //          bf16 hi/lo; this warp owns columns [32 hf, 32 hf + 32).
-    {
-      float v[32];
-      tc::tmem_ld32(tmem + lane + T_KK + 32 * hf, v);
-      const int t = row & 63;
-      const float lgt = s_lg[t];
-      // R_tj = 2^(lg_t - lg_j). When the chunk's decay spans < 2^-100, write it
-      // as 2^(lg_t - lg_0) * 2^(lg_0 - lg_j): both factors stay in range and the
-      // per-element exponentials become one multiply.
-      float rr[32];
-      if (s_lg[0] - s_lg[63] < 100.f) {  // uniform over the CTA
-        const float at = exp2f(lgt - s_lg[0]);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) rr[e] = at * s_inv[32 * hf + e];
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) rr[e] = exp2f(lgt - s_lg[32 * hf + e]);
-      }
-      if (quarter < 2) {
-        const float bt = s_beta[t];
-        float4* arow = reinterpret_cast<float4*>(Xf + t * kAStride + 32 * hf);
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float a[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = 32 * hf + 4 * j4 + e;
-            a[e] = j < t ? bt * rr[4 * j4 + e] * v[4 * j4 + e] : 0.f;
-          }
-          arow[j4] = make_float4(a[0], a[1], a[2], a[3]);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = 32 * hf + e;
-          v[e] = j <= t ? rr[e] * v[e] : 0.f;
-        }
-        store_chunks_hilo(sm + OFF_MH, sm + OFF_ML, t, 4 * hf, v);
-      }
-    }
     __syncthreads();
 
     // ---- (4) X = (I + A)^-1 in place: 8 x 8 diagonal blocks by substitution,
@@ -574,13 +586,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       make_gates(gate_sets + ((c + 1) & 1) * kGateSet);
       if (c + 2 < nchunks) fetch_gates(c + 2);
     }
-    // The next chunk's K/Q tiles, by warp 3 while G12 runs (off the MMA-issuing
-    // thread): the other K/Q buffer was last read by the previous chunk's GS.
-    if (c + 1 < nchunks) {
-      if (tid == 96) issue_kq(c + 1);
-      pending_loads |= 1 << ((c + 1) & 1);
-      kq_last[(c + 1) & 1] = c + 1;
-    }
     if (!wait_mma()) break;
 
     // ---- (8) W^T row i for tokens [32 hf, +32); zero those U^T columns;
@@ -622,9 +627,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       v_last = c + 1;
     }
 
-    // ---- (9) G34: W^T [X;Y]^T accumulated -> U^T | O^T.
+    // ---- (9) The next chunk's G0 (its own commit), then G34: W^T [X;Y]^T
+    //          accumulated -> U^T | O^T.
+    int g0_ok = 1;
     if (tid == 0) {
       tc::fence_after();
+      if (c + 1 < nchunks) {
+        if (mbar_wait_bounded(&bar_kq[(c + 1) & 1], ((c + 1) >> 1) & 1, status))
+          issue_g0(c + 1);
+        else
+          g0_ok = 0;
+        tc::commit(bar_g0);  // arrives even without the G0, so no thread waits in vain
+      }
       constexpr uint32_t id = tc::idesc_bf16(128, 128, false, false);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
@@ -639,7 +653,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::commit(bar_mma);
     }
     pending_mma = 1;
-    if (!wait_mma()) break;
+    // ---- (9b) the next chunk's A/m while G34 runs (G34 writes the T_P columns
+    //           and reads the W and [X;Y] tiles; the S tiles are free).
+    if (c + 1 < nchunks) {
+      const int g0_done = mbar_wait_bounded(bar_g0, g0_phase, status) ? 1 : 0;
+      g0_phase ^= 1;
+      tc::fence_after();
+      if (g0_done) build_am(gate_sets + ((c + 1) & 1) * kGateSet);
+      g0_ok &= g0_done;
+    }
+    if (!wait_mma(g0_ok)) break;
 
     // ---- (10) (U^T r) hi/lo -> smem for tokens [32 hf, +32).
     {
@@ -654,7 +677,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // ---- (11) GS: S += (U^T r) K, K as an MN-major operand (dk halves 16 KiB apart).
-    int g0_ok = 1;
     if (tid == 0) {
       tc::fence_after();
       constexpr uint32_t id = tc::idesc_bf16(128, 128, false, true);
@@ -664,19 +686,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WH) + ks * 32), kd, id, true);
         tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WL) + ks * 32), kd, id, true);
       }
-      // The next chunk's K/Q tiles were fetched a chunk ahead: its G0 joins
-      // this commit, so the next chunk starts with KK^T / QK^T in TMEM.
-      if (c + 1 < nchunks) {
-        if (mbar_wait_bounded(&bar_kq[(c + 1) & 1], ((c + 1) >> 1) & 1, status))
-          issue_g0(c + 1);
-        else
-          g0_ok = 0;
-      }
       tc::commit(bar_mma);
     }
     pending_mma = 1;
-    // ---- (10b) O^T -> out (bf16) for tokens [32 hf, +32) while GS and the next
-    //            G0 run (they write the T_S and T_KK columns only).
+    // ---- (10b) O^T -> out (bf16) for tokens [32 hf, +32) while GS runs (it
+    //            writes the T_S columns only).
     {
       float o[32];
       tc::tmem_ld32(tmem + lane + T_P + 64 + 32 * hf, o);
@@ -685,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = 0; e < 32; ++e)
         if (32 * hf + e < valid) orow[(size_t)e * Hv * kD] = f_to_bf16(o[e]);
     }
-    if (!wait_mma(g0_ok)) break;
+    if (!wait_mma()) break;
   }
 
   if (!ok) {
