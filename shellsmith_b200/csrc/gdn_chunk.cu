@@ -68,6 +68,7 @@ constexpr uint32_t SMEM_BYTES = OFF_SMALL + 2 * kGateSet * 4 + 64 + 1024;  // + 
 
 // TMEM columns (512 allocated).
 constexpr uint32_t T_S = 0, T_P = 128, T_KK = 256, T_Y = 320;
+constexpr uint32_t T_SH = 384, T_SL = 448;  // S hi / lo as bf16 pairs: the A operand of G12
 
 __device__ __forceinline__ void store_chunks_hilo(uint8_t* hi, uint8_t* lo, int row, int c0,
                                                   const float* x) {
@@ -529,19 +530,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part, xc);
       store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part + 1, xc + 8);
     }
+    // ---- (6) S hi/lo (A of G12) -> TMEM cols T_SH / T_SL, also while Y runs (Y
+    //          writes the T_Y columns; S was last written by the previous chunk's
+    //          GS, and its G12 has finished reading T_SH / T_SL). Columns
+    //          [64 hf, +64) of S -> bf16 pair columns [32 hf, +32).
+#pragma unroll 1
+    for (int q = 0; q < 2; ++q) {
+      float v[32];
+      tc::tmem_ld32(tmem + lane + T_S + 64 * hf + 32 * q, v);
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        hi[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+        lo[e] = pack_bf16x2(v[2 * e] - bf16_lo(hi[e]), v[2 * e + 1] - bf16_hi(hi[e]));
+      }
+      tc::tmem_st16(tmem + lane + T_SH + 32 * hf + 16 * q, hi);
+      tc::tmem_st16(tmem + lane + T_SL + 32 * hf + 16 * q, lo);
+    }
+    tc::tmem_wait_st();
     if (!wait_mma()) break;
     if (quarter < 2) {
       float y[32];
       tc::tmem_ld32(tmem + lane + T_Y + 32 * hf, y);
       store_chunks_hilo(sm + OFF_XYH, sm + OFF_XYL, 64 + row, 4 * hf, y);
-    }
-
-    // ---- (6) S hi/lo -> smem (A of G12). Columns [64 hf, +64).
-#pragma unroll 1
-    for (int q = 0; q < 2; ++q) {
-      float v[32];
-      tc::tmem_ld32(tmem + lane + T_S + 64 * hf + 32 * q, v);
-      store_chunks_hilo(sm + OFF_SH + hf * 16384, sm + OFF_SL + hf * 16384, row, 4 * q, v);
     }
     fence_proxy_async_smem();
     tc::fence_before();
@@ -557,10 +568,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            const uint32_t a = smem_addr(sm + (part ? OFF_SL : OFF_SH) + kb * 16384) + ks * 32;
+            const uint32_t a = tmem + (part ? T_SL : T_SH) + 32 * kb + 8 * ks;
             const uint32_t bb = smem_addr(sm + off_kq + kb * 16384) + ks * 32;
-            tc::mma_bf16(tmem + T_P, tc::desc_kmajor(a), tc::desc_kmajor(bb), id,
-                         (part | kb | ks) != 0);
+            tc::mma_bf16_ts(tmem + T_P, a, tc::desc_kmajor(bb), id, (part | kb | ks) != 0);
           }
       tc::commit(bar_mma);
     }
