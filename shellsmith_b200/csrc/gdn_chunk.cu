@@ -66,6 +66,20 @@ static_assert(OFF_TBUF + 32 * kTStride * 4 <= OFF_XYH, "inverse scratch overlaps
 constexpr int kGateSet = 5 * 64;  // floats of one chunk's gate arrays
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + 2 * kGateSet * 4 + 64 + 1024;  // + alignment slack
 
+// 32 fp32 values of this thread's TMEM lane as bf16 hi + lo pair columns: 16
+// columns at hi_col and 16 at lo_col (an A operand of a K = 32 slice).
+__device__ __forceinline__ void tmem_store_hilo(uint32_t hi_col, uint32_t lo_col,
+                                                const float* x) {
+  uint32_t hi[16], lo[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    hi[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
+    lo[e] = pack_bf16x2(x[2 * e] - bf16_lo(hi[e]), x[2 * e + 1] - bf16_hi(hi[e]));
+  }
+  tc::tmem_st16(hi_col, hi);
+  tc::tmem_st16(lo_col, lo);
+}
+
 // TMEM columns (512 allocated).
 constexpr uint32_t T_S = 0, T_P = 128, T_KK = 256, T_Y = 320;
 constexpr uint32_t T_SH = 384, T_SL = 448;  // S hi / lo as bf16 pairs: the A operand of G12
@@ -538,14 +552,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int q = 0; q < 2; ++q) {
       float v[32];
       tc::tmem_ld32(tmem + lane + T_S + 64 * hf + 32 * q, v);
-      uint32_t hi[16], lo[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        hi[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
-        lo[e] = pack_bf16x2(v[2 * e] - bf16_lo(hi[e]), v[2 * e + 1] - bf16_hi(hi[e]));
-      }
-      tc::tmem_st16(tmem + lane + T_SH + 32 * hf + 16 * q, hi);
-      tc::tmem_st16(tmem + lane + T_SL + 32 * hf + 16 * q, lo);
+      tmem_store_hilo(tmem + lane + T_SH + 32 * hf + 16 * q, tmem + lane + T_SL + 32 * hf + 16 * q,
+                      v);
     }
     tc::tmem_wait_st();
     if (!wait_mma()) break;
@@ -598,8 +606,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!wait_mma()) break;
 
-    // ---- (8) W^T row i for tokens [32 hf, +32); zero those U^T columns;
-    //          decay * P2^T in the matching O^T columns.
+    // ---- (8) W^T row i for tokens [32 hf, +32) -> TMEM cols T_SH / T_SL as
+    //          bf16 hi/lo (the A operand of G34; G12 has finished reading S
+    //          there); zero those U^T columns; decay * P2^T in the matching O^T
+    //          columns.
     {
       const int done = mbar_wait_bounded(bar_v, c & 1, status) ? 1 : 0;
       ok = __syncthreads_and(done && ok);
@@ -617,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float vti = bf16_to_f(*reinterpret_cast<const uint16_t*>(vt + tc::swz(t, iv)));
         p[e] = s_beta[t] * (vti - s_decay[t] * p[e]);
       }
-      store_chunks_hilo(sm + OFF_WH, sm + OFF_WL, row, 4 * hf, p);
+      tmem_store_hilo(tmem + lane + T_SH + 16 * hf, tmem + lane + T_SL + 16 * hf, p);
       float z[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) z[e] = 0.f;
@@ -652,13 +662,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id = tc::idesc_bf16(128, 128, false, false);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        const uint64_t wh = tc::desc_kmajor(smem_addr(sm + OFF_WH) + ks * 32);
-        const uint64_t wl = tc::desc_kmajor(smem_addr(sm + OFF_WL) + ks * 32);
+        const uint32_t wh = tmem + T_SH + 8 * ks, wl = tmem + T_SL + 8 * ks;
         const uint64_t xh = tc::desc_kmajor(smem_addr(sm + OFF_XYH) + ks * 32);
         const uint64_t xl = tc::desc_kmajor(smem_addr(sm + OFF_XYL) + ks * 32);
-        tc::mma_bf16(tmem + T_P, wh, xh, id, true);
-        tc::mma_bf16(tmem + T_P, wh, xl, id, true);
-        tc::mma_bf16(tmem + T_P, wl, xh, id, true);
+        tc::mma_bf16_ts(tmem + T_P, wh, xh, id, true);
+        tc::mma_bf16_ts(tmem + T_P, wh, xl, id, true);
+        tc::mma_bf16_ts(tmem + T_P, wl, xh, id, true);
       }
       tc::commit(bar_mma);
     }
@@ -674,15 +683,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!wait_mma(g0_ok)) break;
 
-    // ---- (10) (U^T r) hi/lo -> smem for tokens [32 hf, +32).
+    // ---- (10) (U^T r) hi/lo -> TMEM cols T_SH / T_SL (the A operand of GS; G34
+    //           has finished reading W there) for tokens [32 hf, +32).
     {
       float u[32];
       tc::tmem_ld32(tmem + lane + T_P + 32 * hf, u);
 #pragma unroll
       for (int e = 0; e < 32; ++e) u[e] *= s_r[32 * hf + e];
-      store_chunks_hilo(sm + OFF_WH, sm + OFF_WL, row, 4 * hf, u);
+      tmem_store_hilo(tmem + lane + T_SH + 16 * hf, tmem + lane + T_SL + 16 * hf, u);
+      tc::tmem_wait_st();
     }
-    fence_proxy_async_smem();
     tc::fence_before();
     __syncthreads();
 
@@ -693,8 +703,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
         const uint64_t kd = tc::desc_mnmajor(smem_addr(sm + off_kq) + ks * 2048, 16384);
-        tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WH) + ks * 32), kd, id, true);
-        tc::mma_bf16(tmem + T_S, tc::desc_kmajor(smem_addr(sm + OFF_WL) + ks * 32), kd, id, true);
+        tc::mma_bf16_ts(tmem + T_S, tmem + T_SH + 8 * ks, kd, id, true);
+        tc::mma_bf16_ts(tmem + T_S, tmem + T_SL + 8 * ks, kd, id, true);
       }
       tc::commit(bar_mma);
     }
