@@ -12,14 +12,16 @@
 //   W = beta (V - decay (K S^T)),  U = X W,  O = decay (Q S^T) + (m X) W,
 //   S <- decay_63 S + (r U)^T K.
 //
-// B200 mapping. One CTA (4 warps) owns one (sequence, value head) and walks its
+// B200 mapping. One CTA (8 warps) owns one (sequence, value head) and walks its
 // chunks in order; the 128 x 128 fp32 state lives in tensor memory the whole
 // time. Everything is computed transposed, so TMEM lane = value row i = thread:
 //   G0  [K;Q] K^T            -> A (fp32 smem), m        M128 N64  K128
-//   Y   m X                  -> rows 64.. of [X;Y]      M128 N64  K64
-//   G12 S [K;Q]^T            -> P1^T | P2^T             M128 N128 K128
-//   G34 W^T [X;Y]^T (+= 0 | decay P2^T) -> U^T | O^T    M128 N128 K64
-//   GS  (U^T r) K  (+= decay_63 S)                      M128 N128 K64
+//   Y   m X                  -> rows 64.. of [X;Y]      M128 N64  K64   A in TMEM
+//   G12 S [K;Q]^T            -> P1^T | P2^T             M128 N128 K128  A in TMEM
+//   G34 W^T [X;Y]^T (+= 0 | decay P2^T) -> U^T | O^T    M128 N128 K64   A in TMEM
+//   GS  (U^T r) K  (+= decay_63 S)                      M128 N128 K64   A in TMEM
+// The A operands in TMEM (m, S, W^T, (U^T r), as bf16 hi/lo pair columns) are
+// written by the threads that own their lanes; B operands come from shared memory.
 // Q/K/V chunk tiles arrive by TMA (128-byte swizzle, no multicast); the
 // unit-lower inverse solves its 8 x 8 diagonal blocks column-per-thread in fp32
 // and builds the off-diagonal blocks from them (warp mma.sync tf32 tiles, each
@@ -40,31 +42,31 @@ constexpr int kC = 64;    // chunk length
 constexpr int kD = 128;   // key and value width
 constexpr int kThreads = 256;  // 8 warps: two per TMEM lane quarter
 
-// Shared memory plan (byte offsets from a 1024-aligned base).
+// Shared memory plan (byte offsets from a 1024-aligned base). The MMA operands
+// that are built per TMEM lane (S, W, U r and m as bf16 hi/lo) stay in tensor
+// memory; shared memory holds the TMA tiles, the B operands built from X and Y,
+// and the fp32 scratch of the inverse.
 constexpr uint32_t OFF_KQ = 0;          // [2 dk halves][K rows 0-63 | Q rows 64-127][128 B]
-constexpr uint32_t OFF_V = 32768;       // [2 dv halves][64 rows][128 B]
-constexpr uint32_t OFF_SH = 49152;      // S hi  [2 dk blocks][128 rows][128 B]
-constexpr uint32_t OFF_SL = 81920;      // S lo
-constexpr uint32_t OFF_XYH = 114688;    // [X rows 0-63 | Y rows 64-127][128 B] hi
-constexpr uint32_t OFF_XYL = 131072;    // lo
-constexpr uint32_t OFF_WH = 147456;     // W^T hi, later (U^T r) hi [128 rows][128 B]
-constexpr uint32_t OFF_WL = 163840;     // lo
-constexpr uint32_t OFF_KQ2 = 180224;    // second [K | Q] buffer: chunk c uses KQ[c & 1]
-constexpr uint32_t OFF_SMALL = 212992;  // two gate sets [lg, beta, decay, r, inv][64] floats;
-                                        // barriers; TMEM base
-// Aliases used while a chunk is prepared (regions free at that time):
-constexpr uint32_t OFF_MH = OFF_SH;            // m hi [128 rows (0-63 used)][128 B]
-constexpr uint32_t OFF_ML = OFF_SH + 16384;    // m lo
-constexpr uint32_t OFF_AMAT = OFF_SH + 32768;  // A (strict lower) fp32 [64][68], then X
-constexpr uint32_t OFF_TBUF = OFF_SH + 50176;  // inverse scratch fp32 [32][kTStride]
-constexpr uint32_t OFF_XTH = OFF_WH;           // X^T rows hi [64 rows][128 B]
-constexpr uint32_t OFF_XTL = OFF_WL;           // lo
-constexpr int kAStride = 68;                   // fp32 row stride of A (conflict-free float4 rows)
-constexpr int kTStride = 40;                   // fp32 row stride of the inverse scratch
-constexpr int kMaxRankedSeqs = 4096;           // longer varlen batches keep their order
-static_assert(OFF_TBUF + 32 * kTStride * 4 <= OFF_XYH, "inverse scratch overlaps [X;Y]");
+constexpr uint32_t OFF_KQ2 = 32768;     // second [K | Q] buffer: chunk c uses KQ[c & 1]
+constexpr uint32_t OFF_V = 65536;       // [2 dv halves][64 rows][128 B]
+constexpr uint32_t OFF_XYH = 81920;     // [X rows 0-63 | Y rows 64-127][128 B] hi
+constexpr uint32_t OFF_XYL = 98304;     // lo
+constexpr uint32_t OFF_XTH = 114688;    // X^T rows hi [64 rows][128 B]
+constexpr uint32_t OFF_XTL = 122880;    // lo
+constexpr uint32_t OFF_AMAT = 131072;   // A (strict lower) fp32 [64][kAStride], then X
+constexpr int kAStride = 68;            // fp32 row stride of A (conflict-free float4 rows)
+constexpr uint32_t OFF_TBUF = OFF_AMAT + 64 * kAStride * 4;  // inverse scratch [32][kTStride]
+constexpr int kTStride = 40;            // fp32 row stride of the inverse scratch
+constexpr uint32_t OFF_SMALL = OFF_TBUF + 32 * kTStride * 4;  // two gate sets
+                                        // [lg, beta, decay, r, inv][64] floats; barriers; TMEM base
+constexpr int kMaxRankedSeqs = 4096;    // longer varlen batches keep their order
+// The varlen ranking stages cu_seqlens in the A scratch before the first chunk.
+static_assert((kMaxRankedSeqs + 2) * 4 <= 64 * kAStride * 4, "ranking scratch exceeds A");
 constexpr int kGateSet = 5 * 64;  // floats of one chunk's gate arrays
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + 2 * kGateSet * 4 + 64 + 1024;  // + alignment slack
+// Each CTA allocates all 512 TMEM columns, so two must never share an SM: the
+// shared memory plan alone keeps a second one off (228 KB per SM).
+static_assert(2 * SMEM_BYTES > 228 * 1024, "a second CTA per SM would wait for TMEM");
 
 // 32 fp32 values of this thread's TMEM lane as bf16 hi + lo pair columns: 16
 // columns at hi_col and 16 at lo_col (an A operand of a K = 32 slice).
@@ -147,11 +149,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Varlen batches run longest sequence first: when the grid is more than one
   // wave, the CTAs left for the second wave belong to the shortest sequences.
   // Block row b takes the sequence of rank b (length descending, index
-  // ascending), ranked here from cu_seqlens staged in the state-operand region,
-  // which the chunk loop first writes long after.
+  // ascending), ranked here from cu_seqlens staged in the A scratch, which the
+  // chunk loop first writes long after.
   if (cu_seqlens != nullptr && (int)(gridDim.x / Hv) <= kMaxRankedSeqs) {
     const int nseq = (int)(gridDim.x / Hv);
-    int* s_cu = reinterpret_cast<int*>(sm + OFF_SH);
+    int* s_cu = reinterpret_cast<int*>(sm + OFF_AMAT);
     for (int i = threadIdx.x; i <= nseq; i += blockDim.x) s_cu[i] = cu_seqlens[i];
     __syncthreads();
     for (int i = threadIdx.x; i < nseq; i += blockDim.x) {
@@ -360,8 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = 32 * hf + e;
         v[e] = j <= t ? rr[e] * v[e] : 0.f;
       }
-      store_chunks_hilo(sm + OFF_MH, sm + OFF_ML, t, 4 * hf, v);
+      tmem_store_hilo(tmem + lane + T_Y + 16 * hf, tmem + lane + T_Y + 32 + 16 * hf, v);
+      tc::tmem_wait_st();
     }
+    tc::fence_before();
   };
 
 #pragma unroll 1
@@ -510,25 +514,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     __syncthreads();
 
-    // ---- (5) Y = m X -> TMEM cols T_Y (lanes 0-63); rows -> [X;Y] rows 64-127.
+    // ---- (5) Y = m X, m from TMEM cols T_Y (lanes 64-127: hi, then lo) ->
+    //          TMEM cols T_KK (lanes 64-127; KK^T was read by A/m and the next G0
+    //          comes after G34); rows -> [X;Y] rows 64-127. Lanes 0-63 of the
+    //          product are not used.
     if (tid == 0) {
       tc::fence_after();
       constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        const uint64_t mh = tc::desc_kmajor(smem_addr(sm + OFF_MH) + ks * 32);
-        const uint64_t ml = tc::desc_kmajor(smem_addr(sm + OFF_ML) + ks * 32);
+        const uint32_t mh = tmem + T_Y + 8 * ks, ml = tmem + T_Y + 32 + 8 * ks;
         const uint64_t xh = tc::desc_kmajor(smem_addr(sm + OFF_XTH) + ks * 32);
         const uint64_t xl = tc::desc_kmajor(smem_addr(sm + OFF_XTL) + ks * 32);
-        tc::mma_bf16(tmem + T_Y, mh, xh, id, ks != 0);
-        tc::mma_bf16(tmem + T_Y, mh, xl, id, true);
-        tc::mma_bf16(tmem + T_Y, ml, xh, id, true);
+        tc::mma_bf16_ts(tmem + T_KK, mh, xh, id, ks != 0);
+        tc::mma_bf16_ts(tmem + T_KK, mh, xl, id, true);
+        tc::mma_bf16_ts(tmem + T_KK, ml, xh, id, true);
       }
       tc::commit(bar_mma);
     }
     pending_mma = 1;
-    // X rows (rows 0-63 of [X;Y], read by G34) while Y runs: Y reads the m and
-    // X^T tiles only.
+    // X rows (rows 0-63 of [X;Y], read by G34) while Y runs: Y reads the X^T tiles
+    // and tensor memory only.
     {
       const int j = xj, part = xpart;
       float xc[16];
@@ -545,9 +551,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_chunk8_hilo(sm + OFF_XYH, sm + OFF_XYL, j, 2 * part + 1, xc + 8);
     }
     // ---- (6) S hi/lo (A of G12) -> TMEM cols T_SH / T_SL, also while Y runs (Y
-    //          writes the T_Y columns; S was last written by the previous chunk's
-    //          GS, and its G12 has finished reading T_SH / T_SL). Columns
-    //          [64 hf, +64) of S -> bf16 pair columns [32 hf, +32).
+    //          reads the T_Y and writes the T_KK columns; S was last written by
+    //          the previous chunk's GS, which has finished reading T_SH / T_SL).
+    //          Columns [64 hf, +64) of S -> bf16 pair columns [32 hf, +32).
 #pragma unroll 1
     for (int q = 0; q < 2; ++q) {
       float v[32];
@@ -557,10 +563,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc::tmem_wait_st();
     if (!wait_mma()) break;
-    if (quarter < 2) {
+    if (quarter >= 2) {
       float y[32];
-      tc::tmem_ld32(tmem + lane + T_Y + 32 * hf, y);
-      store_chunks_hilo(sm + OFF_XYH, sm + OFF_XYL, 64 + row, 4 * hf, y);
+      tc::tmem_ld32(tmem + lane + T_KK + 32 * hf, y);
+      store_chunks_hilo(sm + OFF_XYH, sm + OFF_XYL, row, 4 * hf, y);
     }
     fence_proxy_async_smem();
     tc::fence_before();
