@@ -55,24 +55,26 @@ constexpr int kKQBufs = 3;  // K/Q tiles of chunk c live from the prep's G0 to t
 constexpr uint32_t OFF_KQ = 0;          // kKQBufs x [2 dk halves][K rows 0-63 | Q rows 64-127][128 B]
 constexpr uint32_t KQ_BYTES = 32768;
 constexpr uint32_t OFF_V = kKQBufs * KQ_BYTES;  // [2 dv halves][64 rows][128 B]
-constexpr uint32_t OFF_XY = OFF_V + 16384;      // 2 x {[X rows 0-63 | Y rows 64-127][128 B] hi, lo}
-constexpr uint32_t XY_BYTES = 32768;            // chunk c uses [X;Y] buffer c & 1
-constexpr uint32_t OFF_XTH = OFF_XY + 2 * XY_BYTES;  // X^T rows hi [64 rows][128 B]
+constexpr uint32_t OFF_XYH = OFF_V + 16384;     // [X rows 0-63 | Y rows 64-127][128 B] hi
+constexpr uint32_t OFF_XYL = OFF_XYH + 16384;   // lo
+constexpr uint32_t OFF_XTH = OFF_XYL + 16384;   // X^T rows hi [64 rows][128 B]
 constexpr uint32_t OFF_XTL = OFF_XTH + 8192;         // lo
 constexpr uint32_t OFF_AMAT = OFF_XTL + 8192;   // A (strict lower) fp32 [64][kAStride], then X
 constexpr int kAStride = 68;            // fp32 row stride of A (conflict-free float4 rows)
 constexpr uint32_t OFF_TBUF = OFF_AMAT + 64 * kAStride * 4;  // inverse scratch [32][kTStride]
 constexpr int kTStride = 40;            // fp32 row stride of the inverse scratch
-constexpr uint32_t OFF_SMALL = OFF_TBUF + 32 * kTStride * 4;  // two gate sets
+constexpr uint32_t OFF_SMALL = OFF_TBUF + 32 * kTStride * 4;  // kGateSets gate sets
                                         // [lg, beta, decay, r, inv][64] floats; barriers; TMEM base
 constexpr int kMaxRankedSeqs = 4096;    // longer varlen batches keep their order
 // The varlen ranking stages cu_seqlens in the A scratch before the first chunk.
 static_assert((kMaxRankedSeqs + 2) * 4 <= 64 * kAStride * 4, "ranking scratch exceeds A");
-static_assert(OFF_V % 1024 == 0 && OFF_XY % 1024 == 0 && OFF_XTH % 1024 == 0 &&
+static_assert(OFF_V % 1024 == 0 && OFF_XYH % 1024 == 0 && OFF_XYL % 1024 == 0 &&
+                  OFF_XTH % 1024 == 0 &&
                   OFF_XTL % 1024 == 0,
               "swizzled tiles need 1024-byte alignment");
 constexpr int kGateSet = 5 * 64;  // floats of one chunk's gate arrays
-constexpr uint32_t SMEM_BYTES = OFF_SMALL + 2 * kGateSet * 4 + 128 + 1024;  // + alignment slack
+constexpr int kGateSets = 3;      // chunk c uses set c % 3 (made a chunk ahead by the prep)
+constexpr uint32_t SMEM_BYTES = OFF_SMALL + kGateSets * kGateSet * 4 + 128 + 1024;  // + slack
 static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
 // Each CTA allocates all 512 TMEM columns, so two must never share an SM: the
 // shared memory plan alone keeps a second one off (228 KB per SM).
@@ -162,14 +164,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  // Gate arrays of a chunk (set c & 1): log2 prefix sums lg, beta, decay = 2^lg,
-  // r = 2^(lg_63 - lg), inv = 2^(lg_0 - lg) (the column factor of the decay ratios).
+  // Gate arrays of a chunk (set c % kGateSets): log2 prefix sums lg, beta, decay =
+  // 2^lg, r = 2^(lg_63 - lg), inv = 2^(lg_0 - lg) (the column factor of the decay
+  // ratios).
   float* gate_sets = reinterpret_cast<float*>(sm + OFF_SMALL);
-  uint64_t* bar_kq = reinterpret_cast<uint64_t*>(gate_sets + 2 * kGateSet);  // [kKQBufs]
+  uint64_t* bar_kq = reinterpret_cast<uint64_t*>(gate_sets + kGateSets * kGateSet);  // [kKQBufs]
   uint64_t* bar_v = bar_kq + kKQBufs;   // V tile
   uint64_t* bar_mma = bar_v + 1;        // the state chain's MMAs
   uint64_t* bar_g0 = bar_mma + 1;       // the prep's G0
-  uint64_t* bar_mfree = bar_g0 + 1;     // a chunk's Y has read m and X^T
+  uint64_t* bar_mfree = bar_g0 + 1;     // a chunk's X split and Y have read X, m and X^T
   uint64_t* bar_full = bar_mfree + 1;   // [2]: a chunk's prep is in place
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_full + 2);
   float* Xf = reinterpret_cast<float*>(sm + OFF_AMAT);  // A, inverted in place into X
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_v, 1);
     mbar_init(bar_mma, 1);
     mbar_init(bar_g0, 1);
-    mbar_init(bar_mfree, 1);
+    mbar_init(bar_mfree, 2);  // the chain's arrival after the X split, and Y's commit
     mbar_init(&bar_full[0], 1);
     mbar_init(&bar_full[1], 1);
     fence_mbar_init();
@@ -347,50 +350,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     int kq_ok = 1;
-    if (warp == 8) fetch_gates(0);
+    // G0 of a chunk: [K;Q] K^T -> TMEM cols T_KK (lanes 0-63 KK^T, 64-127 QK^T), by
+    // the prep's first thread once the chunk's K/Q tiles have landed. The commit
+    // arrives even without the G0, so no thread waits in vain.
+    auto issue_g0 = [&](int chunk) {
+      const int bi = chunk % kKQBufs;
+      kq_ok = mbar_wait_bounded(&bar_kq[bi], (chunk / kKQBufs) & 1, status) ? 1 : 0;
+      if (kq_ok) {
+        tc::fence_after();
+        const uint32_t kq = OFF_KQ + bi * KQ_BYTES;
+        constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t a = smem_addr(sm + kq + kb * 16384) + ks * 32;
+            tc::mma_bf16(tmem + T_KK, tc::desc_kmajor(a), tc::desc_kmajor(a), id,
+                         (kb | ks) != 0);
+          }
+      }
+      tc::commit(bar_g0);
+    };
+    if (warp == 8) {
+      fetch_gates(0);
+      make_gates(gate_sets);
+      if (1 < nchunks) fetch_gates(1);
+    }
+    if (ptid == 0) issue_g0(0);
+    g0_pending = 1;
 #pragma unroll 1
     for (int n = 0; n < nchunks; ++n) {
-      // m (cols T_M), X^T, gate set n & 1 and [X;Y] buffer n & 1 are free once the
-      // state chain's Y of chunk n - 1 has completed (its chunk n - 2 is over by then).
+      // m (cols T_M) and the fp32 A / X scratch are free once the state chain's X
+      // split and Y of chunk n - 1 have read them.
       if (n >= 1) {
         const int done = mbar_wait_bounded(bar_mfree, (n - 1) & 1, status) ? 1 : 0;
         ok = group_sync_and(kPrepBar, kPrepThreads, done && ok);
         if (!ok) break;
         tc::fence_after();
       }
-      float* gs = gate_sets + (n & 1) * kGateSet;
-      if (warp == 8) {
-        make_gates(gs);
-        if (n + 1 < nchunks) fetch_gates(n + 1);
-      }
-      // G0: [K;Q] K^T -> TMEM cols T_KK (lanes 0-63 KK^T, 64-127 QK^T); the last
-      // reads of T_KK (A / m of chunk n - 1) are behind the barrier above.
-      if (ptid == 0) {
-        const int bi = n % kKQBufs;
-        kq_ok = mbar_wait_bounded(&bar_kq[bi], (n / kKQBufs) & 1, status) ? 1 : 0;
-        if (kq_ok) {
-          tc::fence_after();
-          const uint32_t kq = OFF_KQ + bi * KQ_BYTES;
-          constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
-#pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint32_t a = smem_addr(sm + kq + kb * 16384) + ks * 32;
-              tc::mma_bf16(tmem + T_KK, tc::desc_kmajor(a), tc::desc_kmajor(a), id,
-                           (kb | ks) != 0);
-            }
-        }
-        tc::commit(bar_g0);  // arrives even without the G0, so no thread waits in vain
-      }
-      g0_pending = 1;
+      const float* gs = gate_sets + (n % kGateSets) * kGateSet;
+      // This chunk's G0 went out after the previous chunk's A / m (or before the
+      // loop), and its gate set at the end of the previous iteration.
       {
         const int done = mbar_wait_bounded(bar_g0, g0_phase, status) ? 1 : 0;
         if (done) {
           g0_phase ^= 1;
           g0_pending = 0;
         }
-        // Also publishes the gate set to the other prep warps.
         ok = group_sync_and(kPrepBar, kPrepThreads, done && ok && kq_ok);
         if (!ok) break;
         tc::fence_after();
@@ -400,6 +406,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tmem_wait_st();
       tc::fence_before();
       group_sync(kPrepBar, kPrepThreads);
+      // The next chunk's G0, now that every prep warp has read T_KK.
+      if (n + 1 < nchunks) {
+        if (ptid == 0) {
+          tc::fence_after();
+          issue_g0(n + 1);
+        }
+        g0_pending = 1;
+      }
 
       // X = (I + A)^-1 in place: 8 x 8 diagonal blocks by substitution, then the
       // off-diagonal blocks level by level (8, 16, 32 wide).
@@ -518,33 +532,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       group_sync(kPrepBar, kPrepThreads);
-      // X -> bf16 hi/lo: X^T rows (B of Y) and X rows (rows 0-63 of [X;Y] buffer
-      // n & 1, B of G34). Thread: column / row xj, half xp of the other index.
-      {
-        const int xj = ptid & 63, xp = ptid >> 6;
-        float xc[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) xc[e] = Xf[(32 * xp + e) * kAStride + xj];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, xj, 4 * xp + q, xc + 8 * q);
-        const float4* xr = reinterpret_cast<const float4*>(Xf + xj * kAStride + 32 * xp);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float4 x4 = xr[e];
-          xc[4 * e] = x4.x;
-          xc[4 * e + 1] = x4.y;
-          xc[4 * e + 2] = x4.z;
-          xc[4 * e + 3] = x4.w;
-        }
-        uint8_t* xyh = sm + OFF_XY + (n & 1) * XY_BYTES;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          store_chunk8_hilo(xyh, xyh + 16384, xj, 4 * xp + q, xc + 8 * q);
-      }
-      fence_proxy_async_smem();
-      group_sync(kPrepBar, kPrepThreads);
       if (ptid == 0) mbar_arrive(&bar_full[n & 1]);
+      // The next chunk's gate set goes where chunk n - 2's was; the state chain
+      // finished that chunk before its Y of chunk n - 1.
+      if (warp == 8 && n + 1 < nchunks) {
+        make_gates(gate_sets + ((n + 1) % kGateSets) * kGateSet);
+        if (n + 2 < nchunks) fetch_gates(n + 2);
+      }
     }
     // A bounded wait gave up: let this group's G0 in flight finish.
     if (g0_pending) mbar_wait_bounded(bar_g0, g0_phase, status);
@@ -602,15 +596,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int valid = min(kC, len - c * kC);
       const int bi = c % kKQBufs;
       const uint32_t off_kq = OFF_KQ + bi * KQ_BYTES;
-      uint8_t* xyh = sm + OFF_XY + (c & 1) * XY_BYTES;
-      uint8_t* xyl = xyh + 16384;
-      const float* s_lg = gate_sets + (c & 1) * kGateSet;
+      uint8_t* xyh = sm + OFF_XYH;
+      uint8_t* xyl = sm + OFF_XYL;
+      const float* s_lg = gate_sets + (c % kGateSets) * kGateSet;
       const float* s_beta = s_lg + 64;
       const float* s_decay = s_lg + 128;
       const float* s_r = s_lg + 192;
 
-      // ---- (1) this chunk's prep: gate set, m in cols T_M, X^T, the X rows of
-      //          [X;Y]; and (thread 0) its K/Q tiles, which the prep's G0 waited for.
+      // ---- (1) this chunk's prep: gate set, m in cols T_M, X in the fp32 scratch;
+      //          and (thread 0) its K/Q tiles, which the prep's G0 waited for.
       {
         int done = mbar_wait_bounded(&bar_full[c & 1], (c >> 1) & 1, status) ? 1 : 0;
         if (tid == 0 && done) done = mbar_wait_bounded(&bar_kq[bi], (c / kKQBufs) & 1, status);
@@ -619,11 +613,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after();
         pending_loads &= ~(1 << bi);
       }
+      // ---- (4b) X -> bf16 hi/lo: X^T rows (B of Y) and X rows (rows 0-63 of
+      //           [X;Y], B of G34; the previous chunk's G34 is done). Then the prep
+      //           may overwrite the fp32 X (its other condition is Y's commit).
+      {
+        const int xj = tid & 63, xpart = tid >> 6;
+        float xc[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xc[e] = Xf[(16 * xpart + e) * kAStride + xj];
+        store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, xj, 2 * xpart, xc);
+        store_chunk8_hilo(sm + OFF_XTH, sm + OFF_XTL, xj, 2 * xpart + 1, xc + 8);
+        const float4* xr = reinterpret_cast<const float4*>(Xf + xj * kAStride + 16 * xpart);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 x4 = xr[e];
+          xc[4 * e] = x4.x;
+          xc[4 * e + 1] = x4.y;
+          xc[4 * e + 2] = x4.z;
+          xc[4 * e + 3] = x4.w;
+        }
+        store_chunk8_hilo(xyh, xyl, xj, 2 * xpart, xc);
+        store_chunk8_hilo(xyh, xyl, xj, 2 * xpart + 1, xc + 8);
+      }
+      fence_proxy_async_smem();
+      group_sync(kMainBar, kMainThreads);
+      if (tid == 0) mbar_arrive(bar_mfree);
 
       // ---- (5) Y = m X, m from TMEM cols T_M (lanes 64-127: hi, then lo) -> TMEM
       //          cols T_P (lanes 64-127; G12 writes them next). Lanes 0-63 of the
-      //          product are not used. A second commit tells the prep that m and
-      //          X^T have been read.
+      //          product are not used. A second commit tells the prep that m has
+      //          been read.
       if (tid == 0) {
         tc::fence_after();
         constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
