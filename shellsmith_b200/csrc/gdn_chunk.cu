@@ -401,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc::fence_after();
       }
-      build_am(gs, 0);
-      build_am(gs, 1);
+#pragma unroll 1
+      for (int hx = 0; hx < 2; ++hx) build_am(gs, hx);
       tc::tmem_wait_st();
       tc::fence_before();
       group_sync(kPrepBar, kPrepThreads);
@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gq = lane_id >> 2, t4 = lane_id & 3;
         const int n0 = 8 * pw;
         float acc[2][4];
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < 2; ++i) {
           const int r0 = 32 + 16 * i;
           float* T = Tbuf + (r0 - 32) * kTStride + n0;
@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float2(acc[i][2], acc[i][3]);
         }
         group_sync(kPrepBar, kPrepThreads);  // T complete; every warp is done reading A[32:64][0:32]
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < 2; ++i) {
           const int r0 = 32 + 16 * i;
           acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
