@@ -346,8 +346,12 @@ int gdn_bulk_launch(const char* name, const uint16_t* q, const uint16_t* k, cons
       return set_error(SC_ERR_CUDA, "%s: setup: %s", name, cudaGetErrorString(err));
     configured[dev] = 1;
   }
-  // Fewer CTAs than two per SM: one 16 KiB chunk per CTA instead (more loads in flight).
-  const bool small = (long long)B * Hv * (dv / (kBulkRows * kBulkChunksPerCta)) < 2LL * sms[dev];
+  // Up to ~48 two-chunk CTAs per SM (at 32 value heads, fewer than ~110 rows): one
+  // 16 KiB chunk per CTA instead, twice the CTAs and more loads in flight. Measured on
+  // config-3 steps: 64 rows 3.72 -> 3.62 ms, 32 rows 2.30 -> 2.20 ms, 128 rows even,
+  // 256 rows 12.49 -> 12.68 ms.
+  const bool small =
+      (long long)B * Hv * (dv / (kBulkRows * kBulkChunksPerCta)) < 48LL * sms[dev];
   const int nch = small ? 1 : kBulkChunksPerCta;
   const int smem = nch * (kBulkChunkBytes + 8) + 8;
   cudaLaunchConfig_t cfg = {};
