@@ -564,7 +564,8 @@ def run_ours(args, world, rank, local):
                 if cfg.is_attention(layer):
                     eng.attention_layer(layer, *wl.inputs[layer], wl.outputs[layer])
                 else:
-                    eng.gdn_layer(layer, *wl.inputs[layer], wl.outputs[layer])
+                    eng.gdn_layer(layer, *wl.inputs[layer], wl.outputs[layer],
+                                  chained=layer > 0)
                 e1.record(stream)
                 layer_events.append((cfg.is_attention(layer), e0, e1, lengths))
         s1.record(stream)
@@ -1279,7 +1280,7 @@ def run_e2e(args, wl, world):
             if cfg.is_attention(l):
                 eng.attention_layer(l, *wl.inputs[l], wl.outputs[l])
             else:
-                eng.gdn_layer(l, *wl.inputs[l], wl.outputs[l])
+                eng.gdn_layer(l, *wl.inputs[l], wl.outputs[l], chained=l > 0)
             done = torch.cuda.Event()
             done.record(comp)
             with torch.cuda.stream(d2h):

@@ -315,9 +315,13 @@ class HybridCacheEngine:
         return len(active)
 
     # ------------------------------------------------------------ decode
-    def gdn_layer(self, layer: int, q, k, v, decay, beta, out) -> None:
+    def gdn_layer(self, layer: int, q, k, v, decay, beta, out, chained: bool = False) -> None:
+        """The GDN state update of `layer` for every staged row. chained=True promises
+        that the kernel queued just before it on the stream is another layer's update or
+        an attention layer (it writes neither this layer's state rows nor the slot
+        array), so the state may stream in while that kernel finishes."""
         numerics.gdn_decode(q, k, v, decay, beta, self.state[self.gdn_index[layer]],
-                            self.state_slot, out=out)
+                            self.state_slot, out=out, chained=chained)
 
     def gdn_layer_front(self, layer: int, qkv, z, a, b, weights, out) -> None:
         """A GDN layer from its projections: conv taps, q/k norm, gates, state update
@@ -384,7 +388,8 @@ class HybridCacheEngine:
             if self.cfg.is_attention(layer):
                 self.attention_layer(layer, *inputs[layer], outputs[layer])
             else:
-                self.gdn_layer(layer, *inputs[layer], outputs[layer])
+                # Past the first layer the kernel before is this step's previous layer.
+                self.gdn_layer(layer, *inputs[layer], outputs[layer], chained=layer > 0)
 
     # ------------------------------------------------------------ accounting
     def step_bytes(self, lengths: np.ndarray) -> dict:
