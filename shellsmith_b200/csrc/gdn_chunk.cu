@@ -12,9 +12,12 @@
 //   W = beta (V - decay (K S^T)),  U = X W,  O = decay (Q S^T) + (m X) W,
 //   S <- decay_63 S + (r U)^T K.
 //
-// B200 mapping. One CTA (8 warps) owns one (sequence, value head) and walks its
-// chunks in order; the 128 x 128 fp32 state lives in tensor memory the whole
-// time. Everything is computed transposed, so TMEM lane = value row i = thread:
+// B200 mapping. One CTA owns one (sequence, value head) and walks its chunks in
+// order; the 128 x 128 fp32 state lives in tensor memory the whole time. Twelve
+// warps in two groups: warps 0-7 run chunk c's state chain (X split, Y, G12, W,
+// G34, U r, GS, the O rows) while warps 8-11 prepare chunk c + 1 (gates, G0,
+// A / m, the inverse); mbarriers carry the hand-offs both ways. Everything is
+// computed transposed, so TMEM lane = value row i:
 //   G0  [K;Q] K^T            -> A (fp32 smem), m        M128 N64  K128
 //   Y   m X                  -> rows 64.. of [X;Y]      M128 N64  K64   A in TMEM
 //   G12 S [K;Q]^T            -> P1^T | P2^T             M128 N128 K128  A in TMEM
