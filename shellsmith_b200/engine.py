@@ -115,21 +115,32 @@ class HybridCacheEngine:
                                    cfg.head_dim), dtype=torch.bfloat16, device=dev)
         self.blocks = BlockManager(cfg.num_pages, cfg.page_size, cfg.max_seqs,
                                    cfg.max_pages_per_seq, seed=seed)
-        # Pinned host mirrors, copied to the device once per step.
-        self._h_table = torch.zeros((cfg.max_seqs, cfg.max_pages_per_seq), dtype=torch.int32,
-                                    pin_memory=True)
+        # The step's tables: pinned host mirrors in one buffer, copied to the device's
+        # buffer of the same layout in one transfer per step. int32 words: the block
+        # table, then the slot mapping (int64), context lengths, state slots,
+        # positions and the longest-first order, each segment 16-byte aligned.
+        S, P = cfg.max_seqs, cfg.max_pages_per_seq
+        seg = -(-S // 4) * 4
+        n_table = -(-S * P // 4) * 4
+        words = n_table + 6 * seg
+        self._h_stage = torch.zeros(words, dtype=torch.int32, pin_memory=True)
+        self._d_stage = torch.zeros(words, dtype=torch.int32, device=dev)
+
+        def views(buf):
+            o = n_table + 2 * seg
+            return (buf[:S * P].view(S, P), buf[n_table:n_table + 2 * S].view(torch.int64),
+                    buf[o:o + S], buf[o + seg:o + seg + S], buf[o + 2 * seg:o + 2 * seg + S],
+                    buf[o + 3 * seg:o + 3 * seg + S])
+
+        (self._h_table, self._h_slot_map, self._h_ctx, self._h_state_slot, self._h_position,
+         self._h_order) = views(self._h_stage)
+        (self.table, self.slot_map, self.ctx_len, self.state_slot, self.position,
+         self.seq_order) = views(self._d_stage)
         self.blocks.table = self._h_table.numpy()
-        self._h_ctx = torch.zeros(cfg.max_seqs, dtype=torch.int32, pin_memory=True)
-        self._h_slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, pin_memory=True)
-        self._h_state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, pin_memory=True)
-        self._h_position = torch.zeros(cfg.max_seqs, dtype=torch.int32, pin_memory=True)
-        self._h_order = torch.arange(cfg.max_seqs, dtype=torch.int32).pin_memory()
-        self.table = torch.zeros_like(self._h_table, device=dev)
-        self.ctx_len = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
-        self.slot_map = torch.full((cfg.max_seqs,), -1, dtype=torch.int64, device=dev)
-        self.state_slot = torch.full((cfg.max_seqs,), -1, dtype=torch.int32, device=dev)
-        self.position = torch.zeros(cfg.max_seqs, dtype=torch.int32, device=dev)
-        self.seq_order = torch.arange(cfg.max_seqs, dtype=torch.int32, device=dev)
+        self._h_slot_map.fill_(-1)
+        self._h_state_slot.fill_(-1)
+        self._h_order.copy_(torch.arange(S, dtype=torch.int32))
+        self._d_stage.copy_(self._h_stage)
         self._staged = torch.cuda.Event()
         self._staged.record()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
@@ -305,12 +316,7 @@ class HybridCacheEngine:
         self._h_position.numpy()[:] = np.maximum(blocks.lengths - 1, 0).astype(np.int32)
         self.max_pages_in_batch = max(1, int(blocks.pages_for(ctx.max())))
         self.total_pages = int(np.ceil(blocks.lengths[active] / self.cfg.page_size).sum())
-        self.table.copy_(self._h_table, non_blocking=True)
-        self.ctx_len.copy_(self._h_ctx, non_blocking=True)
-        self.slot_map.copy_(self._h_slot_map, non_blocking=True)
-        self.state_slot.copy_(self._h_state_slot, non_blocking=True)
-        self.position.copy_(self._h_position, non_blocking=True)
-        self.seq_order.copy_(self._h_order, non_blocking=True)
+        self._d_stage.copy_(self._h_stage, non_blocking=True)  # every table at once
         self._staged.record()
         return len(active)
 
