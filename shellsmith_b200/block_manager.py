@@ -118,12 +118,16 @@ class BlockManager:
         # Only a sequence at a page boundary changes its page list (about one row in
         # P per step); every other row's slot is read from the table, which mirrors
         # the page lists row for row.
-        for i in np.flatnonzero(needs_page).tolist():
-            slot, length = int(slots[i]), int(lengths[i])
-            page = self.take_pages(1)[0]
-            self.pages[slot].append(page)
-            self.table[slot, length // self.page_size] = page
-            self.dirty_rows.add(slot)
+        grow = np.flatnonzero(needs_page)
+        if grow.size:
+            # One pop for every row that needs a page, in row order (the same LIFO
+            # pages a row-by-row take would give).
+            new_pages = self.take_pages(int(grow.size))
+            rows = slots[grow]
+            self.table[rows, lengths[grow] // self.page_size] = new_pages
+            for slot, page in zip(rows.tolist(), new_pages):
+                self.pages[slot].append(page)
+            self.dirty_rows.update(rows.tolist())
         out = (self.table[slots, lengths // self.page_size].astype(np.int64) * self.page_size
                + lengths % self.page_size)
         self.lengths[slots] = lengths + 1

@@ -137,6 +137,10 @@ class HybridCacheEngine:
         (self.table, self.slot_map, self.ctx_len, self.state_slot, self.position,
          self.seq_order) = views(self._d_stage)
         self.blocks.table = self._h_table.numpy()
+        # numpy views of the host mirrors, written in place every step
+        self._n_slot_map, self._n_ctx, self._n_state_slot, self._n_position, self._n_order = (
+            t.numpy() for t in (self._h_slot_map, self._h_ctx, self._h_state_slot,
+                                self._h_position, self._h_order))
         self._h_slot_map.fill_(-1)
         self._h_state_slot.fill_(-1)
         self._h_order.copy_(torch.arange(S, dtype=torch.int32))
@@ -303,17 +307,16 @@ class HybridCacheEngine:
                   else np.asarray(sorted(int(r) for r in rows), np.int64))
         if rows is not None and not blocks.active[active].all():
             raise ValueError("begin_step: a listed slot holds no sequence")
-        slot_map = np.full(self.cfg.max_seqs, -1, np.int64)
-        slot_map[active] = blocks.append_token(active)
-        self._h_slot_map.numpy()[:] = slot_map
-        ctx = np.zeros(self.cfg.max_seqs, np.int32)
+        new_slots = blocks.append_token(active)  # raises before anything changes
+        slot_map, ctx, state_slot = self._n_slot_map, self._n_ctx, self._n_state_slot
+        slot_map.fill(-1)
+        slot_map[active] = new_slots
+        ctx.fill(0)
         ctx[active] = blocks.lengths[active]
-        self._h_ctx.numpy()[:] = ctx
-        self._h_order.numpy()[:] = np.argsort(-ctx, kind="stable")  # attention: longest first
-        state_slot = np.full(self.cfg.max_seqs, -1, np.int32)
+        self._n_order[:] = np.argsort(-ctx, kind="stable")  # attention: longest first
+        state_slot.fill(-1)
         state_slot[active] = active
-        self._h_state_slot.numpy()[:] = state_slot
-        self._h_position.numpy()[:] = np.maximum(blocks.lengths - 1, 0).astype(np.int32)
+        np.maximum(blocks.lengths - 1, 0, out=self._n_position, casting="unsafe")
         self.max_pages_in_batch = max(1, int(blocks.pages_for(ctx.max())))
         self.total_pages = int(np.ceil(blocks.lengths[active] / self.cfg.page_size).sum())
         self._d_stage.copy_(self._h_stage, non_blocking=True)  # every table at once
