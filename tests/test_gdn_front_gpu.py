@@ -83,8 +83,12 @@ def _check_stages(front_got, front_want, y_got, state_before, state_after, z, ou
 
 
 # B = 64 with 8 value heads: 1024 update CTAs, more than are resident at once.
-@pytest.mark.parametrize("Hk,Hv,B", [(2, 4, 3), (16, 32, 5), (2, 8, 64)])
-def test_split_decode_stages_match_oracle_over_steps(cuda, Hk, Hv, B):
+# (1, 3, 4): an odd number of heads (5). qkv_off passes qkv 4 bytes past an 8-byte
+# boundary, which the 8-byte vector front cannot take: the per-channel kernel runs.
+@pytest.mark.parametrize("Hk,Hv,B,qkv_off", [(2, 4, 3, False), (16, 32, 5, False),
+                                             (2, 8, 64, False), (1, 3, 4, False),
+                                             (2, 4, 3, True)])
+def test_split_decode_stages_match_oracle_over_steps(cuda, Hk, Hv, B, qkv_off):
     """Five decode steps of the three-kernel form, every stage at its bar."""
     rng = np.random.default_rng(Hk * 10 + Hv)
     w, (conv_w, a_log, dt_bias, norm_w) = _weights(rng, Hk, Hv, cuda)
@@ -100,7 +104,12 @@ def test_split_decode_stages_match_oracle_over_steps(cuda, Hk, Hv, B):
         qkv, z, a, b = _inputs(rng, (B,), Hk, Hv)
         pos = torch.full((B,), step, dtype=torch.int32, device=cuda)
         before = state[idx].double().cpu().numpy()
-        out = gdn_layer.gdn_decode_split(_dev(qkv, cuda), _dev(z, cuda), _dev(a, cuda),
+        qkv_d = _dev(qkv, cuda)
+        if qkv_off:  # the same values, 4 bytes past an 8-byte boundary
+            wide = torch.empty(qkv_d.numel() + 2, dtype=qkv_d.dtype, device=cuda)
+            qkv_d = wide[2:].view(qkv_d.shape).copy_(qkv_d)
+            assert qkv_d.data_ptr() % 8 == 4
+        out = gdn_layer.gdn_decode_split(qkv_d, _dev(z, cuda), _dev(a, cuda),
                                          _dev(b, cuda), w, taps, pos, state, slot_t,
                                          workspace=ws)
         torch.cuda.synchronize()
