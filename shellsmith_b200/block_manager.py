@@ -13,8 +13,9 @@ placement (which page, which slot) is this build's own, deterministic:
   * a page has a reference count: prefix snapshots and forked sequences share
     full pages, and a page returns to the free list when its last owner
     drops it;
-  * state slots come from a LIFO list of [0, max_seqs); a sequence's slot is
-    also its batch row, its block-table row and its GDN state row;
+  * a new sequence takes the lowest free state slot of [0, max_seqs), so the
+    active slots stay packed at the bottom; a sequence's slot is also its batch
+    row, its block-table row and its GDN state row;
   * a sequence of n tokens holds ceil(n / P) pages; the token at position t
     lives at slot page[t // P] * P + t % P.
 
@@ -23,6 +24,8 @@ context lengths and the slot mapping are refreshed by the engine.
 """
 
 from __future__ import annotations
+
+import heapq
 
 import numpy as np
 
@@ -44,7 +47,10 @@ class BlockManager:
                  else np.arange(num_pages))
         # pop() takes from the end: reverse so the first page handed out is order[0].
         self._free_pages = [int(p) for p in order[::-1]]
-        self._free_slots = list(range(max_seqs - 1, -1, -1))
+        # Free slots as a min-heap: a new sequence takes the lowest free slot, so the
+        # active rows stay packed at the bottom and a step can launch over rows
+        # [0, highest active slot] only (highest_active()).
+        self._free_slots = list(range(max_seqs))
         self.table = np.zeros((max_seqs, max_pages_per_seq), np.int32)
         self.refcount = np.zeros(num_pages, np.int32)
         self.lengths = np.zeros(max_seqs, np.int64)
@@ -61,6 +67,12 @@ class BlockManager:
     @property
     def free_slots(self) -> int:
         return len(self._free_slots)
+
+    def highest_active(self) -> int:
+        """1 + the highest active slot (0 when none): a step's kernels need cover only
+        rows [0, highest_active())."""
+        act = np.flatnonzero(self.active)
+        return int(act[-1]) + 1 if act.size else 0
 
     def pages_for(self, tokens: int) -> int:
         return -(-int(tokens) // self.page_size)
@@ -84,7 +96,7 @@ class BlockManager:
             raise OutOfPages(f"{tokens} tokens exceed {self.max_pages_per_seq} pages per sequence")
         if need > len(self._free_pages):
             raise OutOfPages(f"{need} pages needed, {len(self._free_pages)} free")
-        slot = self._free_slots.pop()
+        slot = heapq.heappop(self._free_slots)
         pages = self.take_pages(need)
         self.pages[slot] = pages
         self.owner[slot] = owner
@@ -162,7 +174,7 @@ class BlockManager:
             raise OutOfPages("no free sequence slot")
         if len(pages) > self.max_pages_per_seq or self.pages_for(tokens) != len(pages):
             raise ValueError("adopt: page count does not match the token count")
-        slot = self._free_slots.pop()
+        slot = heapq.heappop(self._free_slots)
         self.pages[slot] = list(pages)
         self.owner[slot] = owner
         self.table[slot, :len(pages)] = pages
@@ -195,7 +207,7 @@ class BlockManager:
         self.owner.pop(slot, None)
         self.lengths[slot] = 0
         self.active[slot] = False
-        self._free_slots.append(slot)
+        heapq.heappush(self._free_slots, slot)
         self.dirty_rows.add(slot)
 
     def take_dirty_rows(self) -> list:

@@ -154,6 +154,7 @@ class HybridCacheEngine:
                                                   device=dev)
         self.max_pages_in_batch = 1
         self.total_pages = 0
+        self.rows = cfg.max_seqs  # rows the step's kernels cover (set by begin_step)
 
     # ------------------------------------------------------------ lifecycle
     def admit(self, owner, prompt_len: int) -> int:
@@ -317,6 +318,11 @@ class HybridCacheEngine:
         state_slot.fill(-1)
         state_slot[active] = active
         np.maximum(blocks.lengths - 1, 0, out=self._n_position, casting="unsafe")
+        # Rows past the highest active slot hold no sequence: the step's kernels
+        # cover rows [0, self.rows) only (the block manager packs slots low). The
+        # longest-first order then starts with exactly those rows: inactive rows
+        # tie at length 0 and keep their index order.
+        self.rows = blocks.highest_active()
         self.max_pages_in_batch = max(1, int(blocks.pages_for(ctx.max())))
         self.total_pages = int(np.ceil(blocks.lengths[active] / self.cfg.page_size).sum())
         self._d_stage.copy_(self._h_stage, non_blocking=True)  # every table at once
@@ -329,8 +335,12 @@ class HybridCacheEngine:
         that the kernel queued just before it on the stream is another layer's update or
         an attention layer (it writes neither this layer's state rows nor the slot
         array), so the state may stream in while that kernel finishes."""
-        numerics.gdn_decode(q, k, v, decay, beta, self.state[self.gdn_index[layer]],
-                            self.state_slot, out=out, chained=chained)
+        n = self.rows
+        if n == 0:
+            return
+        numerics.gdn_decode(q[:n], k[:n], v[:n], decay[:n], beta[:n],
+                            self.state[self.gdn_index[layer]], self.state_slot[:n], out=out[:n],
+                            chained=chained)
 
     def gdn_layer_front(self, layer: int, qkv, z, a, b, weights, out) -> None:
         """A GDN layer from its projections: conv taps, q/k norm, gates, state update
@@ -380,12 +390,16 @@ class HybridCacheEngine:
         """Append each row's new token and attend over its pages (paged.append_and_attend:
         one launch when the batch fits one split per sequence, else append, split-K and
         merge)."""
-        paged.append_and_attend(q, k_new, v_new, self.slot_map, self.kv[self.attn_index[layer]],
-                                self.table, self.ctx_len, self.scale,
+        n = self.rows
+        if n == 0:
+            return
+        paged.append_and_attend(q[:n], k_new[:n], v_new[:n], self.slot_map[:n],
+                                self.kv[self.attn_index[layer]], self.table[:n],
+                                self.ctx_len[:n], self.scale,
                                 max_pages_in_batch=self.max_pages_in_batch,
                                 pages_per_split=self.cfg.pages_per_split,
-                                total_pages=self.total_pages, workspace=self.workspace, out=out,
-                                seq_order=self.seq_order, sms=self.cfg.sms)
+                                total_pages=self.total_pages, workspace=self.workspace,
+                                out=out[:n], seq_order=self.seq_order[:n], sms=self.cfg.sms)
 
     def decode_step(self, inputs: dict, outputs: dict) -> None:
         """Run every layer's cache work for the staged token of each active row.
