@@ -105,3 +105,27 @@ def test_adopt_extend_and_take_check_sizes_first():
         bm.take_pages(4)
     assert bm.free_pages == 3
     np.testing.assert_array_equal(bm.refcount, [1, 0, 0, 0])
+
+
+def test_slots_lowest_first_and_highest_active():
+    """A new sequence takes the lowest free slot, so the engine's decode step can launch
+    over rows [0, highest_active()) only; page growth takes pages in row order."""
+    bm = BlockManager(num_pages=64, page_size=4, max_seqs=8, max_pages_per_seq=8, seed=2)
+    assert bm.highest_active() == 0
+    slots = [bm.admit(i, 4) for i in range(5)]
+    assert slots == [0, 1, 2, 3, 4] and bm.highest_active() == 5
+    bm.release(1)
+    bm.release(3)
+    assert bm.highest_active() == 5
+    assert bm.admit("new", 4) == 1             # the lowest hole, not the last released
+    bm.release(4)
+    assert bm.highest_active() == 3            # slots 0, 1, 2 remain
+    # Every listed row sits at a page boundary (4 tokens): each takes one page, in row
+    # order, from the free list's end.
+    rows = np.array([0, 1, 2, 3], np.int64)
+    rows = rows[bm.active[rows]]
+    expect = [bm._free_pages[-1 - i] for i in range(len(rows))]
+    out = bm.append_token(rows)
+    assert [bm.pages[int(r)][-1] for r in rows] == expect
+    np.testing.assert_array_equal(out, np.array(expect, np.int64) * 4)
+    np.testing.assert_array_equal(bm.lengths[rows], 5)
