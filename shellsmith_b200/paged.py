@@ -166,7 +166,11 @@ def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
     more work per byte, measured best at two waves of at most 256 pages.
 
     min_pages: a split then grows to at least this many pages while the CTAs still
-    number half a wave. Small batches of long sequences meet the wave target only with
+    number half a wave. Last, with `rows` given, a split doubles while its CTAs still
+    fill one wave and an average sequence still spans three splits: config 2's share of
+    32 sequences (U[1k, 32k]) took 0.214-0.215 ms per step with 128-page splits against
+    0.202-0.204 ms with 256 (at 16 sequences the two tie, 0.120-0.123 ms), while config
+    3's shorter sequences (64 of U[512, 16k]: under two 256-page splits each) keep 128. Small batches of long sequences meet the wave target only with
     short splits, and there each CTA's start, partial write and merge cost more than
     the extra waves gain: for bf16 pages at D = 256, 8 or 16 sequences of U[1k, 32k]
     tokens took 0.071 / 0.119 ms with 128-page splits against 0.088 / 0.126 ms with the
@@ -185,6 +189,12 @@ def split_plan(max_pages_in_batch: int, pages_per_split: int | None = None,
             pps *= 2
         while min_pages and pps < min_pages and pps * 2 <= cap and \
                 total_work / (pps * 2) >= sms / 2:
+            pps *= 2
+        # Long sequences: while the CTAs still fill a wave and a sequence still spans
+        # three splits on average, fewer and longer splits cut the per-CTA start, the
+        # partials and the merge more than the extra waves gain.
+        while rows and pps * 2 <= cap and ctas(pps * 2) >= sms and \
+                total_work / rows / (pps * 2) >= 3:
             pps *= 2
     else:
         pps = 64
